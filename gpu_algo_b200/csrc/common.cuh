@@ -1,0 +1,211 @@
+// Shared device helpers for the bfknn kernels (sm_100a).
+#pragma once
+#include <cstdint>
+#include <cuda_runtime.h>
+#include <cuda_fp16.h>
+
+#define BFK_PAD_DIST 3.402823e+38f
+
+namespace bfk {
+
+// ---------------------------------------------------------------------------
+// Workspace header: the first 256 bytes of every workspace.
+// ---------------------------------------------------------------------------
+struct WsHeader {
+  int32_t error;          // device status word: 0 ok, else an ErrCode below
+  uint32_t rx_bits;       // max row norm of X (float bits, positive => ordered as uint)
+  uint32_t qmax_bits;     // max |Q| (float bits)
+  int32_t nonfinite;      // set when a prepared row/query norm is not finite
+  int32_t fallback;       // queries routed to the exact SIMT engine
+  int32_t max_cand;       // max candidates of one query
+  unsigned long long candidates;  // total candidates appended by the filter
+  unsigned long long survivors;   // total rows re-ranked exactly
+  int32_t pad[54];
+};
+static_assert(sizeof(WsHeader) == 256, "header is 256 bytes");
+
+enum ErrCode : int32_t {
+  ERR_NONE = 0,
+  ERR_TIMEOUT_PRODUCER = 1,
+  ERR_TIMEOUT_MMA = 2,
+  ERR_TIMEOUT_EPILOGUE = 3,
+};
+
+// ---------------------------------------------------------------------------
+// Ordering helpers.
+// ---------------------------------------------------------------------------
+// float -> uint32 whose unsigned order equals the float order (no NaN input)
+__device__ __forceinline__ uint32_t f2ord(float f) {
+  uint32_t u = __float_as_uint(f);
+  return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+}
+__device__ __forceinline__ float ord2f(uint32_t u) {
+  return __uint_as_float((u & 0x80000000u) ? (u & 0x7fffffffu) : ~u);
+}
+// 64-bit key ordered by (distance, index); padding = all ones
+__device__ __forceinline__ uint64_t pair_key(float d, int32_t i) {
+  if (i < 0) return ~0ull;
+  return ((uint64_t)f2ord(d) << 32) | (uint32_t)i;
+}
+__device__ __forceinline__ bool pair_lt(float da, int32_t ia, float db, int32_t ib) {
+  return da < db || (da == db && ia < ib);
+}
+
+// The reference kernels' distance step (bf/fp32.py:80), spelled out so that
+// no other contraction can happen: dif = q - x (rounded), acc = fma(dif, dif, acc).
+__device__ __forceinline__ float dist_step(float q, float x, float acc) {
+  float dif = __fsub_rn(q, x);
+  return __fmaf_rn(dif, dif, acc);
+}
+
+// ---------------------------------------------------------------------------
+// Bounded waiting: every spin on the device gives up after a wall-clock limit,
+// records an error code in the workspace header and lets the kernel return.
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ uint64_t globaltimer_ns() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %globaltimer;" : "=l"(t));
+  return t;
+}
+
+constexpr uint64_t kWaitLimitNs = 2000000000ull;  // 2 s; a healthy wait is microseconds
+
+// ---------------------------------------------------------------------------
+// mbarrier
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ uint32_t smem_u32(const void *p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+__device__ __forceinline__ void mbar_init(uint64_t *bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count));
+}
+__device__ __forceinline__ void fence_mbar_init() {
+  asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+}
+__device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t *bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)),
+               "r"(bytes)
+               : "memory");
+}
+__device__ __forceinline__ void mbar_arrive(uint64_t *bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+__device__ __forceinline__ bool mbar_try_wait(uint64_t *bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+// Returns false when the limit ran out or `abort_flag` was raised by another role.
+__device__ __forceinline__ bool mbar_wait_bounded(uint64_t *bar, uint32_t parity,
+                                                  volatile int *abort_flag) {
+  if (mbar_try_wait(bar, parity)) return true;
+  uint64_t t0 = globaltimer_ns();
+  for (uint32_t it = 1;; ++it) {
+    if (mbar_try_wait(bar, parity)) return true;
+    if ((it & 63u) == 0) {
+      if (*abort_flag) return false;
+      if (globaltimer_ns() - t0 > kWaitLimitNs) return false;
+    }
+  }
+}
+
+// ---------------------------------------------------------------------------
+// TMA (2D tiled loads, no multicast) and bulk copies
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ void tma_load_2d(void *smem_dst, const void *tmap, uint64_t *bar,
+                                            int32_t x, int32_t y) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%3, %4}], [%2];" ::"r"(smem_u32(smem_dst)),
+      "l"(reinterpret_cast<uint64_t>(tmap)), "r"(smem_u32(bar)), "r"(x), "r"(y)
+      : "memory");
+}
+__device__ __forceinline__ void tma_prefetch_desc(const void *tmap) {
+  asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(tmap)) : "memory");
+}
+
+// ---------------------------------------------------------------------------
+// tcgen05 (5th-generation tensor cores, accumulators in tensor memory)
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ void tmem_alloc(uint32_t *dst_smem, uint32_t ncols) {
+  asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                   smem_u32(dst_smem)),
+               "r"(ncols)
+               : "memory");
+}
+__device__ __forceinline__ void tmem_relinquish() {
+  asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void tmem_dealloc(uint32_t taddr, uint32_t ncols) {
+  asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols)
+               : "memory");
+}
+__device__ __forceinline__ void tc_fence_before() {
+  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+}
+__device__ __forceinline__ void tc_fence_after() {
+  asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+}
+// D[tmem] (+)= A[smem] * B[smem]^T, kind::f16, cta_group::1
+__device__ __forceinline__ void tc_mma_f16(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc,
+                                           uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+// arrive on `bar` once every previously issued tcgen05.mma of this thread has completed
+__device__ __forceinline__ void tc_commit(uint64_t *bar) {
+  asm volatile(
+      "tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
+          smem_u32(bar))
+      : "memory");
+}
+// 32 lanes x 32 consecutive columns of 32-bit data: thread i gets lane (base+i), columns c..c+31
+__device__ __forceinline__ void tmem_ld_32x32b_x32(uint32_t taddr, uint32_t (&r)[32]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
+      "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
+      "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
+        "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]),
+        "=r"(r[14]), "=r"(r[15]), "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]),
+        "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]), "=r"(r[25]),
+        "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+      : "r"(taddr));
+}
+__device__ __forceinline__ void tmem_ld_wait() {
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+}
+
+// UMMA shared-memory descriptor, K-major operand, 128-byte swizzle: rows of
+// 128 bytes, 8-row groups 1024 bytes apart.  `addr` must sit in a
+// 1024-byte-aligned swizzle atom (plus a K offset of a multiple of 32 bytes).
+__device__ __forceinline__ uint64_t umma_desc_k_sw128(uint32_t addr) {
+  uint64_t desc = 0;
+  desc |= (uint64_t)((addr >> 4) & 0x3FFFu);          // start address  [0,14)
+  desc |= (uint64_t)1u << 16;                          // LBO (unused for SW128 K-major) [16,30)
+  desc |= (uint64_t)(1024u >> 4) << 32;                // SBO = 1024 B   [32,46)
+  desc |= (uint64_t)1u << 46;                          // descriptor version (sm_100) [46,48)
+  desc |= (uint64_t)2u << 61;                          // layout: SWIZZLE_128B [61,64)
+  return desc;
+}
+
+// Instruction descriptor for kind::f16: f16 x f16 -> f32, both K-major, M x N.
+__host__ __device__ constexpr uint32_t idesc_f16_f32(int M, int N) {
+  return (1u << 4)                        // D format: F32
+         | (0u << 7)                      // A format: F16
+         | (0u << 10)                     // B format: F16
+         | ((uint32_t)(N >> 3) << 17)     // N / 8
+         | ((uint32_t)(M >> 4) << 24);    // M / 16
+}
+
+}  // namespace bfk

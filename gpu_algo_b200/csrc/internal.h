@@ -1,0 +1,47 @@
+// Host-side launch wrappers shared between the translation units of libbfknn.
+#pragma once
+#include <cstddef>
+#include <cstdint>
+#include <cuda_runtime.h>
+
+namespace bfk {
+
+// direct.cu -- exact SIMT engine
+size_t direct_smem_bytes(int tq, int k);
+const void *direct_kernel_ptr(int tq);
+cudaError_t launch_direct(const float *Q, int64_t n, const float *X, int64_t m, int d, int k,
+                          int64_t id_offset, int slices, int tq, float *out_d, int32_t *out_i,
+                          cudaStream_t stream);
+
+// merge.cu -- sorted-list merge
+cudaError_t launch_merge(const float *cand_d, const int32_t *cand_i, int64_t n, int lists, int k,
+                         float *out_d, int32_t *out_i, cudaStream_t stream);
+int merge_max_k();
+cudaError_t launch_fill_pad(float *out_d, int32_t *out_i, int64_t count, cudaStream_t stream);
+
+// tc.cu -- tcgen05 filter engine
+struct TcPlan {
+  int64_t n, m;
+  int d, k;
+  int d_pad;        // d rounded up to 64 (f16 K chunks of 128 bytes)
+  int q_tiles;      // ceil(n / 128)
+  int64_t x_tiles;  // ceil(m / 256)
+  int slices;       // database slices per query tile
+  int64_t tiles_per_slice;
+  int cand_cap;     // per-query candidate pool
+  // workspace offsets (bytes from the workspace base)
+  size_t off_xh, off_xnorm, off_xscale, off_qh, off_qinfo, off_rpub, off_rflag, off_cand,
+      off_ccount, off_flags, off_fbq, off_fbd, off_fbi, off_fbpart_d, off_fbpart_i, total;
+  int fb_slices;
+};
+bool tc_supported(int d, int k);
+bool tc_make_plan(int64_t n, int64_t m, int d, int k, int slices, int cand_cap, TcPlan *p);
+// Returns 0 ok, 1 CUDA error, 2 device timeout.  t0/t1 (may be null) are
+// recorded around the main kernel; *launches counts the kernels launched.
+int tc_run(const float *Q, const float *X, int64_t id_offset, float *out_d, int32_t *out_i,
+           void *ws, const TcPlan &p, cudaStream_t stream, cudaEvent_t t0, cudaEvent_t t1,
+           int *launches);
+const void *tc_kernel_ptr(int d, int k);
+size_t tc_smem_bytes(int d, int k);
+
+}  // namespace bfk

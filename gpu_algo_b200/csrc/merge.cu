@@ -1,0 +1,95 @@
+// k-way merge of sorted candidate lists (per query) into the k best by
+// (distance, index).  Replaces bf_fp32_tiled_merge (bf/fp32_tiled.py:118-178)
+// and bf_fp32_qgroup_merge (bf/fp32_qgroup.py:153-213), which re-insert every
+// partial through a per-thread heap and a thread-0 serial merge; here one
+// block per query sorts 64-bit (distance, index) keys with a shared-memory
+// bitonic network, taking the lists in groups so any number of lists fits.
+#include "common.cuh"
+#include "internal.h"
+
+namespace bfk {
+
+constexpr int kMergeThreads = 256;
+constexpr int kMergeCap = 8192;  // keys sorted at once (64 KB of shared memory)
+
+__device__ void block_bitonic_sort(uint64_t *keys, int P) {
+  for (int size = 2; size <= P; size <<= 1) {
+    for (int stride = size >> 1; stride > 0; stride >>= 1) {
+      __syncthreads();
+      for (int t = threadIdx.x; t < P / 2; t += blockDim.x) {
+        int lo = 2 * stride * (t / stride) + (t % stride);
+        int hi = lo + stride;
+        bool up = ((lo & size) == 0);
+        uint64_t a = keys[lo], b = keys[hi];
+        if ((a > b) == up) { keys[lo] = b; keys[hi] = a; }
+      }
+    }
+  }
+  __syncthreads();
+}
+
+// grid (n), block kMergeThreads, dynamic smem kMergeCap * 8.
+// cand (lists, n, k) -> out (n, k)
+__global__ void __launch_bounds__(kMergeThreads) knn_merge_kernel(
+    const float *__restrict__ cand_d, const int32_t *__restrict__ cand_i, int64_t n, int lists,
+    int k, float *__restrict__ out_d, int32_t *__restrict__ out_i) {
+  extern __shared__ __align__(16) uint64_t keys[];
+  const int64_t qi = blockIdx.x;
+  const int group = (kMergeCap - k) / k;  // lists added per round (>= 1 since k <= kMergeCap/2)
+  int have = 0;                           // keys carried from the previous round (sorted)
+  for (int l0 = 0; l0 < lists; l0 += group) {
+    const int l1 = l0 + group < lists ? l0 + group : lists;
+    const int total = have + (l1 - l0) * k;
+    int P = 1;
+    while (P < total) P <<= 1;
+    for (int e = threadIdx.x; e < P - have; e += blockDim.x) {
+      uint64_t key = ~0ull;
+      if (e < (l1 - l0) * k) {
+        const int l = l0 + e / k, j = e % k;
+        const int64_t off = ((int64_t)l * n + qi) * k + j;
+        key = pair_key(cand_d[off], cand_i[off]);
+      }
+      keys[have + e] = key;
+    }
+    block_bitonic_sort(keys, P);
+    have = k;
+  }
+  for (int j = threadIdx.x; j < k; j += blockDim.x) {
+    const uint64_t key = keys[j];
+    const bool pad = key == ~0ull;
+    out_d[qi * k + j] = pad ? BFK_PAD_DIST : ord2f((uint32_t)(key >> 32));
+    out_i[qi * k + j] = pad ? -1 : (int32_t)(uint32_t)(key & 0xffffffffu);
+  }
+}
+
+cudaError_t launch_merge(const float *cand_d, const int32_t *cand_i, int64_t n, int lists, int k,
+                         float *out_d, int32_t *out_i, cudaStream_t stream) {
+  if (n == 0) return cudaSuccess;
+  const size_t smem = (size_t)kMergeCap * sizeof(uint64_t);
+  cudaError_t e = cudaFuncSetAttribute((const void *)knn_merge_kernel,
+                                       cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  if (e != cudaSuccess) return e;
+  knn_merge_kernel<<<(unsigned)n, kMergeThreads, smem, stream>>>(cand_d, cand_i, n, lists, k,
+                                                                 out_d, out_i);
+  return cudaGetLastError();
+}
+
+int merge_max_k() { return kMergeCap / 2; }
+
+__global__ void fill_pad_kernel(float *out_d, int32_t *out_i, int64_t count) {
+  for (int64_t e = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; e < count;
+       e += (int64_t)gridDim.x * blockDim.x) {
+    out_d[e] = BFK_PAD_DIST;
+    out_i[e] = -1;
+  }
+}
+
+cudaError_t launch_fill_pad(float *out_d, int32_t *out_i, int64_t count, cudaStream_t stream) {
+  if (count == 0) return cudaSuccess;
+  int64_t blocks = (count + 255) / 256;
+  if (blocks > 4096) blocks = 4096;
+  fill_pad_kernel<<<(unsigned)blocks, 256, 0, stream>>>(out_d, out_i, count);
+  return cudaGetLastError();
+}
+
+}  // namespace bfk

@@ -1,0 +1,159 @@
+"""Device-side search API over torch CUDA tensors (PyTorch is only the buffer).
+
+``search(Q, X, k)`` is the call every ``bf`` runner makes: Q (n, d) and X
+(m, d) float32 CUDA tensors (or any object with ``__cuda_array_interface__``,
+e.g. a CuPy array, wrapped without a copy) -> (dists (n, k) float32,
+ids (n, k) int32) on the same device, sorted ascending by (distance, index).
+"""
+from __future__ import annotations
+
+import ctypes
+import threading
+
+import torch
+
+from . import _lib
+
+_ws_lock = threading.Lock()
+_ws_cache: dict[tuple[int, int], torch.Tensor] = {}
+
+
+def as_device_f32(a, name: str) -> torch.Tensor:
+    """Zero-copy view of a CUDA float32 array as a contiguous torch tensor."""
+    if not isinstance(a, torch.Tensor):
+        if hasattr(a, "__cuda_array_interface__"):
+            a = torch.as_tensor(a, device="cuda")
+        else:
+            raise TypeError(f"{name} must be a CUDA array (torch tensor or __cuda_array_interface__)")
+    if not a.is_cuda:
+        raise TypeError(f"{name} must live on a CUDA device")
+    if a.dtype != torch.float32:
+        raise TypeError(f"{name} must be float32, got {a.dtype}")
+    if a.dim() != 2:
+        raise ValueError(f"{name} must be 2-D, got shape {tuple(a.shape)}")
+    return a.contiguous()
+
+
+def workspace(nbytes: int, device: torch.device, stream: torch.cuda.Stream | None = None
+              ) -> torch.Tensor:
+    """A cached, grow-only device workspace (one per device and stream)."""
+    dev = device.index if device.index is not None else torch.cuda.current_device()
+    s = stream if stream is not None else torch.cuda.current_stream(dev)
+    key = (dev, s.cuda_stream)
+    with _ws_lock:
+        buf = _ws_cache.get(key)
+        if buf is None or buf.numel() < nbytes:
+            buf = torch.empty(max(nbytes, 256), dtype=torch.uint8, device=f"cuda:{dev}")
+            _ws_cache[key] = buf
+        return buf
+
+
+def workspace_size(n: int, m: int, d: int, k: int, opts: _lib.Opts) -> int:
+    nb = ctypes.c_uint64()
+    _lib.check(_lib.load().bfk_workspace_size(n, m, d, k, ctypes.byref(opts), ctypes.byref(nb)),
+               "bfk_workspace_size")
+    return int(nb.value)
+
+
+def search(Q, X, k: int, *, engine: str = "auto", slices: int = 0, max_candidates: int = 0,
+           id_offset: int = 0, out: tuple[torch.Tensor, torch.Tensor] | None = None,
+           ws: torch.Tensor | None = None, time_main: bool = False):
+    """Exact k-NN on the GPU.  Returns (dists, ids) device tensors."""
+    Q = as_device_f32(Q, "Q")
+    X = as_device_f32(X, "X")
+    n, d = Q.shape
+    m = X.shape[0]
+    if X.shape[1] != d:
+        raise ValueError(f"Q has d={d} but X has d={X.shape[1]}")
+    if Q.device != X.device:
+        raise ValueError("Q and X must be on the same device")
+    k = int(k)
+    if k <= 0:
+        raise ValueError("k must be positive")
+    lib = _lib.load()
+    opts = _lib.make_opts(engine, slices, max_candidates,
+                          _lib.FLAG_TIME_MAIN if time_main else 0)
+    with torch.cuda.device(Q.device):
+        stream = torch.cuda.current_stream()
+        if out is None:
+            dists = torch.empty((n, k), dtype=torch.float32, device=Q.device)
+            ids = torch.empty((n, k), dtype=torch.int32, device=Q.device)
+        else:
+            dists, ids = out
+        nbytes = workspace_size(n, m, d, k, opts)
+        if ws is None:
+            ws = workspace(nbytes, Q.device, stream)
+        elif ws.numel() < nbytes:
+            raise ValueError(f"workspace needs {nbytes} bytes, got {ws.numel()}")
+        st = lib.bfk_search(Q.data_ptr(), n, X.data_ptr() if m else None, m, d, k, int(id_offset),
+                            dists.data_ptr(), ids.data_ptr(), ws.data_ptr(), ws.numel(),
+                            ctypes.byref(opts), ctypes.c_void_p(stream.cuda_stream))
+        _lib.check(st, "bfk_search")
+    return dists, ids
+
+
+def last_stats(Q, X, k: int, *, engine: str = "auto", slices: int = 0,
+               max_candidates: int = 0) -> dict:
+    """Statistics of the last search of this shape on the current stream's workspace."""
+    Q = as_device_f32(Q, "Q")
+    X = as_device_f32(X, "X")
+    n, d = Q.shape
+    m = X.shape[0]
+    opts = _lib.make_opts(engine, slices, max_candidates)
+    with torch.cuda.device(Q.device):
+        stream = torch.cuda.current_stream()
+        ws = workspace(workspace_size(n, m, d, k, opts), Q.device, stream)
+        s = _lib.Stats()
+        _lib.check(_lib.load().bfk_search_stats(ws.data_ptr(), n, m, d, k, ctypes.byref(opts),
+                                                ctypes.c_void_p(stream.cuda_stream),
+                                                ctypes.byref(s)), "bfk_search_stats")
+    return {
+        "engine": _lib.ENGINE_NAMES.get(s.engine_used, s.engine_used),
+        "fallback_queries": s.fallback_queries,
+        "candidates": s.candidates,
+        "max_query_candidates": s.max_query_candidates,
+        "slices": s.slices,
+        "survivors": s.survivors,
+        "device_error": s.device_error,
+        "kernel_launches": s.kernel_launches,
+        "timed_calls": s.timed_calls,
+        "main_kernel_ms": s.main_kernel_ms,
+    }
+
+
+def merge(cand_d: torch.Tensor, cand_i: torch.Tensor, k: int):
+    """Merge (lists, n, k) sorted candidate lists into the k best per query."""
+    if cand_d.dim() != 3 or cand_d.shape != cand_i.shape:
+        raise ValueError("candidates must be (lists, n, k) distance/index pairs")
+    if cand_d.dtype != torch.float32 or cand_i.dtype != torch.int32:
+        raise TypeError("candidates must be float32 distances and int32 indices")
+    lists, n, kk = cand_d.shape
+    if kk != k:
+        raise ValueError("list length must equal k")
+    cand_d = cand_d.contiguous()
+    cand_i = cand_i.contiguous()
+    with torch.cuda.device(cand_d.device):
+        stream = torch.cuda.current_stream()
+        out_d = torch.empty((n, k), dtype=torch.float32, device=cand_d.device)
+        out_i = torch.empty((n, k), dtype=torch.int32, device=cand_d.device)
+        _lib.check(_lib.load().bfk_merge(cand_d.data_ptr(), cand_i.data_ptr(), n, lists, k,
+                                         out_d.data_ptr(), out_i.data_ptr(),
+                                         ctypes.c_void_p(stream.cuda_stream)), "bfk_merge")
+    return out_d, out_i
+
+
+def kernel_attrs(engine: str, d: int, k: int) -> dict:
+    a = _lib.Attrs()
+    _lib.check(_lib.load().bfk_kernel_attrs(_lib.ENGINES[engine], d, k, ctypes.byref(a)),
+               "bfk_kernel_attrs")
+    return {
+        "num_regs": a.num_regs,
+        "shared_size_bytes": a.shared_size_bytes + a.dynamic_smem_bytes,
+        "local_size_bytes": a.local_size_bytes,
+        "const_size_bytes": a.const_size_bytes,
+        "max_threads_per_block": a.max_threads_per_block,
+        "binary_version": a.binary_version,
+        "ptx_version": a.ptx_version,
+        "block_threads": a.block_threads,
+        "dynamic_smem_bytes": a.dynamic_smem_bytes,
+    }

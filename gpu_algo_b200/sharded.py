@@ -1,0 +1,59 @@
+"""Row-sharded multi-GPU search: one process per GPU, NCCL over NVLink.
+
+The database is split by rows across the ranks of a process group; every
+rank searches its own shard (global row index = shard start + local row),
+one all-gather moves each rank's (n, k) sorted (distance, index) lists to
+every rank, and the on-device merge kernel (``bfk_merge``) reduces the
+(world, n, k) candidates to the final k per query.  The reference has no
+multi-GPU path; this is the exchange step its split-N partial/merge design
+(bf/fp32_tiled.py:182-239) implies once the tiles live on different GPUs.
+"""
+from __future__ import annotations
+
+from typing import Callable
+
+import torch
+import torch.distributed as dist
+
+
+def shard_range(total_rows: int, rank: int, world: int) -> tuple[int, int]:
+    """Rows [begin, end) of `rank`: contiguous, sizes differ by at most one."""
+    if world <= 0 or not 0 <= rank < world:
+        raise ValueError("bad rank/world")
+    base, rem = divmod(total_rows, world)
+    begin = rank * base + min(rank, rem)
+    return begin, begin + base + (1 if rank < rem else 0)
+
+
+def gather_lists(d_: torch.Tensor, i_: torch.Tensor, group=None) -> tuple[torch.Tensor, torch.Tensor]:
+    """All-gather (n, k) lists into (world, n, k) on every rank."""
+    world = dist.get_world_size(group)
+    n, k = d_.shape
+    all_d = torch.empty((world * n * k,), dtype=d_.dtype, device=d_.device)
+    all_i = torch.empty((world * n * k,), dtype=i_.dtype, device=i_.device)
+    dist.all_gather_into_tensor(all_d, d_.contiguous().view(-1), group=group)
+    dist.all_gather_into_tensor(all_i, i_.contiguous().view(-1), group=group)
+    return all_d.view(world, n, k), all_i.view(world, n, k)
+
+
+def sharded_search(Q, X_shard, k: int, row_begin: int, group=None,
+                   local_search: Callable | None = None,
+                   merge_fn: Callable | None = None) -> tuple[torch.Tensor, torch.Tensor]:
+    """Exact k-NN over the union of every rank's shard; result on every rank.
+
+    `local_search(Q, X, k, id_offset)` and `merge_fn(all_d, all_i, k)` default
+    to the CUDA engine; tests substitute CPU stand-ins to exercise the
+    orchestration over gloo.
+    """
+    if local_search is None:
+        from .engine import search
+
+        def local_search(Q_, X_, k_, id_offset):
+            return search(Q_, X_, k_, id_offset=id_offset)
+    if merge_fn is None:
+        from .engine import merge as merge_fn
+    d_, i_ = local_search(Q, X_shard, k, row_begin)
+    if not dist.is_initialized() or dist.get_world_size(group) == 1:
+        return d_, i_
+    all_d, all_i = gather_lists(d_, i_, group)
+    return merge_fn(all_d, all_i, k)

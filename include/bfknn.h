@@ -1,0 +1,147 @@
+/*
+ * bfknn -- exact brute-force k-NN for NVIDIA B200 (sm_100a), C ABI.
+ *
+ * Drop-in boundary for the reference's `bf/` kernels (hantaoyu-theory/gpu_algo).
+ * Every entry point takes plain pointers and sizes; device pointers are
+ * caller-owned CUDA device memory, `stream` is a cudaStream_t (NULL = the
+ * legacy default stream).  Launches are asynchronous on that stream; no entry
+ * point allocates device memory, calls exit(), or throws.  Results:
+ *   out_dists (n, k) float32  squared L2 distances, ascending;
+ *   out_ids   (n, k) int32    id_offset + database row, ties by lower index;
+ *   missing slots (m < k, or rows whose distance is NaN) are padded with
+ *   (3.402823e38f, -1).
+ * Distances are bit-identical to the reference kernels' direct-difference
+ * arithmetic (bf/fp32.py:74-82: dif = q - x; dist = fma(dif, dif, dist),
+ * in dimension order).
+ */
+#ifndef BFKNN_H_
+#define BFKNN_H_
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#if defined(__GNUC__)
+#define BFK_API __attribute__((visibility("default")))
+#else
+#define BFK_API
+#endif
+
+#define BFK_VERSION_MAJOR 0
+#define BFK_VERSION_MINOR 1
+
+typedef enum {
+  BFK_OK = 0,
+  BFK_ERR_INVALID_ARGUMENT = 1, /* null pointer, bad shape, k <= 0, misaligned pointer */
+  BFK_ERR_UNSUPPORTED = 2,      /* shape/k outside what the library was built for   */
+  BFK_ERR_WORKSPACE = 3,        /* workspace too small or not 256-byte aligned       */
+  BFK_ERR_CUDA = 4,             /* a CUDA runtime call failed                        */
+  BFK_ERR_DEVICE_TIMEOUT = 5,   /* a kernel's bounded wait ran out (device status)   */
+  BFK_ERR_NO_DEVICE = 6         /* no sm_100 device is current                       */
+} bfk_status_t;
+
+typedef enum {
+  BFK_ENGINE_AUTO = 0,   /* pick per shape                                              */
+  BFK_ENGINE_DIRECT = 1, /* SIMT direct differences with a fused per-query top-k        */
+  BFK_ENGINE_TC_F16 = 2  /* tcgen05 f16 distance filter + exact FP32 re-rank            */
+} bfk_engine_t;
+
+#define BFK_FLAG_TIME_MAIN 1 /* time the main kernel of every call with CUDA events      */
+
+typedef struct {
+  int32_t engine;         /* bfk_engine_t                                                */
+  int32_t slices;         /* database slices per query block, 0 = auto                   */
+  int32_t max_candidates; /* TC engines: per-query candidate pool, 0 = auto              */
+  int32_t flags;          /* BFK_FLAG_*                                                  */
+  int32_t reserved[4];    /* must be zero                                                */
+} bfk_opts_t;
+
+typedef struct {
+  int32_t num_regs;
+  int32_t shared_size_bytes;   /* static shared memory                                  */
+  int32_t dynamic_smem_bytes;  /* dynamic shared memory the launch requests             */
+  int32_t local_size_bytes;
+  int32_t const_size_bytes;
+  int32_t max_threads_per_block;
+  int32_t binary_version;
+  int32_t ptx_version;
+  int32_t block_threads;       /* threads per block used at launch                      */
+  int32_t reserved[7];
+} bfk_attrs_t;
+
+typedef struct {
+  int32_t engine_used;         /* bfk_engine_t actually run                              */
+  int32_t fallback_queries;    /* TC engines: queries finished by the exact SIMT engine  */
+  int64_t candidates;          /* TC engines: candidates written by the filter           */
+  int32_t max_query_candidates;
+  int32_t slices;
+  int64_t survivors;           /* TC engines: rows re-ranked with exact FP32             */
+  int32_t device_error;        /* device status word (0 = none)                          */
+  int32_t kernel_launches;     /* kernels the last call launched                         */
+  int32_t timed_calls;         /* calls timed since the last read (BFK_FLAG_TIME_MAIN)   */
+  float main_kernel_ms;        /* summed main-kernel time of those calls                 */
+  int32_t reserved[2];
+} bfk_stats_t;
+
+/* Library version.  No reference counterpart. */
+BFK_API bfk_status_t bfk_version(int32_t *major, int32_t *minor);
+
+/* Human-readable status.  No reference counterpart (the reference raises CuPy errors). */
+BFK_API const char *bfk_status_string(int32_t status);
+
+/*
+ * Device-memory workspace `bfk_search` needs for this shape (bytes, a multiple
+ * of 256).  Replaces the per-call CuPy allocations of the reference runners
+ * (bf/fp32.py:261-262, bf/fp32_tiled.py:204-207, bf/fp32_qgroup.py:245-248).
+ */
+BFK_API bfk_status_t bfk_workspace_size(int64_t n, int64_t m, int32_t d, int32_t k,
+                                const bfk_opts_t *opts, uint64_t *bytes);
+
+/*
+ * Exact k-NN of Q (n, d) against X (m, d), both row-major float32 device
+ * arrays.  Replaces one launch of the reference kernels:
+ *   bf_fp32 / bf_fp32_smallk   bf/fp32.py:265-271 (kernel bf/fp32.py:53-92, 115-192)
+ *   bf_fp32_heap               bf/fp32_heap.py:160-166
+ *   bf_fp32_tiled partial+merge bf/fp32_tiled.py:212-224
+ *   bf_fp32_qgroup partial+merge bf/fp32_qgroup.py:253-268
+ *   bf_fp32_q2                 bf/fp32_q2.py:160-166
+ * with the same (out_ids, out_dists) contract, sorted ascending.
+ * `workspace` must be 256-byte aligned and at least bfk_workspace_size bytes.
+ */
+BFK_API bfk_status_t bfk_search(const float *Q, int64_t n, const float *X, int64_t m, int32_t d,
+                        int32_t k, int64_t id_offset, float *out_dists, int32_t *out_ids,
+                        void *workspace, uint64_t workspace_bytes, const bfk_opts_t *opts,
+                        void *stream);
+
+/*
+ * Merge `lists` sorted candidate lists per query, laid out (lists, n, k), into
+ * the k best per query by (distance, index); index -1 entries are padding.
+ * Replaces bf_fp32_tiled_merge (bf/fp32_tiled.py:118-178) and
+ * bf_fp32_qgroup_merge (bf/fp32_qgroup.py:153-213); also merges the per-GPU
+ * lists of a sharded search.
+ */
+BFK_API bfk_status_t bfk_merge(const float *cand_dists, const int32_t *cand_ids, int64_t n,
+                       int32_t lists, int32_t k, float *out_dists, int32_t *out_ids,
+                       void *stream);
+
+/*
+ * Attributes of the main kernel an engine launches for (d, k).  Replaces
+ * kernel_attrs (bf/fp32.py:238-249, CuPy RawKernel.attributes).
+ */
+BFK_API bfk_status_t bfk_kernel_attrs(int32_t engine, int32_t d, int32_t k, bfk_attrs_t *out);
+
+/*
+ * Statistics of the last bfk_search that used this workspace (synchronises
+ * `stream`); also returns and resets the main-kernel times this thread
+ * recorded with BFK_FLAG_TIME_MAIN.  No reference counterpart.
+ */
+BFK_API bfk_status_t bfk_search_stats(const void *workspace, int64_t n, int64_t m, int32_t d, int32_t k,
+                              const bfk_opts_t *opts, void *stream, bfk_stats_t *out);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* BFKNN_H_ */

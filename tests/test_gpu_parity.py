@@ -1,0 +1,123 @@
+"""Parity of the CUDA engines with the oracle, through the C ABI (B200 only).
+
+The engines return the reference kernels' exact FP32 distances, so the check
+is bit-exact equality with the oracle's (distance, index) lists; the
+tolerance rule of check_parity (1e-5 tie window, 1e-4 relative distance) is
+asserted as well.
+"""
+import numpy as np
+import pytest
+import torch
+
+from gpu_algo_b200 import _lib, engine
+from oracle import check_parity, oracle_knn, oracle_merge
+
+pytestmark = pytest.mark.gpu
+
+ENGINES = ["direct", "auto"]
+
+
+def dev(a):
+    return torch.from_numpy(np.ascontiguousarray(a)).cuda()
+
+
+def run(Q, X, k, **kw):
+    d_, i_ = engine.search(dev(Q), dev(X), k, **kw)
+    torch.cuda.synchronize()
+    return d_.cpu().numpy(), i_.cpu().numpy()
+
+
+def assert_exact(got_d, got_i, exp_d, exp_i, what=""):
+    np.testing.assert_array_equal(got_i, exp_i, err_msg=f"{what}: ids")
+    np.testing.assert_array_equal(got_d, exp_d, err_msg=f"{what}: dists")
+
+
+@pytest.mark.parametrize("eng", ENGINES)
+def test_plumbing_bit_exact(plumbing, eng):
+    X, Q, gd, gi = plumbing
+    d_, i_ = run(Q, X, 10, engine=eng)
+    assert_exact(d_, i_, gd, gi, eng)
+    rd, ri = oracle_knn(Q[:128], X, 11)
+    assert check_parity(d_[:128], i_[:128], rd, ri, 10) == []
+
+
+@pytest.mark.parametrize("eng", ENGINES)
+def test_edge_cases_bit_exact(edges, eng):
+    for name, (Q, X, k, gd, gi) in edges.items():
+        d_, i_ = run(Q, X, k, engine=eng)
+        assert_exact(d_, i_, gd, gi, f"{eng}/{name}")
+
+
+@pytest.mark.parametrize("slices", [1, 3, 17, 64])
+def test_direct_slices_agree(plumbing, slices):
+    X, Q, gd, gi = plumbing
+    d_, i_ = run(Q[:100], X, 10, engine="direct", slices=slices)
+    assert_exact(d_, i_, gd[:100], gi[:100], f"slices={slices}")
+
+
+def test_id_offset_and_empty_inputs(plumbing):
+    X, Q, gd, gi = plumbing
+    d_, i_ = run(Q[:50], X, 10, id_offset=1_000_000)
+    assert_exact(d_, i_, gd[:50], gi[:50] + 1_000_000)
+    d_, i_ = run(Q[:5], X[:0], 7)
+    assert (i_ == -1).all() and (d_ == np.float32(3.402823e38)).all()
+    d_, i_ = run(Q[:0], X, 7)
+    assert d_.shape == (0, 7)
+
+
+def test_merge_kernel_matches_oracle_merge(plumbing):
+    X, Q, gd, gi = plumbing
+    rng = np.random.Generator(np.random.PCG64(3))
+    lists, n, k = 9, 300, 10
+    parts = [oracle_knn(Q[:n], X[a:a + 7000], k, id_offset=a)
+             for a in rng.integers(0, 58_000, size=lists)]
+    cd = np.stack([p[0] for p in parts])
+    ci = np.stack([p[1] for p in parts])
+    ci[2, :, 6:] = -1  # padding entries are skipped
+    cd[2, :, 6:] = np.float32(3.402823e38)
+    ed, ei = oracle_merge(cd, ci, k)
+    md, mi = engine.merge(dev(cd), dev(ci), k)
+    assert_exact(md.cpu().numpy(), mi.cpu().numpy(), ed, ei, "merge")
+
+
+def test_large_k_and_high_d():
+    rng = np.random.Generator(np.random.PCG64(11))
+    X = rng.standard_normal((20_000, 960), dtype=np.float32)
+    Q = rng.standard_normal((40, 960), dtype=np.float32)
+    for k in (100, 1024):
+        ed, ei = oracle_knn(Q, X, k)
+        d_, i_ = run(Q, X, k)
+        assert_exact(d_, i_, ed, ei, f"d=960 k={k}")
+
+
+def test_errors_are_raised():
+    Q = torch.zeros((4, 8), device="cuda")
+    X = torch.zeros((16, 8), device="cuda")
+    with pytest.raises(_lib.BfkError) as e:
+        engine.search(Q, X, 5000)
+    assert e.value.status == 2
+    with pytest.raises(TypeError):
+        engine.search(Q.double(), X, 3)
+    with pytest.raises(ValueError):
+        engine.search(Q, torch.zeros((16, 9), device="cuda"), 3)
+
+
+def test_bf_dropin_runners(plumbing):
+    from gpu_algo_b200.bf import fp32, fp32_heap, fp32_q2, fp32_qgroup, fp32_tiled
+    X, Q, gd, gi = plumbing
+    Qd, Xd = dev(Q[:200]), dev(X)
+    for res in (fp32.run_bf_fp32(Qd, Xd, 10, reps=2),
+                fp32_heap.run_bf_fp32_heap(Qd, Xd, 10, reps=2),
+                fp32_q2.run_bf_fp32_q2(Qd, Xd, 10, reps=2),
+                fp32_qgroup.run_bf_fp32_qgroup(Qd, Xd, 10, qpb=8, reps=2),
+                fp32_tiled.run_bf_fp32_tiled(Qd, Xd, 10, tile_size=20_000, reps=2)):
+        np.testing.assert_array_equal(res["ids"], gi[:200])
+        np.testing.assert_array_equal(res["dists"], gd[:200])
+        assert res["ms"] > 0 and res["block"] > 0
+    r = fp32_tiled.run_bf_fp32_tiled(Qd, Xd, 10, tile_size=20_000, reps=1)
+    assert r["n_tiles"] == 4 and r["tile_size"] == 20_000
+    fn, out_ids, out_dists, block, smem, attrs = fp32.build_bf_fp32_runner(Qd, Xd, 10)
+    fn()
+    torch.cuda.synchronize()
+    np.testing.assert_array_equal(out_ids.cpu().numpy(), gi[:200])
+    assert attrs["num_regs"] > 0 and "kernel_variant" in attrs
