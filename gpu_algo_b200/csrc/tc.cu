@@ -1,11 +1,878 @@
-// placeholder until the tcgen05 engine lands
+// Tensor-core engine: a tcgen05 f16 distance filter with a fused per-query
+// threshold, then an exact FP32 re-rank of the few survivors.
+//
+// Pass 0 (prep): queries and database rows are scaled by powers of two and
+//   rounded to f16 (rows in 256-row blocks sharing one scale), with their
+//   FP32 squared norms and a per-query error margin m (bound on |approx -
+//   reference distance|, derived below).
+// Pass 1 (filter, one CTA per (128-query tile, database slice)): TMA streams
+//   f16 row tiles (256 rows x 64 dims, 128-byte swizzle) into a shared-memory
+//   ring; one thread issues tcgen05.mma (M=128 queries, N=256 rows, K=16) into
+//   a double-buffered FP32 accumulator in tensor memory; four epilogue warps
+//   read it with tcgen05.ld (one query per thread) and compute
+//       v = ||x||^2 - 2 q.x   (= approximate distance - ||q||^2).
+//   Each thread keeps a max-heap of the k smallest v seen (shared memory);
+//   R = its root bounds the k-th reference distance from above once shifted
+//   by ||q||^2 + m, so every row with v <= R + 2m may be a true neighbour and
+//   is appended to the query's candidate pool in global memory.  Slices
+//   publish their final R so later CTAs of the same query tile start tight.
+// Pass 2 (select): per query, R* = k-th smallest v among its candidates (a
+//   radix select); rows with v <= R* + 2m are re-ranked with the reference
+//   arithmetic (dif = q - x; acc = fma(dif, dif, acc), bf/fp32.py:80) in FP32
+//   and the k best by (distance, index) are written.  Output distances are
+//   therefore bit-identical to the reference kernels'.
+// Queries whose pool overflows (degenerate data: huge exact-tie groups) are
+// finished by the exact SIMT engine.
+#include <cuda.h>
+#include <cudaTypedefs.h>
+
+#include <cmath>
+
 #include "common.cuh"
 #include "internal.h"
+
 namespace bfk {
-bool tc_supported(int, int) { return false; }
-bool tc_make_plan(int64_t, int64_t, int, int, int, int, TcPlan *) { return false; }
-int tc_run(const float *, const float *, int64_t, float *, int32_t *, void *, const TcPlan &,
-           cudaStream_t, cudaEvent_t, cudaEvent_t, int *) { return 1; }
-const void *tc_kernel_ptr(int, int) { return nullptr; }
-size_t tc_smem_bytes(int, int) { return 0; }
+
+constexpr int kBM = 128;            // queries per tile (MMA M, TMEM lanes)
+constexpr int kBN = 256;            // rows per tile (MMA N, accumulator columns)
+constexpr int kBK = 64;             // f16 elements per K chunk (128 bytes, one swizzle atom row)
+constexpr int kAChunkBytes = kBM * kBK * 2;   // 16 KB
+constexpr int kBChunkBytes = kBN * kBK * 2;   // 32 KB
+constexpr int kTcThreads = 192;     // warp 0 TMA, warp 1 MMA, warps 2-5 epilogue
+constexpr int kSmemLimit = 232448;  // 227 KB opt-in per block
+constexpr int kMaxKch = 4;          // d <= 256
+constexpr int kTcMaxK = 256;
+constexpr int kSelThreads = 256;
+constexpr int kSurvCap = 2048;      // exact re-rank capacity per query
+constexpr int kDefaultCandCap = 8192;
+constexpr int kRefreshTiles = 64;   // re-read published thresholds every this many tiles
+
+struct TcArgs {
+  const float *xnorm;     // (x_tiles*256) ||x||^2, NaN past m
+  const float *xinv;      // (x_tiles) 1/scale of each 256-row block
+  const float2 *qinfo;    // (q_tiles*128) (||q||^2, 2*margin); margin NaN for padding rows
+  const float *inv_sq;    // 1/scale of the queries (device scalar)
+  int64_t n, m;
+  int k, q_tiles, slices, tiles_per_slice;
+  int64_t x_tiles;
+  float *rpub;            // (q_tiles, slices, 128) published thresholds
+  int *rflag;             // (q_tiles, slices)
+  uint2 *cand;            // (n, cap) (row, v bits)
+  int *ccount;            // (n)
+  int cap;
+  WsHeader *hdr;
+};
+
+// ---------------------------------------------------------------------------
+// smem layout of the filter kernel
+// ---------------------------------------------------------------------------
+struct TcLayout {
+  int kch, ns, k;
+  size_t a_off, b_off, heap_off, nx_off, bar_off, total;
+};
+__host__ __device__ inline TcLayout tc_layout(int kch, int k) {
+  TcLayout L{};
+  L.kch = kch;
+  L.k = k;
+  L.a_off = 0;
+  L.b_off = (size_t)kch * kAChunkBytes;
+  const size_t fixed = (size_t)kBM * k * 4 + 2 * kBN * 4 + 256;
+  size_t ns = ((size_t)kSmemLimit - 1024 - L.b_off - fixed) / kBChunkBytes;
+  if (ns > 6) ns = 6;
+  L.ns = (int)ns;
+  L.heap_off = L.b_off + (size_t)L.ns * kBChunkBytes;
+  L.nx_off = L.heap_off + (size_t)kBM * k * 4;
+  L.bar_off = L.nx_off + 2 * kBN * 4;
+  L.total = L.bar_off + 256 + 1024;  // + alignment slack
+  return L;
 }
+
+__device__ __forceinline__ void set_error(WsHeader *h, int code, volatile int *abort_flag) {
+  atomicCAS(&h->error, 0, code);
+  *abort_flag = 1;
+}
+
+__device__ __forceinline__ void epi_bar() { asm volatile("bar.sync 1, 128;" ::: "memory"); }
+
+__device__ __forceinline__ int ld_acquire(const int *p) {
+  int v;
+  asm volatile("ld.acquire.gpu.global.b32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+__device__ __forceinline__ void st_release(int *p, int v) {
+  asm volatile("st.release.gpu.global.b32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+
+// min over the thresholds other slices of this query tile have published
+__device__ float read_published(const TcArgs &a, int qt, int s, int r) {
+  float best = INFINITY;
+  for (int s2 = 0; s2 < a.slices; s2++) {
+    if (s2 == s) continue;
+    const int slot = qt * a.slices + s2;
+    if (ld_acquire(a.rflag + slot)) best = fminf(best, a.rpub[(size_t)slot * kBM + r]);
+  }
+  return best;
+}
+
+// Rare path of the epilogue: append a candidate row to the query's pool and,
+// when it beats the heap root, replace the root and sift down.  Returns the
+// new root.  Kept out of line so the hot loop keeps its values in registers.
+__device__ __noinline__ float epi_insert(float vi, uint32_t row, float R, int k, float *hp,
+                                         uint2 *cand, int *ccount, int cap) {
+  const int slot = atomicAdd(ccount, 1);
+  if (slot < cap) cand[slot] = make_uint2(row, __float_as_uint(vi));
+  if (!(vi < R)) return R;
+  int p = 0;
+  for (;;) {
+    int c = 2 * p + 1;
+    if (c >= k) break;
+    float hc = hp[c * kBM];
+    if (c + 1 < k) {
+      const float h2 = hp[(c + 1) * kBM];
+      if (h2 > hc) { hc = h2; c++; }
+    }
+    if (hc <= vi) break;
+    hp[p * kBM] = hc;
+    p = c;
+  }
+  hp[p * kBM] = vi;
+  return hp[0];
+}
+
+__global__ void __launch_bounds__(kTcThreads, 1)
+    knn_tc_filter_kernel(const __grid_constant__ CUtensorMap tmap_q,
+                         const __grid_constant__ CUtensorMap tmap_x, const TcArgs a, int kch) {
+  extern __shared__ __align__(1024) unsigned char smem_raw[];
+  // align the dynamic smem base to 1024 bytes (swizzle atoms)
+  unsigned char *smem = reinterpret_cast<unsigned char *>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
+  const TcLayout L = tc_layout(kch, a.k);
+  unsigned char *sA = smem + L.a_off;
+  unsigned char *sB = smem + L.b_off;
+  float *heap = reinterpret_cast<float *>(smem + L.heap_off);
+  float *nxs = reinterpret_cast<float *>(smem + L.nx_off);
+  uint64_t *bars = reinterpret_cast<uint64_t *>(smem + L.bar_off);
+  uint64_t *full = bars;                 // [ns]
+  uint64_t *empty = bars + L.ns;         // [ns]
+  uint64_t *a_full = bars + 2 * L.ns;    // [1]
+  uint64_t *acc_full = a_full + 1;       // [2]
+  uint64_t *acc_empty = acc_full + 2;    // [2]
+  uint64_t *drain = acc_empty + 2;       // [1]
+  uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(drain + 1);
+  volatile int *abort_flag = reinterpret_cast<volatile int *>(tmem_slot + 1);
+  volatile int *epi_stop = abort_flag + 1;  // the epilogue's copy of abort_flag, one per tile
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int qt = blockIdx.x % a.q_tiles;
+  const int s = blockIdx.x / a.q_tiles;
+  const int64_t t_begin = (int64_t)s * a.tiles_per_slice;
+  int64_t t_end = t_begin + a.tiles_per_slice;
+  if (t_end > a.x_tiles) t_end = a.x_tiles;
+  const int ntiles = t_end > t_begin ? (int)(t_end - t_begin) : 0;
+  const int ns = L.ns;
+
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < ns; i++) { mbar_init(full + i, 1); mbar_init(empty + i, 1); }
+    mbar_init(a_full, 1);
+    mbar_init(acc_full, 1);
+    mbar_init(acc_full + 1, 1);
+    mbar_init(acc_empty, 4);
+    mbar_init(acc_empty + 1, 4);
+    mbar_init(drain, 1);
+    *abort_flag = 0;
+    *epi_stop = 0;
+    fence_mbar_init();
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, 512);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  if (warp == 0) {
+    // ---------------- TMA producer ----------------
+    if (lane == 0 && ntiles > 0) {
+      tma_prefetch_desc(&tmap_q);
+      tma_prefetch_desc(&tmap_x);
+      mbar_arrive_expect_tx(a_full, (uint32_t)(kch * kAChunkBytes));
+      for (int c = 0; c < kch; c++)
+        tma_load_2d(sA + c * kAChunkBytes, &tmap_q, a_full, c * kBK, qt * kBM);
+      uint32_t it = 0;
+      bool ok = true;
+      for (int lt = 0; lt < ntiles && ok; lt++) {
+        const int32_t row0 = (int32_t)((t_begin + lt) * kBN);
+        for (int c = 0; c < kch; c++, it++) {
+          const uint32_t st = it % ns, ph = (it / ns) & 1;
+          if (!mbar_wait_bounded(empty + st, ph ^ 1, abort_flag)) {
+            set_error(a.hdr, ERR_TIMEOUT_PRODUCER, abort_flag);
+            ok = false;
+            break;
+          }
+          mbar_arrive_expect_tx(full + st, kBChunkBytes);
+          tma_load_2d(sB + st * kBChunkBytes, &tmap_x, full + st, c * kBK, row0);
+        }
+      }
+      // every issued copy must land before the CTA may exit
+      const uint32_t first = it > (uint32_t)ns ? it - ns : 0;
+      for (uint32_t i = first; i < it; i++)
+        mbar_wait_bounded(full + (i % ns), (i / ns) & 1, abort_flag);
+      mbar_wait_bounded(a_full, 0, abort_flag);
+    }
+  } else if (warp == 1) {
+    // ---------------- MMA issuer ----------------
+    if (lane == 0 && ntiles > 0) {
+      constexpr uint32_t idesc = idesc_f16_f32(kBM, kBN);
+      const uint32_t a_addr = smem_u32(sA), b_addr = smem_u32(sB);
+      bool ok = mbar_wait_bounded(a_full, 0, abort_flag);
+      if (!ok) set_error(a.hdr, ERR_TIMEOUT_MMA, abort_flag);
+      uint32_t it = 0;
+      for (int lt = 0; lt < ntiles && ok; lt++) {
+        const int b = lt & 1;
+        if (!mbar_wait_bounded(acc_empty + b, ((lt >> 1) & 1) ^ 1, abort_flag)) {
+          set_error(a.hdr, ERR_TIMEOUT_MMA, abort_flag);
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + (uint32_t)(b * kBN);
+        for (int c = 0; c < kch && ok; c++, it++) {
+          const uint32_t st = it % ns, ph = (it / ns) & 1;
+          if (!mbar_wait_bounded(full + st, ph, abort_flag)) {
+            set_error(a.hdr, ERR_TIMEOUT_MMA, abort_flag);
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+#pragma unroll
+          for (int kk = 0; kk < kBK / 16; kk++) {
+            const uint64_t ad = umma_desc_k_sw128(a_addr + c * kAChunkBytes + kk * 32);
+            const uint64_t bd = umma_desc_k_sw128(b_addr + st * kBChunkBytes + kk * 32);
+            tc_mma_f16(d_tmem, ad, bd, idesc, (c | kk) != 0);
+          }
+          tc_commit(empty + st);
+        }
+        if (ok) tc_commit(acc_full + b);
+      }
+      // all issued MMAs must finish before tensor memory is released
+      tc_commit(drain);
+      mbar_wait_bounded(drain, 0, abort_flag);
+    }
+  } else {
+    // ---------------- epilogue: one query per thread ----------------
+    const int quarter = warp & 3;             // TMEM lanes this warp may access
+    const int r = quarter * 32 + lane;        // query row within the tile
+    const int tid_e = threadIdx.x - 64;       // 0..127 among epilogue threads
+    const int64_t q = (int64_t)qt * kBM + r;
+    const bool valid = q < a.n;
+    const float2 qi = a.qinfo[(size_t)qt * kBM + r];
+    const float m2 = qi.y;
+    const int k = a.k;
+    float *hp = heap + r;                     // heap slot i at hp[i * 128]
+    for (int i = 0; i < k; i++) hp[i * kBM] = INFINITY;
+    float R = INFINITY;                        // root of this thread's heap
+    float Rpub = valid ? read_published(a, qt, s, r) : INFINITY;
+    float theta = valid ? __fadd_ru(fminf(R, Rpub), m2) : -INFINITY;
+    int appended = 0;
+    uint2 *cand = a.cand + (size_t)(valid ? q : 0) * a.cap;
+    int *ccount = a.ccount + (valid ? q : 0);
+    const uint32_t lane_base = tmem_base + ((uint32_t)(quarter * 32) << 16);
+
+    const float inv_sq = *a.inv_sq;
+    for (int lt = 0; lt < ntiles; lt++) {
+      const int b = lt & 1;
+      const int64_t tile = t_begin + lt;
+      // stage ||x||^2 of the tile's 256 rows (NaN past m)
+      // Stop decision, uniform across the 128 epilogue threads: one thread snapshots
+      // the abort flag before the barrier and all read the snapshot after it.  The
+      // snapshot of the next tile is written only after everyone passed the second
+      // barrier of this tile, so no thread can see two different values.
+      if (tid_e == 0) *epi_stop = *abort_flag;
+      epi_bar();
+      if (*epi_stop) break;
+      nxs[b * kBN + tid_e] = a.xnorm[tile * kBN + tid_e];
+      nxs[b * kBN + 128 + tid_e] = a.xnorm[tile * kBN + 128 + tid_e];
+      const float cscale = -2.0f * inv_sq * a.xinv[tile];  // exact power of two
+      epi_bar();
+      if ((lt & (kRefreshTiles - 1)) == kRefreshTiles - 1 && valid) {
+        Rpub = fminf(Rpub, read_published(a, qt, s, r));
+        theta = __fadd_ru(fminf(R, Rpub), m2);
+      }
+      // tcgen05.ld is warp-collective: the whole warp proceeds or none of it
+      const bool got = __all_sync(0xffffffffu, mbar_wait_bounded(acc_full + b, (lt >> 1) & 1,
+                                                                 abort_flag));
+      if (!got) {
+        set_error(a.hdr, ERR_TIMEOUT_EPILOGUE, abort_flag);
+        continue;  // reach the next barrier, where every epilogue thread stops
+      }
+      tc_fence_after();
+      const float *nxt = nxs + b * kBN;
+      const int32_t row0 = (int32_t)(tile * kBN);
+#pragma unroll 1
+      for (int ch = 0; ch < kBN / 32; ch += 2) {
+        uint32_t va[32], vb[32];
+        tmem_ld_32x32b_x32(lane_base + (uint32_t)(b * kBN + ch * 32), va);
+        tmem_ld_32x32b_x32(lane_base + (uint32_t)(b * kBN + ch * 32 + 32), vb);
+        tmem_ld_wait();
+        if (ch == kBN / 32 - 2) {
+          // the accumulator is in registers: hand the buffer back to the MMA warp
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(acc_empty + b);
+        }
+        float v[64];
+        bool any = false;
+#pragma unroll
+        for (int i = 0; i < 32; i++) {
+          v[i] = __fmaf_rn(__uint_as_float(va[i]), cscale, nxt[ch * 32 + i]);
+          v[32 + i] = __fmaf_rn(__uint_as_float(vb[i]), cscale, nxt[ch * 32 + 32 + i]);
+        }
+#pragma unroll
+        for (int i = 0; i < 64; i++) any |= v[i] <= theta;
+        if (any) {
+#pragma unroll
+          for (int i = 0; i < 64; i++) {
+            if (v[i] <= theta) {
+              appended++;
+              R = epi_insert(v[i], (uint32_t)(row0 + ch * 32 + i), R, k, hp, cand, ccount, a.cap);
+              theta = __fadd_ru(fminf(R, Rpub), m2);
+            }
+          }
+        }
+      }
+    }
+    if (valid) {
+      atomicAdd(&a.hdr->candidates, (unsigned long long)appended);
+      a.rpub[((size_t)qt * a.slices + s) * kBM + r] = fminf(R, Rpub);
+    }
+    __threadfence();
+    epi_bar();
+    if (tid_e == 0) st_release(a.rflag + qt * a.slices + s, 1);
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  if (warp == 1) tmem_dealloc(tmem_base, 512);
+}
+
+// ---------------------------------------------------------------------------
+// prep: database rows -> f16 (256-row blocks share a power-of-two scale)
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ float pow2_scale_for(float maxabs) {
+  // scale s = 2^e with maxabs * s in [2^13, 2^14): f16 max is 65504
+  if (!(maxabs > 0.f) || !isfinite(maxabs)) return 1.f;
+  int e;
+  frexpf(maxabs, &e);  // maxabs = f * 2^e, f in [0.5, 1)
+  int p = 14 - e;
+  if (p > 126) p = 126;
+  if (p < -126) p = -126;
+  return ldexpf(1.f, p);
+}
+
+// grid (x_tiles), block 256 (8 warps x 32 rows)
+__global__ void __launch_bounds__(256) tc_prep_x_kernel(const float *__restrict__ X, int64_t m,
+                                                        int d, int d_pad, __half *__restrict__ Xh,
+                                                        float *__restrict__ xnorm,
+                                                        float *__restrict__ xinv, WsHeader *hdr) {
+  __shared__ float s_max[8], s_rn[8];
+  __shared__ float s_scale;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int64_t tile = blockIdx.x;
+  float wmax = 0.f, wrn = 0.f;
+  bool bad = false;
+  for (int rr = warp; rr < kBN; rr += 8) {
+    const int64_t row = tile * kBN + rr;
+    float nrm = NAN;
+    if (row < m) {
+      const float *x = X + row * d;
+      float ss = 0.f, mx = 0.f;
+      for (int c = lane; c < d; c += 32) {
+        const float v = x[c];
+        ss = __fmaf_rn(v, v, ss);
+        mx = fmaxf(mx, fabsf(v));
+      }
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) {
+        ss += __shfl_xor_sync(0xffffffffu, ss, o);
+        mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+      }
+      nrm = ss;
+      if (!isfinite(ss)) bad = true;
+      wmax = fmaxf(wmax, mx);
+      wrn = fmaxf(wrn, sqrtf(ss));
+    }
+    if (lane == 0) xnorm[row] = nrm;
+  }
+  if (lane == 0) { s_max[warp] = wmax; s_rn[warp] = wrn; }
+  if (bad && lane == 0) atomicOr(&hdr->nonfinite, 1);
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    float mx = 0.f, rn = 0.f;
+    for (int w = 0; w < 8; w++) { mx = fmaxf(mx, s_max[w]); rn = fmaxf(rn, s_rn[w]); }
+    const float sc = pow2_scale_for(mx);
+    s_scale = sc;
+    xinv[tile] = 1.f / sc;
+    // row norms only grow the bound: ordered as unsigned bits since they are >= 0
+    // sqrt of an FP32 sum of d squares: (1 + 2^-10) covers its rounding for d <= 4096
+    if (isfinite(rn)) atomicMax(&hdr->rx_bits, __float_as_uint(rn * (1.f + 0.0009765625f)));
+  }
+  __syncthreads();
+  const float sc = s_scale;
+  for (int rr = warp; rr < kBN; rr += 8) {
+    const int64_t row = tile * kBN + rr;
+    if (row >= m) break;
+    const float *x = X + row * d;
+    __half *xh = Xh + row * d_pad;
+    for (int c = lane; c < d_pad; c += 32)
+      xh[c] = __float2half_rn(c < d ? x[c] * sc : 0.f);
+  }
+}
+
+// max |Q| -> hdr->qmax_bits
+__global__ void tc_qmax_kernel(const float *__restrict__ Q, int64_t count, WsHeader *hdr) {
+  float mx = 0.f;
+  for (int64_t e = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; e < count;
+       e += (int64_t)gridDim.x * blockDim.x)
+    mx = fmaxf(mx, fabsf(Q[e]));
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+  if ((threadIdx.x & 31) == 0 && mx > 0.f) {
+    if (isfinite(mx)) atomicMax(&hdr->qmax_bits, __float_as_uint(mx));
+    else atomicOr(&hdr->nonfinite, 1);
+  }
+}
+
+// grid (q_tiles * 128 / 8), block 256: one warp per query row.  Writes the f16
+// query tile rows (zero for padding rows), ||q||^2 and the error margin.
+__global__ void __launch_bounds__(256) tc_prep_q_kernel(const float *__restrict__ Q, int64_t n,
+                                                        int d, int d_pad, int64_t q_rows,
+                                                        __half *__restrict__ Qh,
+                                                        float2 *__restrict__ qinfo,
+                                                        float *__restrict__ inv_sq_out,
+                                                        WsHeader *hdr) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int64_t row = (int64_t)blockIdx.x * 8 + warp;
+  if (row >= q_rows) return;
+  const float qmax = __uint_as_float(hdr->qmax_bits);
+  const float sq = pow2_scale_for(qmax);
+  if (row == 0 && lane == 0) *inv_sq_out = 1.f / sq;
+  __half *qh = Qh + row * d_pad;
+  if (row >= n) {
+    for (int c = lane; c < d_pad; c += 32) qh[c] = __float2half_rn(0.f);
+    if (lane == 0) qinfo[row] = make_float2(0.f, NAN);
+    return;
+  }
+  const float *qp = Q + row * d;
+  float ss = 0.f;
+  for (int c = lane; c < d_pad; c += 32) {
+    const float v = c < d ? qp[c] : 0.f;
+    ss = __fmaf_rn(v, v, ss);
+    qh[c] = __float2half_rn(v * sq);
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+  if (lane == 0) {
+    if (!isfinite(ss)) atomicOr(&hdr->nonfinite, 1);
+    // Error margin (see the header comment of this file): with u = 2^-11 the
+    // f16 unit roundoff, qn >= ||q||, Rx >= max ||x||,
+    //   e_q = u qn + sqrt(d) 2^-25 / s_q        (f16 rounding of q, incl. subnormals)
+    //   e_x = (u + sqrt(d) 2^-38) Rx             (rows scaled to [2^13, 2^14) per block)
+    //   dot rounding  <= e_q Rx + qn e_x + e_q e_x
+    //   accumulation  <= (d_pad + 16) 2^-22 (qn + e_q)(Rx + e_x)   (tensor-core FP32 sums)
+    //   FP32 terms    <= 2 (d + 8) 2^-24 (qn + Rx)^2  (norms, the fused epilogue step,
+    //                                                  and the reference's own rounding)
+    //   margin = 2 (dot rounding + accumulation) + FP32 terms;  stored: 2 * margin.
+    const double u = 1.0 / 2048.0;
+    const double qn = sqrt((double)ss) * (1.0 + ldexp(1.0, -10));
+    const double rx = (double)__uint_as_float(hdr->rx_bits);
+    const double sd = sqrt((double)d);
+    const double eq = u * qn + sd * ldexp(1.0, -25) / (double)sq;
+    const double ex = (u + sd * ldexp(1.0, -38)) * rx;
+    const double dotr = eq * rx + qn * ex + eq * ex;
+    const double acc = (double)(d_pad + 16) * ldexp(1.0, -22) * (qn + eq) * (rx + ex);
+    const double f32 = 2.0 * (double)(d + 8) * ldexp(1.0, -24) * (qn + rx) * (qn + rx);
+    const double margin = 2.0 * (dotr + acc) + f32;
+    qinfo[row] = make_float2(ss, __double2float_ru(2.0 * margin * (1.0 + 1e-6)));
+  }
+}
+
+// ---------------------------------------------------------------------------
+// select + exact re-rank: one block per query
+// ---------------------------------------------------------------------------
+__device__ void bitonic_sort_u64(uint64_t *keys, int P) {
+  for (int size = 2; size <= P; size <<= 1) {
+    for (int stride = size >> 1; stride > 0; stride >>= 1) {
+      __syncthreads();
+      for (int t = threadIdx.x; t < P / 2; t += blockDim.x) {
+        const int lo = 2 * stride * (t / stride) + (t % stride);
+        const int hi = lo + stride;
+        const bool up = (lo & size) == 0;
+        const uint64_t x = keys[lo], y = keys[hi];
+        if ((x > y) == up) { keys[lo] = y; keys[hi] = x; }
+      }
+    }
+  }
+  __syncthreads();
+}
+
+struct SelArgs {
+  const float *Q;
+  const float *X;
+  int64_t n, m;
+  int d, k, cap;
+  int64_t id_offset;
+  const float2 *qinfo;
+  const uint2 *cand;
+  const int *ccount;
+  int *fb_list;       // queries left to the SIMT engine
+  WsHeader *hdr;
+  float *out_d;
+  int32_t *out_i;
+};
+
+// dynamic smem: cap * 8 (candidates) + kSurvCap * 8 (survivor keys) + d * 4 (query)
+__global__ void __launch_bounds__(kSelThreads) tc_select_kernel(const SelArgs a) {
+  extern __shared__ __align__(1024) unsigned char smem_raw[];
+  uint2 *cs = reinterpret_cast<uint2 *>(smem_raw);
+  uint64_t *keys = reinterpret_cast<uint64_t *>(cs + a.cap);
+  float *qs = reinterpret_cast<float *>(keys + kSurvCap);
+  __shared__ int hist[256];
+  __shared__ int s_nsurv, s_sel_rank;
+  __shared__ uint32_t s_prefix;
+  const int64_t q = blockIdx.x;
+  const int cnt = a.ccount[q];
+  // overflowed pool, or non-finite inputs (the margin argument needs finite norms)
+  if (cnt > a.cap || a.hdr->nonfinite) {
+    if (threadIdx.x == 0) {
+      const int slot = atomicAdd(&a.hdr->fallback, 1);
+      a.fb_list[slot] = (int)q;
+    }
+    return;
+  }
+  for (int e = threadIdx.x; e < cnt; e += blockDim.x) cs[e] = a.cand[(size_t)q * a.cap + e];
+  for (int c = threadIdx.x; c < a.d; c += blockDim.x) qs[c] = a.Q[q * a.d + c];
+  if (threadIdx.x == 0) { s_nsurv = 0; s_prefix = 0u; s_sel_rank = a.k; }
+  __syncthreads();
+  // R* = k-th smallest v (radix select over order-preserving keys)
+  float theta = INFINITY;
+  if (cnt >= a.k) {
+    uint32_t mask = 0u;
+    for (int shift = 24; shift >= 0; shift -= 8) {
+      for (int b = threadIdx.x; b < 256; b += blockDim.x) hist[b] = 0;
+      __syncthreads();
+      const uint32_t prefix = s_prefix;
+      for (int e = threadIdx.x; e < cnt; e += blockDim.x) {
+        const uint32_t key = f2ord(__uint_as_float(cs[e].y));
+        if ((key & mask) == prefix) atomicAdd(&hist[(key >> shift) & 255], 1);
+      }
+      __syncthreads();
+      if (threadIdx.x == 0) {
+        int need = s_sel_rank, b = 0;
+        for (; b < 255; b++) {
+          if (hist[b] >= need) break;
+          need -= hist[b];
+        }
+        s_sel_rank = need;
+        s_prefix = prefix | ((uint32_t)b << shift);
+      }
+      __syncthreads();
+      mask |= 255u << shift;
+    }
+    theta = __fadd_ru(ord2f(s_prefix), a.qinfo[q].y);
+  }
+  // survivors -> exact distance with the reference arithmetic
+  for (int e = threadIdx.x; e < cnt; e += blockDim.x) {
+    const float v = __uint_as_float(cs[e].y);
+    if (v <= theta) {
+      const int slot = atomicAdd(&s_nsurv, 1);
+      if (slot < kSurvCap) {
+        const int64_t row = cs[e].x;
+        const float *x = a.X + row * a.d;
+        float acc = 0.f;
+        for (int c = 0; c < a.d; c++) acc = dist_step(qs[c], x[c], acc);
+        keys[slot] = acc == acc ? pair_key(acc, (int32_t)(a.id_offset + row)) : ~0ull;
+      }
+    }
+  }
+  __syncthreads();
+  const int ns = s_nsurv;
+  if (ns > kSurvCap) {
+    if (threadIdx.x == 0) {
+      const int slot = atomicAdd(&a.hdr->fallback, 1);
+      a.fb_list[slot] = (int)q;
+    }
+    return;
+  }
+  int P = 1;
+  while (P < ns || P < 2) P <<= 1;
+  for (int e = ns + threadIdx.x; e < P; e += blockDim.x) keys[e] = ~0ull;
+  bitonic_sort_u64(keys, P);
+  for (int j = threadIdx.x; j < a.k; j += blockDim.x) {
+    const uint64_t key = j < ns ? keys[j] : ~0ull;
+    const bool pad = key == ~0ull;
+    a.out_d[q * a.k + j] = pad ? BFK_PAD_DIST : ord2f((uint32_t)(key >> 32));
+    a.out_i[q * a.k + j] = pad ? -1 : (int32_t)(uint32_t)(key & 0xffffffffu);
+  }
+  if (threadIdx.x == 0) {
+    atomicAdd(&a.hdr->survivors, (unsigned long long)ns);
+    atomicMax(&a.hdr->max_cand, cnt);
+  }
+}
+
+// fallback helpers: gather rows of Q; scatter merged rows back
+__global__ void tc_gather_rows(const float *__restrict__ Q, int d, const int *__restrict__ list,
+                               int count, float *__restrict__ out) {
+  for (int64_t e = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; e < (int64_t)count * d;
+       e += (int64_t)gridDim.x * blockDim.x)
+    out[e] = Q[(int64_t)list[e / d] * d + e % d];
+}
+__global__ void tc_scatter_rows(const float *__restrict__ sd, const int32_t *__restrict__ si,
+                                int k, const int *__restrict__ list, int count,
+                                float *__restrict__ out_d, int32_t *__restrict__ out_i) {
+  for (int64_t e = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; e < (int64_t)count * k;
+       e += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t q = list[e / k];
+    out_d[q * k + e % k] = sd[e];
+    out_i[q * k + e % k] = si[e];
+  }
+}
+
+// ---------------------------------------------------------------------------
+// host side
+// ---------------------------------------------------------------------------
+static size_t al256(size_t x) { return (x + 255) & ~(size_t)255; }
+
+static int kch_for(int d) { return (d + kBK - 1) / kBK; }
+
+bool tc_supported(int d, int k) {
+  if (d <= 0 || d > kMaxKch * kBK || k <= 0 || k > kTcMaxK) return false;
+  const TcLayout L = tc_layout(kch_for(d), k);
+  return L.ns >= 2 && L.total <= (size_t)kSmemLimit;
+}
+
+size_t tc_smem_bytes(int d, int k) { return tc_layout(kch_for(d), k).total; }
+
+const void *tc_kernel_ptr(int, int) { return (const void *)knn_tc_filter_kernel; }
+
+static int num_sms() {
+  int dev = 0, sms = 148;
+  if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  return sms > 0 ? sms : 148;
+}
+
+bool tc_make_plan(int64_t n, int64_t m, int d, int k, int slices, int cand_cap, TcPlan *p) {
+  if (!tc_supported(d, k) || n <= 0 || m <= 0) return false;
+  TcPlan P{};
+  P.n = n;
+  P.m = m;
+  P.d = d;
+  P.k = k;
+  P.d_pad = kch_for(d) * kBK;
+  P.q_tiles = (int)((n + kBM - 1) / kBM);
+  P.x_tiles = (m + kBN - 1) / kBN;
+  if (slices <= 0) {
+    // fill the SMs with whole waves: pick the slice count whose last wave is fullest,
+    // with slices no shorter than 64 tiles where possible
+    const int sms = num_sms();
+    const int64_t max_s = P.x_tiles;
+    int best = 1;
+    double best_eff = -1.0;
+    for (int s = 1; s <= 512 && s <= max_s; s++) {
+      const int64_t ctas = (int64_t)P.q_tiles * s;
+      const int64_t tps = (P.x_tiles + s - 1) / s;
+      if (s > 1 && tps < 64 && ctas > sms) break;
+      const int64_t waves = (ctas + sms - 1) / sms;
+      const double eff = (double)ctas / (double)(waves * sms);
+      if (eff > best_eff + 0.02) { best_eff = eff; best = s; }
+      if (eff > 0.97) break;
+    }
+    slices = best;
+  }
+  if (slices > P.x_tiles) slices = (int)P.x_tiles;
+  P.tiles_per_slice = (P.x_tiles + slices - 1) / slices;
+  P.slices = (int)((P.x_tiles + P.tiles_per_slice - 1) / P.tiles_per_slice);
+  P.cand_cap = cand_cap > 0 ? cand_cap : kDefaultCandCap;
+  if (P.cand_cap < k) P.cand_cap = k;
+  if ((size_t)P.cand_cap * 8 + kSurvCap * 8 + (size_t)d * 4 > (size_t)kSmemLimit - 4096) return false;
+  // fallback: the SIMT engine over up to n queries in slices
+  P.fb_slices = (int)((m + 262143) / 262144);
+  if (P.fb_slices > 32) P.fb_slices = 32;
+  if (P.fb_slices < 1) P.fb_slices = 1;
+  const int64_t q_rows = (int64_t)P.q_tiles * kBM;
+  size_t off = sizeof(WsHeader);
+  P.off_xh = off;       off = al256(off + (size_t)m * P.d_pad * 2);
+  P.off_xnorm = off;    off = al256(off + (size_t)P.x_tiles * kBN * 4);
+  P.off_xscale = off;   off = al256(off + (size_t)P.x_tiles * 4 + 16);
+  P.off_qh = off;       off = al256(off + (size_t)q_rows * P.d_pad * 2);
+  P.off_qinfo = off;    off = al256(off + (size_t)q_rows * 8);
+  P.off_rpub = off;     off = al256(off + (size_t)P.q_tiles * P.slices * kBM * 4);
+  P.off_rflag = off;    off = al256(off + (size_t)P.q_tiles * P.slices * 4);
+  P.off_cand = off;     off = al256(off + (size_t)n * P.cand_cap * 8);
+  P.off_ccount = off;   off = al256(off + (size_t)n * 4);
+  P.off_flags = off;    off = al256(off + (size_t)n * 4);
+  P.off_fbq = off;      off = al256(off + (size_t)n * d * 4);
+  P.off_fbd = off;      off = al256(off + (size_t)n * k * 4);
+  P.off_fbi = off;      off = al256(off + (size_t)n * k * 4);
+  P.off_fbpart_d = off; off = al256(off + (size_t)P.fb_slices * n * k * 4);
+  P.off_fbpart_i = off; off = al256(off + (size_t)P.fb_slices * n * k * 4);
+  P.total = off;
+  *p = P;
+  return true;
+}
+
+static PFN_cuTensorMapEncodeTiled_v12000 get_encode() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  if (!fn) {
+    void *ptr = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q) ==
+            cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(ptr);
+  }
+  return fn;
+}
+
+// 2D f16 tensor map: rows x cols (cols contiguous), box box_rows x 64, 128B swizzle
+static bool make_tmap(CUtensorMap *map, const void *base, int64_t rows, int cols_pad,
+                      int box_rows) {
+  auto enc = get_encode();
+  if (!enc) return false;
+  cuuint64_t dims[2] = {(cuuint64_t)cols_pad, (cuuint64_t)rows};
+  cuuint64_t strides[1] = {(cuuint64_t)cols_pad * 2};
+  cuuint32_t box[2] = {(cuuint32_t)kBK, (cuuint32_t)box_rows};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<void *>(base), dims,
+                   strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                   CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS;
+}
+
+int tc_run(const float *Q, const float *X, int64_t id_offset, float *out_d, int32_t *out_i,
+           void *ws_, const TcPlan &p, cudaStream_t stream, cudaEvent_t t0, cudaEvent_t t1,
+           int *launches) {
+  unsigned char *ws = static_cast<unsigned char *>(ws_);
+  WsHeader *hdr = reinterpret_cast<WsHeader *>(ws);
+  __half *Xh = reinterpret_cast<__half *>(ws + p.off_xh);
+  float *xnorm = reinterpret_cast<float *>(ws + p.off_xnorm);
+  float *xinv = reinterpret_cast<float *>(ws + p.off_xscale);
+  float *inv_sq = xinv + p.x_tiles;  // one float after the block scales
+  __half *Qh = reinterpret_cast<__half *>(ws + p.off_qh);
+  float2 *qinfo = reinterpret_cast<float2 *>(ws + p.off_qinfo);
+  float *rpub = reinterpret_cast<float *>(ws + p.off_rpub);
+  int *rflag = reinterpret_cast<int *>(ws + p.off_rflag);
+  uint2 *cand = reinterpret_cast<uint2 *>(ws + p.off_cand);
+  int *ccount = reinterpret_cast<int *>(ws + p.off_ccount);
+  int *fb_list = reinterpret_cast<int *>(ws + p.off_flags);
+  const int64_t q_rows = (int64_t)p.q_tiles * kBM;
+  int nl = 0;
+
+#define BFK_TRY(x)                    \
+  do {                                \
+    if ((x) != cudaSuccess) return 1; \
+  } while (0)
+
+  BFK_TRY(cudaMemsetAsync(hdr, 0, sizeof(WsHeader), stream));
+  BFK_TRY(cudaMemsetAsync(rflag, 0, (size_t)p.q_tiles * p.slices * 4, stream));
+  BFK_TRY(cudaMemsetAsync(ccount, 0, (size_t)p.n * 4, stream));
+  // pass 0: prep
+  tc_qmax_kernel<<<592, 256, 0, stream>>>(Q, p.n * p.d, hdr);
+  tc_prep_x_kernel<<<(unsigned)p.x_tiles, 256, 0, stream>>>(X, p.m, p.d, p.d_pad, Xh, xnorm, xinv, hdr);
+  tc_prep_q_kernel<<<(unsigned)(q_rows / 8), 256, 0, stream>>>(Q, p.n, p.d, p.d_pad, q_rows, Qh,
+                                                                qinfo, inv_sq, hdr);
+  nl += 3;
+  BFK_TRY(cudaGetLastError());
+
+  // pass 1: filter
+  CUtensorMap tq, tx;
+  if (!make_tmap(&tq, Qh, q_rows, p.d_pad, kBM)) return 1;
+  if (!make_tmap(&tx, Xh, p.m, p.d_pad, kBN)) return 1;
+  TcArgs A{};
+  A.xnorm = xnorm;
+  A.xinv = xinv;
+  A.qinfo = qinfo;
+  A.inv_sq = inv_sq;
+  A.n = p.n;
+  A.m = p.m;
+  A.k = p.k;
+  A.q_tiles = p.q_tiles;
+  A.slices = p.slices;
+  A.tiles_per_slice = (int)p.tiles_per_slice;
+  A.x_tiles = p.x_tiles;
+  A.rpub = rpub;
+  A.rflag = rflag;
+  A.cand = cand;
+  A.ccount = ccount;
+  A.cap = p.cand_cap;
+  A.hdr = hdr;
+  const int kch = p.d_pad / kBK;
+  const size_t smem = tc_smem_bytes(p.d, p.k);
+  BFK_TRY(cudaFuncSetAttribute((const void *)knn_tc_filter_kernel,
+                               cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+  if (t0) cudaEventRecord(t0, stream);
+  knn_tc_filter_kernel<<<(unsigned)(p.q_tiles * p.slices), kTcThreads, smem, stream>>>(tq, tx, A,
+                                                                                       kch);
+  if (t1) cudaEventRecord(t1, stream);
+  nl++;
+  BFK_TRY(cudaGetLastError());
+
+  // pass 2: select + exact re-rank
+  SelArgs S{};
+  S.Q = Q;
+  S.X = X;
+  S.n = p.n;
+  S.m = p.m;
+  S.d = p.d;
+  S.k = p.k;
+  S.cap = p.cand_cap;
+  S.id_offset = id_offset;
+  S.qinfo = qinfo;
+  S.cand = cand;
+  S.ccount = ccount;
+  S.fb_list = fb_list;
+  S.hdr = hdr;
+  S.out_d = out_d;
+  S.out_i = out_i;
+  const size_t ssmem = (size_t)p.cand_cap * 8 + kSurvCap * 8 + (size_t)p.d * 4;
+  BFK_TRY(cudaFuncSetAttribute((const void *)tc_select_kernel,
+                               cudaFuncAttributeMaxDynamicSharedMemorySize, (int)ssmem));
+  tc_select_kernel<<<(unsigned)p.n, kSelThreads, ssmem, stream>>>(S);
+  nl++;
+  BFK_TRY(cudaGetLastError());
+
+  // queries the filter could not finish (pool overflow) -> exact SIMT engine
+  int32_t h_fb = 0, h_err = 0;
+  BFK_TRY(cudaMemcpyAsync(&h_fb, &hdr->fallback, 4, cudaMemcpyDeviceToHost, stream));
+  BFK_TRY(cudaMemcpyAsync(&h_err, &hdr->error, 4, cudaMemcpyDeviceToHost, stream));
+  BFK_TRY(cudaStreamSynchronize(stream));
+  if (h_err) {
+    *launches = nl;
+    return 2;
+  }
+  if (h_fb > 0) {
+    float *Qf = reinterpret_cast<float *>(ws + p.off_fbq);
+    float *fd = reinterpret_cast<float *>(ws + p.off_fbd);
+    int32_t *fi = reinterpret_cast<int32_t *>(ws + p.off_fbi);
+    float *pd = reinterpret_cast<float *>(ws + p.off_fbpart_d);
+    int32_t *pi = reinterpret_cast<int32_t *>(ws + p.off_fbpart_i);
+    tc_gather_rows<<<256, 256, 0, stream>>>(Q, p.d, fb_list, h_fb, Qf);
+    BFK_TRY(launch_direct(Qf, h_fb, X, p.m, p.d, p.k, id_offset, p.fb_slices, h_fb >= 64 ? 4 : 1,
+                          p.fb_slices > 1 ? pd : fd, p.fb_slices > 1 ? pi : fi, stream));
+    nl += 2;
+    if (p.fb_slices > 1) {
+      BFK_TRY(launch_merge(pd, pi, h_fb, p.fb_slices, p.k, fd, fi, stream));
+      nl++;
+    }
+    tc_scatter_rows<<<256, 256, 0, stream>>>(fd, fi, p.k, fb_list, h_fb, out_d, out_i);
+    nl++;
+    BFK_TRY(cudaGetLastError());
+  }
+  *launches = nl;
+  return 0;
+#undef BFK_TRY
+}
+
+}  // namespace bfk

@@ -14,7 +14,7 @@ from oracle import check_parity, oracle_knn, oracle_merge
 
 pytestmark = pytest.mark.gpu
 
-ENGINES = ["direct", "auto"]
+ENGINES = ["direct", "auto", "tc_f16"]
 
 
 def dev(a):
@@ -25,6 +25,16 @@ def run(Q, X, k, **kw):
     d_, i_ = engine.search(dev(Q), dev(X), k, **kw)
     torch.cuda.synchronize()
     return d_.cpu().numpy(), i_.cpu().numpy()
+
+
+def tc_ok(d, k):
+    """Whether the tensor-core engine takes this (d, k) (it rejects, never falls back)."""
+    try:
+        engine.workspace_size(64, 8192, d, k, _lib.make_opts("tc_f16"))
+        return True
+    except _lib.BfkError as e:
+        assert e.status == 2
+        return False
 
 
 def assert_exact(got_d, got_i, exp_d, exp_i, what=""):
@@ -44,8 +54,61 @@ def test_plumbing_bit_exact(plumbing, eng):
 @pytest.mark.parametrize("eng", ENGINES)
 def test_edge_cases_bit_exact(edges, eng):
     for name, (Q, X, k, gd, gi) in edges.items():
+        if eng == "tc_f16" and not tc_ok(Q.shape[1], k):
+            continue
         d_, i_ = run(Q, X, k, engine=eng)
         assert_exact(d_, i_, gd, gi, f"{eng}/{name}")
+
+
+def test_tc_stats_plumbing(plumbing):
+    X, Q, gd, gi = plumbing
+    Qd, Xd = dev(Q), dev(X)
+    engine.search(Qd, Xd, 10, engine="tc_f16")
+    st = engine.last_stats(Qd, Xd, 10, engine="tc_f16")
+    assert st["engine"] == "tc_f16" and st["device_error"] == 0
+    assert st["fallback_queries"] == 0
+    assert st["survivors"] >= Q.shape[0] * 10
+    assert st["candidates"] >= st["survivors"]
+
+
+@pytest.mark.parametrize("slices", [1, 2, 5, 64])
+def test_tc_slices_agree(plumbing, slices):
+    X, Q, gd, gi = plumbing
+    d_, i_ = run(Q[:300], X, 10, engine="tc_f16", slices=slices)
+    assert_exact(d_, i_, gd[:300], gi[:300], f"tc slices={slices}")
+
+
+def test_tc_pool_overflow_falls_back_exactly(plumbing):
+    X, Q, gd, gi = plumbing
+    Qd, Xd = dev(Q[:200]), dev(X)
+    d_, i_ = engine.search(Qd, Xd, 10, engine="tc_f16", max_candidates=12)
+    st = engine.last_stats(Qd, Xd, 10, engine="tc_f16", max_candidates=12)
+    assert st["fallback_queries"] > 0
+    assert_exact(d_.cpu().numpy(), i_.cpu().numpy(), gd[:200], gi[:200], "overflow")
+
+
+def test_tc_nonfinite_rows_use_exact_engine():
+    rng = np.random.Generator(np.random.PCG64(5))
+    X = rng.standard_normal((9000, 64), dtype=np.float32)
+    X[123, 7] = np.nan
+    X[4567, 0] = np.inf
+    Q = rng.standard_normal((130, 64), dtype=np.float32)
+    ed, ei = oracle_knn(Q, X, 16)
+    d_, i_ = run(Q, X, 16, engine="tc_f16")
+    assert_exact(d_, i_, ed, ei, "nonfinite")
+
+
+@pytest.mark.parametrize("name,n,m,k", [("mixture-k-sweep", 300, 200_000, 32),
+                                        ("mixture-k-sweep", 257, 120_000, 100),
+                                        ("unit-10m", 256, 300_000, 100),
+                                        ("stream-100m", 130, 250_000, 10),
+                                        ("mixture-k-sweep", 200, 100_000, 1)])
+def test_tc_workload_samples(name, n, m, k):
+    from gpu_algo_b200 import data
+    X, Q = data.workload_arrays(name, n_rows=m, n_queries=n)
+    ed, ei = oracle_knn(Q, X, k)
+    d_, i_ = run(Q, X, k, engine="tc_f16")
+    assert_exact(d_, i_, ed, ei, f"{name} n={n} m={m} k={k}")
 
 
 @pytest.mark.parametrize("slices", [1, 3, 17, 64])
