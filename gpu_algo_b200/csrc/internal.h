@@ -20,18 +20,28 @@ int merge_max_k();
 cudaError_t launch_fill_pad(float *out_d, int32_t *out_i, int64_t count, cudaStream_t stream);
 
 // tc.cu -- tcgen05 filter engine
+constexpr int kMaxLevels = 6;
+struct LevelPlan {
+  int64_t tiles;            // 256-row tiles this level reads (evenly spaced)
+  int64_t tiles_per_slice;
+  int slices;
+  int region;               // candidate entries per (query, slice)
+};
 struct TcPlan {
   int64_t n, m;
   int d, k;
   int d_pad;        // d rounded up to 64 (f16 K chunks of 128 bytes)
   int q_tiles;      // ceil(n / 128)
   int64_t x_tiles;  // ceil(m / 256)
-  int slices;       // database slices per query tile
+  int levels;       // filter passes; the last one reads every tile
+  LevelPlan level[kMaxLevels];
+  int slices;       // slices of the last level
   int64_t tiles_per_slice;
-  int cand_cap;     // per-query candidate pool
+  int max_slices;
+  int cand_cap;     // candidate entries per query
   // workspace offsets (bytes from the workspace base)
-  size_t off_xh, off_xnorm, off_xscale, off_qh, off_qinfo, off_rpub, off_rflag, off_cand,
-      off_ccount, off_flags, off_fbq, off_fbd, off_fbi, off_fbpart_d, off_fbpart_i, total;
+  size_t off_xh, off_xnorm, off_xscale, off_qh, off_qinfo, off_rlev, off_cand, off_ccount,
+      off_flags, off_fbq, off_fbd, off_fbi, off_fbpart_d, off_fbpart_i, total;
   int fb_slices;
 };
 bool tc_supported(int d, int k);

@@ -1,28 +1,31 @@
-// Tensor-core engine: a tcgen05 f16 distance filter with a fused per-query
-// threshold, then an exact FP32 re-rank of the few survivors.
+// Tensor-core engine: tcgen05 f16 distance filter passes under sampled
+// per-query thresholds, then an exact FP32 re-rank of the few survivors.
 //
 // Pass 0 (prep): queries and database rows are scaled by powers of two and
-//   rounded to f16 (rows in 256-row blocks sharing one scale), with their
-//   FP32 squared norms and a per-query error margin m (bound on |approx -
-//   reference distance|, derived below).
-// Pass 1 (filter, one CTA per (128-query tile, database slice)): TMA streams
-//   f16 row tiles (256 rows x 64 dims, 128-byte swizzle) into a shared-memory
-//   ring; one thread issues tcgen05.mma (M=128 queries, N=256 rows, K=16) into
-//   a double-buffered FP32 accumulator in tensor memory; four epilogue warps
-//   read it with tcgen05.ld (one query per thread) and compute
-//       v = ||x||^2 - 2 q.x   (= approximate distance - ||q||^2).
-//   Each thread keeps a max-heap of the k smallest v seen (shared memory);
-//   R = its root bounds the k-th reference distance from above once shifted
-//   by ||q||^2 + m, so every row with v <= R + 2m may be a true neighbour and
-//   is appended to the query's candidate pool in global memory.  Slices
-//   publish their final R so later CTAs of the same query tile start tight.
-// Pass 2 (select): per query, R* = k-th smallest v among its candidates (a
-//   radix select); rows with v <= R* + 2m are re-ranked with the reference
-//   arithmetic (dif = q - x; acc = fma(dif, dif, acc), bf/fp32.py:80) in FP32
-//   and the k best by (distance, index) are written.  Output distances are
-//   therefore bit-identical to the reference kernels'.
-// Queries whose pool overflows (degenerate data: huge exact-tie groups) are
-// finished by the exact SIMT engine.
+//   rounded to f16 (rows in 256-row blocks sharing one scale), with their FP32
+//   squared norms and a per-query error margin m, a bound on
+//   |approximate distance - reference distance| (derived in tc_prep_q_kernel).
+// Filter passes (one CTA per (128-query tile, slice of a tile set)): TMA
+//   streams f16 row tiles (256 rows x 64 dims, 128-byte swizzle) into a
+//   shared-memory ring; one thread issues tcgen05.mma (M=128 queries, N=256
+//   rows, K=16) into a double-buffered FP32 accumulator in tensor memory; four
+//   epilogue warps read it with tcgen05.ld, one query per thread, and compute
+//       v = ||x||^2 - 2 q.x     (approximate distance - ||q||^2).
+//   Rows with v <= theta_q are appended to the query's candidate region
+//   (plain stores into a per-(query, slice) region: no atomics).
+// Levels: the tile sets grow geometrically: level 0 is a handful of evenly
+//   spaced tiles with theta = +inf; after each level a select pass sets
+//   R_q = k-th smallest v among the level's candidates and the next level uses
+//   theta_q = R_q + 2m.  R_q is the k-th smallest v over a set of real rows, so
+//   ||q||^2 + R_q + m bounds the k-th reference distance from above and no true
+//   neighbour is dropped.  The last level is every tile; the sample levels
+//   cost about 1/ratio of it.
+// Final select: R* = k-th smallest v among the last level's candidates; rows
+//   with v <= R* + 2m are re-ranked with the reference arithmetic
+//   (dif = q - x; acc = fma(dif, dif, acc), bf/fp32.py:80) and the k best by
+//   (distance, index) are written, so output distances are bit-identical to
+//   the reference kernels'.  A query whose final candidate region overflowed
+//   (degenerate data) is finished by the exact SIMT engine.
 #include <cuda.h>
 #include <cudaTypedefs.h>
 
@@ -40,48 +43,47 @@ constexpr int kAChunkBytes = kBM * kBK * 2;   // 16 KB
 constexpr int kBChunkBytes = kBN * kBK * 2;   // 32 KB
 constexpr int kTcThreads = 192;     // warp 0 TMA, warp 1 MMA, warps 2-5 epilogue
 constexpr int kSmemLimit = 232448;  // 227 KB opt-in per block
-constexpr int kMaxKch = 4;          // d <= 256
-constexpr int kTcMaxK = 256;
+constexpr int kMaxKch = 4;          // d <= 256 (query tile resident in shared memory)
+constexpr int kTcMaxK = 512;
 constexpr int kSelThreads = 256;
 constexpr int kSurvCap = 2048;      // exact re-rank capacity per query
-constexpr int kDefaultCandCap = 8192;
-constexpr int kRefreshTiles = 64;   // re-read published thresholds every this many tiles
+constexpr int kDefaultPool = 8192;  // candidate entries per query (all regions of a level)
 
-struct TcArgs {
-  const float *xnorm;     // (x_tiles*256) ||x||^2, NaN past m
-  const float *xinv;      // (x_tiles) 1/scale of each 256-row block
-  const float2 *qinfo;    // (q_tiles*128) (||q||^2, 2*margin); margin NaN for padding rows
-  const float *inv_sq;    // 1/scale of the queries (device scalar)
-  int64_t n, m;
-  int k, q_tiles, slices, tiles_per_slice;
-  int64_t x_tiles;
-  float *rpub;            // (q_tiles, slices, 128) published thresholds
-  int *rflag;             // (q_tiles, slices)
-  uint2 *cand;            // (n, cap) (row, v bits)
-  int *ccount;            // (n)
-  int cap;
+struct FilterArgs {
+  const float *xnorm;    // (x_tiles*256) ||x||^2, NaN past m
+  const float *xinv;     // (x_tiles) 1/scale of each 256-row block
+  const float2 *qinfo;   // (q_tiles*128) (||q||^2, 2*margin); NaN margin for padding rows
+  const float *inv_sq;   // 1/scale of the queries (device scalar)
+  const float *r_in;     // (n) threshold of the previous level, null = +inf
+  int64_t n;
+  int64_t x_tiles;       // tiles of the whole database
+  int64_t level_tiles;   // tiles of this level (evenly spaced over the database)
+  int q_tiles, slices, tiles_per_slice;
+  int region;            // entries per (query, slice) region
+  int pool;              // entries per query
+  int max_slices;        // stride of the count array
+  uint2 *cand;           // (n, pool) (row, v bits)
+  int *ccount;           // (n, max_slices)
   WsHeader *hdr;
 };
 
 // ---------------------------------------------------------------------------
-// smem layout of the filter kernel
+// shared-memory layout of the filter kernel
 // ---------------------------------------------------------------------------
 struct TcLayout {
-  int kch, ns, k;
-  size_t a_off, b_off, heap_off, nx_off, bar_off, total;
+  int kch, ns;
+  size_t a_off, b_off, nx_off, bar_off, total;
 };
-__host__ __device__ inline TcLayout tc_layout(int kch, int k) {
+__host__ __device__ inline TcLayout tc_layout(int kch) {
   TcLayout L{};
   L.kch = kch;
-  L.k = k;
   L.a_off = 0;
   L.b_off = (size_t)kch * kAChunkBytes;
-  const size_t fixed = (size_t)kBM * k * 4 + 2 * kBN * 4 + 256;
+  const size_t fixed = 2 * kBN * 4 + 256;
   size_t ns = ((size_t)kSmemLimit - 1024 - L.b_off - fixed) / kBChunkBytes;
   if (ns > 6) ns = 6;
   L.ns = (int)ns;
-  L.heap_off = L.b_off + (size_t)L.ns * kBChunkBytes;
-  L.nx_off = L.heap_off + (size_t)kBM * k * 4;
+  L.nx_off = L.b_off + (size_t)L.ns * kBChunkBytes;
   L.bar_off = L.nx_off + 2 * kBN * 4;
   L.total = L.bar_off + 256 + 1024;  // + alignment slack
   return L;
@@ -94,62 +96,20 @@ __device__ __forceinline__ void set_error(WsHeader *h, int code, volatile int *a
 
 __device__ __forceinline__ void epi_bar() { asm volatile("bar.sync 1, 128;" ::: "memory"); }
 
-__device__ __forceinline__ int ld_acquire(const int *p) {
-  int v;
-  asm volatile("ld.acquire.gpu.global.b32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
-  return v;
-}
-__device__ __forceinline__ void st_release(int *p, int v) {
-  asm volatile("st.release.gpu.global.b32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
-}
-
-// min over the thresholds other slices of this query tile have published
-__device__ float read_published(const TcArgs &a, int qt, int s, int r) {
-  float best = INFINITY;
-  for (int s2 = 0; s2 < a.slices; s2++) {
-    if (s2 == s) continue;
-    const int slot = qt * a.slices + s2;
-    if (ld_acquire(a.rflag + slot)) best = fminf(best, a.rpub[(size_t)slot * kBM + r]);
-  }
-  return best;
-}
-
-// Rare path of the epilogue: append a candidate row to the query's pool and,
-// when it beats the heap root, replace the root and sift down.  Returns the
-// new root.  Kept out of line so the hot loop keeps its values in registers.
-__device__ __noinline__ float epi_insert(float vi, uint32_t row, float R, int k, float *hp,
-                                         uint2 *cand, int *ccount, int cap) {
-  const int slot = atomicAdd(ccount, 1);
-  if (slot < cap) cand[slot] = make_uint2(row, __float_as_uint(vi));
-  if (!(vi < R)) return R;
-  int p = 0;
-  for (;;) {
-    int c = 2 * p + 1;
-    if (c >= k) break;
-    float hc = hp[c * kBM];
-    if (c + 1 < k) {
-      const float h2 = hp[(c + 1) * kBM];
-      if (h2 > hc) { hc = h2; c++; }
-    }
-    if (hc <= vi) break;
-    hp[p * kBM] = hc;
-    p = c;
-  }
-  hp[p * kBM] = vi;
-  return hp[0];
+__device__ __forceinline__ int64_t level_tile(const FilterArgs &a, int64_t j) {
+  return a.level_tiles == a.x_tiles ? j : (j * a.x_tiles) / a.level_tiles;
 }
 
 __global__ void __launch_bounds__(kTcThreads, 1)
     knn_tc_filter_kernel(const __grid_constant__ CUtensorMap tmap_q,
-                         const __grid_constant__ CUtensorMap tmap_x, const TcArgs a, int kch) {
+                         const __grid_constant__ CUtensorMap tmap_x, const FilterArgs a, int kch) {
   extern __shared__ __align__(1024) unsigned char smem_raw[];
   // align the dynamic smem base to 1024 bytes (swizzle atoms)
   unsigned char *smem = reinterpret_cast<unsigned char *>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
-  const TcLayout L = tc_layout(kch, a.k);
+  const TcLayout L = tc_layout(kch);
   unsigned char *sA = smem + L.a_off;
   unsigned char *sB = smem + L.b_off;
-  float *heap = reinterpret_cast<float *>(smem + L.heap_off);
   float *nxs = reinterpret_cast<float *>(smem + L.nx_off);
   uint64_t *bars = reinterpret_cast<uint64_t *>(smem + L.bar_off);
   uint64_t *full = bars;                 // [ns]
@@ -165,10 +125,10 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int qt = blockIdx.x % a.q_tiles;
   const int s = blockIdx.x / a.q_tiles;
-  const int64_t t_begin = (int64_t)s * a.tiles_per_slice;
-  int64_t t_end = t_begin + a.tiles_per_slice;
-  if (t_end > a.x_tiles) t_end = a.x_tiles;
-  const int ntiles = t_end > t_begin ? (int)(t_end - t_begin) : 0;
+  const int64_t j_begin = (int64_t)s * a.tiles_per_slice;
+  int64_t j_end = j_begin + a.tiles_per_slice;
+  if (j_end > a.level_tiles) j_end = a.level_tiles;
+  const int ntiles = j_end > j_begin ? (int)(j_end - j_begin) : 0;
   const int ns = L.ns;
 
   if (threadIdx.x == 0) {
@@ -203,7 +163,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       uint32_t it = 0;
       bool ok = true;
       for (int lt = 0; lt < ntiles && ok; lt++) {
-        const int32_t row0 = (int32_t)((t_begin + lt) * kBN);
+        const int32_t row0 = (int32_t)(level_tile(a, j_begin + lt) * kBN);
         for (int c = 0; c < kch; c++, it++) {
           const uint32_t st = it % ns, ph = (it / ns) & 1;
           if (!mbar_wait_bounded(empty + st, ph ^ 1, abort_flag)) {
@@ -267,24 +227,18 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     const int tid_e = threadIdx.x - 64;       // 0..127 among epilogue threads
     const int64_t q = (int64_t)qt * kBM + r;
     const bool valid = q < a.n;
-    const float2 qi = a.qinfo[(size_t)qt * kBM + r];
-    const float m2 = qi.y;
-    const int k = a.k;
-    float *hp = heap + r;                     // heap slot i at hp[i * 128]
-    for (int i = 0; i < k; i++) hp[i * kBM] = INFINITY;
-    float R = INFINITY;                        // root of this thread's heap
-    float Rpub = valid ? read_published(a, qt, s, r) : INFINITY;
-    float theta = valid ? __fadd_ru(fminf(R, Rpub), m2) : -INFINITY;
-    int appended = 0;
-    uint2 *cand = a.cand + (size_t)(valid ? q : 0) * a.cap;
-    int *ccount = a.ccount + (valid ? q : 0);
+    const float m2 = a.qinfo[(size_t)qt * kBM + r].y;
+    float theta = -INFINITY;
+    if (valid) theta = a.r_in ? __fadd_ru(a.r_in[q], m2) : INFINITY;
+    uint2 *region = a.cand + (size_t)(valid ? q : 0) * a.pool + (size_t)s * a.region;
+    const int cap = a.region;
+    int cnt = 0;
     const uint32_t lane_base = tmem_base + ((uint32_t)(quarter * 32) << 16);
-
     const float inv_sq = *a.inv_sq;
+
     for (int lt = 0; lt < ntiles; lt++) {
       const int b = lt & 1;
-      const int64_t tile = t_begin + lt;
-      // stage ||x||^2 of the tile's 256 rows (NaN past m)
+      const int64_t tile = level_tile(a, j_begin + lt);
       // Stop decision, uniform across the 128 epilogue threads: one thread snapshots
       // the abort flag before the barrier and all read the snapshot after it.  The
       // snapshot of the next tile is written only after everyone passed the second
@@ -292,14 +246,11 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       if (tid_e == 0) *epi_stop = *abort_flag;
       epi_bar();
       if (*epi_stop) break;
+      // stage ||x||^2 of the tile's 256 rows (NaN past m)
       nxs[b * kBN + tid_e] = a.xnorm[tile * kBN + tid_e];
       nxs[b * kBN + 128 + tid_e] = a.xnorm[tile * kBN + 128 + tid_e];
       const float cscale = -2.0f * inv_sq * a.xinv[tile];  // exact power of two
       epi_bar();
-      if ((lt & (kRefreshTiles - 1)) == kRefreshTiles - 1 && valid) {
-        Rpub = fminf(Rpub, read_published(a, qt, s, r));
-        theta = __fadd_ru(fminf(R, Rpub), m2);
-      }
       // tcgen05.ld is warp-collective: the whole warp proceeds or none of it
       const bool got = __all_sync(0xffffffffu, mbar_wait_bounded(acc_full + b, (lt >> 1) & 1,
                                                                  abort_flag));
@@ -309,7 +260,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       }
       tc_fence_after();
       const float *nxt = nxs + b * kBN;
-      const int32_t row0 = (int32_t)(tile * kBN);
+      const uint32_t row0 = (uint32_t)(tile * kBN);
 #pragma unroll 1
       for (int ch = 0; ch < kBN / 32; ch += 2) {
         uint32_t va[32], vb[32];
@@ -323,33 +274,31 @@ __global__ void __launch_bounds__(kTcThreads, 1)
           if (lane == 0) mbar_arrive(acc_empty + b);
         }
         float v[64];
-        bool any = false;
 #pragma unroll
         for (int i = 0; i < 32; i++) {
           v[i] = __fmaf_rn(__uint_as_float(va[i]), cscale, nxt[ch * 32 + i]);
           v[32 + i] = __fmaf_rn(__uint_as_float(vb[i]), cscale, nxt[ch * 32 + 32 + i]);
         }
+        // min over the 64 values as a tree (NaN loses in fminf)
+        float mn[32];
 #pragma unroll
-        for (int i = 0; i < 64; i++) any |= v[i] <= theta;
-        if (any) {
+        for (int i = 0; i < 32; i++) mn[i] = fminf(v[i], v[32 + i]);
+#pragma unroll
+        for (int w = 16; w >= 1; w >>= 1)
+#pragma unroll
+          for (int i = 0; i < w; i++) mn[i] = fminf(mn[i], mn[i + w]);
+        if (mn[0] <= theta) {
 #pragma unroll
           for (int i = 0; i < 64; i++) {
             if (v[i] <= theta) {
-              appended++;
-              R = epi_insert(v[i], (uint32_t)(row0 + ch * 32 + i), R, k, hp, cand, ccount, a.cap);
-              theta = __fadd_ru(fminf(R, Rpub), m2);
+              if (cnt < cap) region[cnt] = make_uint2(row0 + ch * 32 + i, __float_as_uint(v[i]));
+              cnt++;
             }
           }
         }
       }
     }
-    if (valid) {
-      atomicAdd(&a.hdr->candidates, (unsigned long long)appended);
-      a.rpub[((size_t)qt * a.slices + s) * kBM + r] = fminf(R, Rpub);
-    }
-    __threadfence();
-    epi_bar();
-    if (tid_e == 0) st_release(a.rflag + qt * a.slices + s, 1);
+    if (valid) a.ccount[(size_t)q * a.max_slices + s] = cnt;
   }
 
   tc_fence_before();
@@ -415,8 +364,8 @@ __global__ void __launch_bounds__(256) tc_prep_x_kernel(const float *__restrict_
     const float sc = pow2_scale_for(mx);
     s_scale = sc;
     xinv[tile] = 1.f / sc;
-    // row norms only grow the bound: ordered as unsigned bits since they are >= 0
-    // sqrt of an FP32 sum of d squares: (1 + 2^-10) covers its rounding for d <= 4096
+    // sqrt of an FP32 sum of d squares: (1 + 2^-10) covers its rounding for d <= 4096;
+    // the bound only grows, and non-negative floats order like their bit patterns
     if (isfinite(rn)) atomicMax(&hdr->rx_bits, __float_as_uint(rn * (1.f + 0.0009765625f)));
   }
   __syncthreads();
@@ -426,8 +375,7 @@ __global__ void __launch_bounds__(256) tc_prep_x_kernel(const float *__restrict_
     if (row >= m) break;
     const float *x = X + row * d;
     __half *xh = Xh + row * d_pad;
-    for (int c = lane; c < d_pad; c += 32)
-      xh[c] = __float2half_rn(c < d ? x[c] * sc : 0.f);
+    for (int c = lane; c < d_pad; c += 32) xh[c] = __float2half_rn(c < d ? x[c] * sc : 0.f);
   }
 }
 
@@ -445,8 +393,8 @@ __global__ void tc_qmax_kernel(const float *__restrict__ Q, int64_t count, WsHea
   }
 }
 
-// grid (q_tiles * 128 / 8), block 256: one warp per query row.  Writes the f16
-// query tile rows (zero for padding rows), ||q||^2 and the error margin.
+// grid (q_rows / 8), block 256: one warp per query row.  Writes the f16 query
+// tile rows (zero for padding rows), ||q||^2 and twice the error margin.
 __global__ void __launch_bounds__(256) tc_prep_q_kernel(const float *__restrict__ Q, int64_t n,
                                                         int d, int d_pad, int64_t q_rows,
                                                         __half *__restrict__ Qh,
@@ -476,8 +424,7 @@ __global__ void __launch_bounds__(256) tc_prep_q_kernel(const float *__restrict_
   for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
   if (lane == 0) {
     if (!isfinite(ss)) atomicOr(&hdr->nonfinite, 1);
-    // Error margin (see the header comment of this file): with u = 2^-11 the
-    // f16 unit roundoff, qn >= ||q||, Rx >= max ||x||,
+    // Error margin.  With u = 2^-11 the f16 unit roundoff, qn >= ||q||, Rx >= max ||x||:
     //   e_q = u qn + sqrt(d) 2^-25 / s_q        (f16 rounding of q, incl. subnormals)
     //   e_x = (u + sqrt(d) 2^-38) Rx             (rows scaled to [2^13, 2^14) per block)
     //   dot rounding  <= e_q Rx + qn e_x + e_q e_x
@@ -485,6 +432,8 @@ __global__ void __launch_bounds__(256) tc_prep_q_kernel(const float *__restrict_
     //   FP32 terms    <= 2 (d + 8) 2^-24 (qn + Rx)^2  (norms, the fused epilogue step,
     //                                                  and the reference's own rounding)
     //   margin = 2 (dot rounding + accumulation) + FP32 terms;  stored: 2 * margin.
+    // Then |(||q||^2 + v) - D| <= margin for every row, v the epilogue value and D
+    // the reference kernel's FP32 distance.
     const double u = 1.0 / 2048.0;
     const double qn = sqrt((double)ss) * (1.0 + ldexp(1.0, -10));
     const double rx = (double)__uint_as_float(hdr->rx_bits);
@@ -500,7 +449,7 @@ __global__ void __launch_bounds__(256) tc_prep_q_kernel(const float *__restrict_
 }
 
 // ---------------------------------------------------------------------------
-// select + exact re-rank: one block per query
+// selection helpers
 // ---------------------------------------------------------------------------
 __device__ void bitonic_sort_u64(uint64_t *keys, int P) {
   for (int size = 2; size <= P; size <<= 1) {
@@ -518,11 +467,87 @@ __device__ void bitonic_sort_u64(uint64_t *keys, int P) {
   __syncthreads();
 }
 
+// Gather a query's candidates of one level into shared memory (compacted).
+// Returns the number gathered; *s_over is set when a region lost entries.
+__device__ int gather_level(const uint2 *cand, const int *ccount, int64_t q, int pool, int region,
+                            int slices, int max_slices, uint2 *out, int *s_total, int *s_over) {
+  if (threadIdx.x == 0) { *s_total = 0; *s_over = 0; }
+  __syncthreads();
+  for (int sl = 0; sl < slices; sl++) {
+    int c = ccount[(size_t)q * max_slices + sl];
+    if (c > region) {
+      if (threadIdx.x == 0) *s_over = 1;
+      c = region;
+    }
+    const int base = *s_total;
+    const uint2 *src = cand + (size_t)q * pool + (size_t)sl * region;
+    for (int e = threadIdx.x; e < c; e += blockDim.x) out[base + e] = src[e];
+    __syncthreads();
+    if (threadIdx.x == 0) *s_total = base + c;
+    __syncthreads();
+  }
+  return *s_total;
+}
+
+// k-th smallest v (as float) among cnt entries, by radix select on order keys.
+__device__ float block_kth(const uint2 *cs, int cnt, int k, int *hist, uint32_t *s_prefix,
+                           int *s_rank) {
+  if (threadIdx.x == 0) { *s_prefix = 0u; *s_rank = k; }
+  uint32_t mask = 0u;
+  for (int shift = 24; shift >= 0; shift -= 8) {
+    for (int b = threadIdx.x; b < 256; b += blockDim.x) hist[b] = 0;
+    __syncthreads();
+    const uint32_t prefix = *s_prefix;
+    for (int e = threadIdx.x; e < cnt; e += blockDim.x) {
+      const uint32_t key = f2ord(__uint_as_float(cs[e].y));
+      if ((key & mask) == prefix) atomicAdd(&hist[(key >> shift) & 255], 1);
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      int need = *s_rank, b = 0;
+      for (; b < 255; b++) {
+        if (hist[b] >= need) break;
+        need -= hist[b];
+      }
+      *s_rank = need;
+      *s_prefix = prefix | ((uint32_t)b << shift);
+    }
+    __syncthreads();
+    mask |= 255u << shift;
+  }
+  return ord2f(*s_prefix);
+}
+
+struct LevelSelArgs {
+  const uint2 *cand;
+  const int *ccount;
+  int64_t n;
+  int k, pool, region, slices, max_slices;
+  float *r_out;  // (n) k-th smallest v of the level, +inf when fewer than k
+};
+
+// one block per query: R_q for the next level
+__global__ void __launch_bounds__(kSelThreads) tc_level_select_kernel(const LevelSelArgs a) {
+  extern __shared__ __align__(1024) unsigned char smem_raw[];
+  uint2 *cs = reinterpret_cast<uint2 *>(smem_raw);
+  __shared__ int hist[256];
+  __shared__ int s_total, s_over, s_rank;
+  __shared__ uint32_t s_prefix;
+  const int64_t q = blockIdx.x;
+  const int cnt = gather_level(a.cand, a.ccount, q, a.pool, a.region, a.slices, a.max_slices, cs,
+                               &s_total, &s_over);
+  // entries lost to a full region only make R larger than it could be: still a
+  // valid bound, since R is the k-th smallest over real rows that were kept
+  float R = INFINITY;
+  if (cnt >= a.k) R = block_kth(cs, cnt, a.k, hist, &s_prefix, &s_rank);
+  if (threadIdx.x == 0) a.r_out[q] = R;
+}
+
 struct SelArgs {
   const float *Q;
   const float *X;
   int64_t n, m;
-  int d, k, cap;
+  int d, k, pool, region, slices, max_slices;
   int64_t id_offset;
   const float2 *qinfo;
   const uint2 *cand;
@@ -533,56 +558,32 @@ struct SelArgs {
   int32_t *out_i;
 };
 
-// dynamic smem: cap * 8 (candidates) + kSurvCap * 8 (survivor keys) + d * 4 (query)
-__global__ void __launch_bounds__(kSelThreads) tc_select_kernel(const SelArgs a) {
+// dynamic smem: pool * 8 (candidates) + kSurvCap * 8 (survivor keys) + d * 4 (query)
+__global__ void __launch_bounds__(kSelThreads) tc_final_select_kernel(const SelArgs a) {
   extern __shared__ __align__(1024) unsigned char smem_raw[];
   uint2 *cs = reinterpret_cast<uint2 *>(smem_raw);
-  uint64_t *keys = reinterpret_cast<uint64_t *>(cs + a.cap);
+  uint64_t *keys = reinterpret_cast<uint64_t *>(cs + a.pool);
   float *qs = reinterpret_cast<float *>(keys + kSurvCap);
   __shared__ int hist[256];
-  __shared__ int s_nsurv, s_sel_rank;
+  __shared__ int s_total, s_over, s_rank, s_nsurv;
   __shared__ uint32_t s_prefix;
   const int64_t q = blockIdx.x;
-  const int cnt = a.ccount[q];
-  // overflowed pool, or non-finite inputs (the margin argument needs finite norms)
-  if (cnt > a.cap || a.hdr->nonfinite) {
+  const int cnt = gather_level(a.cand, a.ccount, q, a.pool, a.region, a.slices, a.max_slices, cs,
+                               &s_total, &s_over);
+  // a region that lost entries, or non-finite inputs (the margin needs finite norms)
+  if (s_over || a.hdr->nonfinite) {
     if (threadIdx.x == 0) {
       const int slot = atomicAdd(&a.hdr->fallback, 1);
       a.fb_list[slot] = (int)q;
     }
     return;
   }
-  for (int e = threadIdx.x; e < cnt; e += blockDim.x) cs[e] = a.cand[(size_t)q * a.cap + e];
   for (int c = threadIdx.x; c < a.d; c += blockDim.x) qs[c] = a.Q[q * a.d + c];
-  if (threadIdx.x == 0) { s_nsurv = 0; s_prefix = 0u; s_sel_rank = a.k; }
-  __syncthreads();
-  // R* = k-th smallest v (radix select over order-preserving keys)
+  if (threadIdx.x == 0) s_nsurv = 0;
   float theta = INFINITY;
-  if (cnt >= a.k) {
-    uint32_t mask = 0u;
-    for (int shift = 24; shift >= 0; shift -= 8) {
-      for (int b = threadIdx.x; b < 256; b += blockDim.x) hist[b] = 0;
-      __syncthreads();
-      const uint32_t prefix = s_prefix;
-      for (int e = threadIdx.x; e < cnt; e += blockDim.x) {
-        const uint32_t key = f2ord(__uint_as_float(cs[e].y));
-        if ((key & mask) == prefix) atomicAdd(&hist[(key >> shift) & 255], 1);
-      }
-      __syncthreads();
-      if (threadIdx.x == 0) {
-        int need = s_sel_rank, b = 0;
-        for (; b < 255; b++) {
-          if (hist[b] >= need) break;
-          need -= hist[b];
-        }
-        s_sel_rank = need;
-        s_prefix = prefix | ((uint32_t)b << shift);
-      }
-      __syncthreads();
-      mask |= 255u << shift;
-    }
-    theta = __fadd_ru(ord2f(s_prefix), a.qinfo[q].y);
-  }
+  if (cnt >= a.k) theta = __fadd_ru(block_kth(cs, cnt, a.k, hist, &s_prefix, &s_rank),
+                                    a.qinfo[q].y);
+  __syncthreads();
   // survivors -> exact distance with the reference arithmetic
   for (int e = threadIdx.x; e < cnt; e += blockDim.x) {
     const float v = __uint_as_float(cs[e].y);
@@ -606,8 +607,8 @@ __global__ void __launch_bounds__(kSelThreads) tc_select_kernel(const SelArgs a)
     }
     return;
   }
-  int P = 1;
-  while (P < ns || P < 2) P <<= 1;
+  int P = 2;
+  while (P < ns) P <<= 1;
   for (int e = ns + threadIdx.x; e < P; e += blockDim.x) keys[e] = ~0ull;
   bitonic_sort_u64(keys, P);
   for (int j = threadIdx.x; j < a.k; j += blockDim.x) {
@@ -618,6 +619,7 @@ __global__ void __launch_bounds__(kSelThreads) tc_select_kernel(const SelArgs a)
   }
   if (threadIdx.x == 0) {
     atomicAdd(&a.hdr->survivors, (unsigned long long)ns);
+    atomicAdd(&a.hdr->candidates, (unsigned long long)cnt);
     atomicMax(&a.hdr->max_cand, cnt);
   }
 }
@@ -649,11 +651,11 @@ static int kch_for(int d) { return (d + kBK - 1) / kBK; }
 
 bool tc_supported(int d, int k) {
   if (d <= 0 || d > kMaxKch * kBK || k <= 0 || k > kTcMaxK) return false;
-  const TcLayout L = tc_layout(kch_for(d), k);
+  const TcLayout L = tc_layout(kch_for(d));
   return L.ns >= 2 && L.total <= (size_t)kSmemLimit;
 }
 
-size_t tc_smem_bytes(int d, int k) { return tc_layout(kch_for(d), k).total; }
+size_t tc_smem_bytes(int d, int) { return tc_layout(kch_for(d)).total; }
 
 const void *tc_kernel_ptr(int, int) { return (const void *)knn_tc_filter_kernel; }
 
@@ -663,7 +665,26 @@ static int num_sms() {
   return sms > 0 ? sms : 148;
 }
 
-bool tc_make_plan(int64_t n, int64_t m, int d, int k, int slices, int cand_cap, TcPlan *p) {
+// slices for a level of `tiles` tiles: whole waves of CTAs, at most `max_s`
+static int choose_slices(int q_tiles, int64_t tiles, int sms, int max_s) {
+  int best = 1;
+  double best_eff = -1.0;
+  for (int s = 1; s <= max_s && s <= tiles; s++) {
+    const int64_t ctas = (int64_t)q_tiles * s;
+    const int64_t tps = (tiles + s - 1) / s;
+    const int64_t used = (tiles + tps - 1) / tps;  // slices that get tiles
+    if (used != s) continue;
+    const int64_t waves = (ctas + sms - 1) / sms;
+    const double eff = (double)ctas / (double)(waves * sms);
+    // prefer fuller waves; among similar, fewer slices (larger regions)
+    if (eff > best_eff + 0.03) { best_eff = eff; best = s; }
+    if (waves >= 4 && eff > 0.9) break;
+    if (tps < 8) break;
+  }
+  return best;
+}
+
+bool tc_make_plan(int64_t n, int64_t m, int d, int k, int slices, int pool, TcPlan *p) {
   if (!tc_supported(d, k) || n <= 0 || m <= 0) return false;
   TcPlan P{};
   P.n = n;
@@ -673,30 +694,40 @@ bool tc_make_plan(int64_t n, int64_t m, int d, int k, int slices, int cand_cap, 
   P.d_pad = kch_for(d) * kBK;
   P.q_tiles = (int)((n + kBM - 1) / kBM);
   P.x_tiles = (m + kBN - 1) / kBN;
-  if (slices <= 0) {
-    // fill the SMs with whole waves: pick the slice count whose last wave is fullest,
-    // with slices no shorter than 64 tiles where possible
-    const int sms = num_sms();
-    const int64_t max_s = P.x_tiles;
-    int best = 1;
-    double best_eff = -1.0;
-    for (int s = 1; s <= 512 && s <= max_s; s++) {
-      const int64_t ctas = (int64_t)P.q_tiles * s;
-      const int64_t tps = (P.x_tiles + s - 1) / s;
-      if (s > 1 && tps < 64 && ctas > sms) break;
-      const int64_t waves = (ctas + sms - 1) / sms;
-      const double eff = (double)ctas / (double)(waves * sms);
-      if (eff > best_eff + 0.02) { best_eff = eff; best = s; }
-      if (eff > 0.97) break;
-    }
-    slices = best;
-  }
-  if (slices > P.x_tiles) slices = (int)P.x_tiles;
-  P.tiles_per_slice = (P.x_tiles + slices - 1) / slices;
-  P.slices = (int)((P.x_tiles + P.tiles_per_slice - 1) / P.tiles_per_slice);
-  P.cand_cap = cand_cap > 0 ? cand_cap : kDefaultCandCap;
-  if (P.cand_cap < k) P.cand_cap = k;
+  P.cand_cap = pool > 0 ? pool : kDefaultPool;
+  if (P.cand_cap < 2 * k) P.cand_cap = 2 * k;
   if ((size_t)P.cand_cap * 8 + kSurvCap * 8 + (size_t)d * 4 > (size_t)kSmemLimit - 4096) return false;
+  // level sizes: each level's expected candidates ~ target = pool / 2
+  const int64_t target = P.cand_cap / 2;
+  int64_t ratio = target / k;
+  if (ratio < 4) ratio = 4;
+  int64_t sizes[kMaxLevels];
+  int nl = 0;
+  sizes[nl++] = P.x_tiles;
+  while (nl < kMaxLevels && sizes[nl - 1] * kBN > target) {
+    int64_t prev = (sizes[nl - 1] + ratio - 1) / ratio;
+    if (prev * kBN < 2 * k) prev = (2 * k + kBN - 1) / kBN;  // the base needs >= k rows
+    if (prev >= sizes[nl - 1]) break;
+    sizes[nl++] = prev;
+  }
+  P.levels = nl;
+  const int sms = num_sms();
+  int max_s = 1;
+  for (int l = 0; l < nl; l++) {
+    LevelPlan &lv = P.level[l];
+    lv.tiles = sizes[nl - 1 - l];
+    const bool last = l == nl - 1;
+    int s = (last && slices > 0) ? slices : choose_slices(P.q_tiles, lv.tiles, sms, 64);
+    if (s > lv.tiles) s = (int)lv.tiles;
+    if (s < 1) s = 1;
+    lv.tiles_per_slice = (lv.tiles + s - 1) / s;
+    lv.slices = (int)((lv.tiles + lv.tiles_per_slice - 1) / lv.tiles_per_slice);
+    lv.region = P.cand_cap / lv.slices;
+    if (lv.slices > max_s) max_s = lv.slices;
+  }
+  P.max_slices = max_s;
+  P.slices = P.level[nl - 1].slices;
+  P.tiles_per_slice = P.level[nl - 1].tiles_per_slice;
   // fallback: the SIMT engine over up to n queries in slices
   P.fb_slices = (int)((m + 262143) / 262144);
   if (P.fb_slices > 32) P.fb_slices = 32;
@@ -708,10 +739,9 @@ bool tc_make_plan(int64_t n, int64_t m, int d, int k, int slices, int cand_cap, 
   P.off_xscale = off;   off = al256(off + (size_t)P.x_tiles * 4 + 16);
   P.off_qh = off;       off = al256(off + (size_t)q_rows * P.d_pad * 2);
   P.off_qinfo = off;    off = al256(off + (size_t)q_rows * 8);
-  P.off_rpub = off;     off = al256(off + (size_t)P.q_tiles * P.slices * kBM * 4);
-  P.off_rflag = off;    off = al256(off + (size_t)P.q_tiles * P.slices * 4);
+  P.off_rlev = off;     off = al256(off + (size_t)n * 4);
   P.off_cand = off;     off = al256(off + (size_t)n * P.cand_cap * 8);
-  P.off_ccount = off;   off = al256(off + (size_t)n * 4);
+  P.off_ccount = off;   off = al256(off + (size_t)n * max_s * 4);
   P.off_flags = off;    off = al256(off + (size_t)n * 4);
   P.off_fbq = off;      off = al256(off + (size_t)n * d * 4);
   P.off_fbd = off;      off = al256(off + (size_t)n * k * 4);
@@ -762,8 +792,7 @@ int tc_run(const float *Q, const float *X, int64_t id_offset, float *out_d, int3
   float *inv_sq = xinv + p.x_tiles;  // one float after the block scales
   __half *Qh = reinterpret_cast<__half *>(ws + p.off_qh);
   float2 *qinfo = reinterpret_cast<float2 *>(ws + p.off_qinfo);
-  float *rpub = reinterpret_cast<float *>(ws + p.off_rpub);
-  int *rflag = reinterpret_cast<int *>(ws + p.off_rflag);
+  float *rlev = reinterpret_cast<float *>(ws + p.off_rlev);
   uint2 *cand = reinterpret_cast<uint2 *>(ws + p.off_cand);
   int *ccount = reinterpret_cast<int *>(ws + p.off_ccount);
   int *fb_list = reinterpret_cast<int *>(ws + p.off_flags);
@@ -776,8 +805,6 @@ int tc_run(const float *Q, const float *X, int64_t id_offset, float *out_d, int3
   } while (0)
 
   BFK_TRY(cudaMemsetAsync(hdr, 0, sizeof(WsHeader), stream));
-  BFK_TRY(cudaMemsetAsync(rflag, 0, (size_t)p.q_tiles * p.slices * 4, stream));
-  BFK_TRY(cudaMemsetAsync(ccount, 0, (size_t)p.n * 4, stream));
   // pass 0: prep
   tc_qmax_kernel<<<592, 256, 0, stream>>>(Q, p.n * p.d, hdr);
   tc_prep_x_kernel<<<(unsigned)p.x_tiles, 256, 0, stream>>>(X, p.m, p.d, p.d_pad, Xh, xnorm, xinv, hdr);
@@ -786,40 +813,62 @@ int tc_run(const float *Q, const float *X, int64_t id_offset, float *out_d, int3
   nl += 3;
   BFK_TRY(cudaGetLastError());
 
-  // pass 1: filter
   CUtensorMap tq, tx;
   if (!make_tmap(&tq, Qh, q_rows, p.d_pad, kBM)) return 1;
   if (!make_tmap(&tx, Xh, p.m, p.d_pad, kBN)) return 1;
-  TcArgs A{};
+  const int kch = p.d_pad / kBK;
+  const size_t smem = tc_smem_bytes(p.d, p.k);
+  BFK_TRY(cudaFuncSetAttribute((const void *)knn_tc_filter_kernel,
+                               cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+  const size_t lsmem = (size_t)p.cand_cap * 8;
+  BFK_TRY(cudaFuncSetAttribute((const void *)tc_level_select_kernel,
+                               cudaFuncAttributeMaxDynamicSharedMemorySize, (int)lsmem));
+  FilterArgs A{};
   A.xnorm = xnorm;
   A.xinv = xinv;
   A.qinfo = qinfo;
   A.inv_sq = inv_sq;
   A.n = p.n;
-  A.m = p.m;
-  A.k = p.k;
-  A.q_tiles = p.q_tiles;
-  A.slices = p.slices;
-  A.tiles_per_slice = (int)p.tiles_per_slice;
   A.x_tiles = p.x_tiles;
-  A.rpub = rpub;
-  A.rflag = rflag;
+  A.q_tiles = p.q_tiles;
+  A.pool = p.cand_cap;
+  A.max_slices = p.max_slices;
   A.cand = cand;
   A.ccount = ccount;
-  A.cap = p.cand_cap;
   A.hdr = hdr;
-  const int kch = p.d_pad / kBK;
-  const size_t smem = tc_smem_bytes(p.d, p.k);
-  BFK_TRY(cudaFuncSetAttribute((const void *)knn_tc_filter_kernel,
-                               cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
-  if (t0) cudaEventRecord(t0, stream);
-  knn_tc_filter_kernel<<<(unsigned)(p.q_tiles * p.slices), kTcThreads, smem, stream>>>(tq, tx, A,
-                                                                                       kch);
-  if (t1) cudaEventRecord(t1, stream);
-  nl++;
-  BFK_TRY(cudaGetLastError());
+  for (int l = 0; l < p.levels; l++) {
+    const LevelPlan &lv = p.level[l];
+    const bool last = l == p.levels - 1;
+    A.r_in = l == 0 ? nullptr : rlev;
+    A.level_tiles = lv.tiles;
+    A.slices = lv.slices;
+    A.tiles_per_slice = (int)lv.tiles_per_slice;
+    A.region = lv.region;
+    if (last && t0) cudaEventRecord(t0, stream);
+    knn_tc_filter_kernel<<<(unsigned)(p.q_tiles * lv.slices), kTcThreads, smem, stream>>>(tq, tx,
+                                                                                          A, kch);
+    if (last && t1) cudaEventRecord(t1, stream);
+    nl++;
+    BFK_TRY(cudaGetLastError());
+    if (!last) {
+      LevelSelArgs S{};
+      S.cand = cand;
+      S.ccount = ccount;
+      S.n = p.n;
+      S.k = p.k;
+      S.pool = p.cand_cap;
+      S.region = lv.region;
+      S.slices = lv.slices;
+      S.max_slices = p.max_slices;
+      S.r_out = rlev;
+      tc_level_select_kernel<<<(unsigned)p.n, kSelThreads, lsmem, stream>>>(S);
+      nl++;
+      BFK_TRY(cudaGetLastError());
+    }
+  }
 
-  // pass 2: select + exact re-rank
+  // final select + exact re-rank
+  const LevelPlan &lv = p.level[p.levels - 1];
   SelArgs S{};
   S.Q = Q;
   S.X = X;
@@ -827,7 +876,10 @@ int tc_run(const float *Q, const float *X, int64_t id_offset, float *out_d, int3
   S.m = p.m;
   S.d = p.d;
   S.k = p.k;
-  S.cap = p.cand_cap;
+  S.pool = p.cand_cap;
+  S.region = lv.region;
+  S.slices = lv.slices;
+  S.max_slices = p.max_slices;
   S.id_offset = id_offset;
   S.qinfo = qinfo;
   S.cand = cand;
@@ -837,13 +889,13 @@ int tc_run(const float *Q, const float *X, int64_t id_offset, float *out_d, int3
   S.out_d = out_d;
   S.out_i = out_i;
   const size_t ssmem = (size_t)p.cand_cap * 8 + kSurvCap * 8 + (size_t)p.d * 4;
-  BFK_TRY(cudaFuncSetAttribute((const void *)tc_select_kernel,
+  BFK_TRY(cudaFuncSetAttribute((const void *)tc_final_select_kernel,
                                cudaFuncAttributeMaxDynamicSharedMemorySize, (int)ssmem));
-  tc_select_kernel<<<(unsigned)p.n, kSelThreads, ssmem, stream>>>(S);
+  tc_final_select_kernel<<<(unsigned)p.n, kSelThreads, ssmem, stream>>>(S);
   nl++;
   BFK_TRY(cudaGetLastError());
 
-  // queries the filter could not finish (pool overflow) -> exact SIMT engine
+  // queries the filter could not finish -> exact SIMT engine
   int32_t h_fb = 0, h_err = 0;
   BFK_TRY(cudaMemcpyAsync(&h_fb, &hdr->fallback, 4, cudaMemcpyDeviceToHost, stream));
   BFK_TRY(cudaMemcpyAsync(&h_err, &hdr->error, 4, cudaMemcpyDeviceToHost, stream));
