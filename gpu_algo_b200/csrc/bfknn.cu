@@ -243,7 +243,7 @@ bfk_status_t bfk_kernel_attrs(int32_t engine, int32_t d, int32_t k, bfk_attrs_t 
   if (engine == BFK_ENGINE_TC_F16) {
     if (!tc_supported(d, k)) return BFK_ERR_UNSUPPORTED;
     fn = tc_kernel_ptr(d, k);
-    threads = 192;
+    threads = 320;
     dyn = tc_smem_bytes(d, k);
   } else if (engine == BFK_ENGINE_DIRECT || engine == BFK_ENGINE_AUTO) {
     const int tq = k <= 512 ? 4 : 1;

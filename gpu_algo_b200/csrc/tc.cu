@@ -29,6 +29,7 @@
 #include <cuda.h>
 #include <cudaTypedefs.h>
 
+#include <cfloat>
 #include <cmath>
 
 #include "common.cuh"
@@ -41,7 +42,9 @@ constexpr int kBN = 256;            // rows per tile (MMA N, accumulator columns
 constexpr int kBK = 64;             // f16 elements per K chunk (128 bytes, one swizzle atom row)
 constexpr int kAChunkBytes = kBM * kBK * 2;   // 16 KB
 constexpr int kBChunkBytes = kBN * kBK * 2;   // 32 KB
-constexpr int kTcThreads = 192;     // warp 0 TMA, warp 1 MMA, warps 2-5 epilogue
+constexpr int kTcThreads = 320;     // warp 0 TMA, warp 1 MMA, warps 2-9 epilogue
+constexpr int kEpiWarps = 8;        // two warps per TMEM lane quarter: one per column half
+constexpr int kHalfN = kBN / 2;     // accumulator columns an epilogue warp reads per tile
 constexpr int kSmemLimit = 232448;  // 227 KB opt-in per block
 constexpr int kMaxKch = 4;          // d <= 256 (query tile resident in shared memory)
 constexpr int kTcMaxK = 512;
@@ -50,7 +53,7 @@ constexpr int kSurvCap = 2048;      // exact re-rank capacity per query
 constexpr int kDefaultPool = 8192;  // candidate entries per query (all regions of a level)
 
 struct FilterArgs {
-  const float *xnorm;    // (x_tiles*256) ||x||^2, NaN past m
+  const float *xnorm;    // (x_tiles*256) ||x||^2, +inf past m
   const float *xinv;     // (x_tiles) 1/scale of each 256-row block
   const float2 *qinfo;   // (q_tiles*128) (||q||^2, 2*margin); NaN margin for padding rows
   const float *inv_sq;   // 1/scale of the queries (device scalar)
@@ -59,11 +62,11 @@ struct FilterArgs {
   int64_t x_tiles;       // tiles of the whole database
   int64_t level_tiles;   // tiles of this level (evenly spaced over the database)
   int q_tiles, slices, tiles_per_slice;
-  int region;            // entries per (query, slice) region
+  int region;            // entries per (query, slice, column half) region
   int pool;              // entries per query
-  int max_slices;        // stride of the count array
+  int max_slices;        // count array stride / 2 (two column halves per slice)
   uint2 *cand;           // (n, pool) (row, v bits)
-  int *ccount;           // (n, max_slices)
+  int *ccount;           // (n, 2 * max_slices)
   WsHeader *hdr;
 };
 
@@ -79,12 +82,12 @@ __host__ __device__ inline TcLayout tc_layout(int kch) {
   L.kch = kch;
   L.a_off = 0;
   L.b_off = (size_t)kch * kAChunkBytes;
-  const size_t fixed = 2 * kBN * 4 + 256;
+  const size_t fixed = (size_t)kEpiWarps * 2 * kHalfN * 4 + 256;
   size_t ns = ((size_t)kSmemLimit - 1024 - L.b_off - fixed) / kBChunkBytes;
   if (ns > 6) ns = 6;
   L.ns = (int)ns;
   L.nx_off = L.b_off + (size_t)L.ns * kBChunkBytes;
-  L.bar_off = L.nx_off + 2 * kBN * 4;
+  L.bar_off = L.nx_off + (size_t)kEpiWarps * 2 * kHalfN * 4;
   L.total = L.bar_off + 256 + 1024;  // + alignment slack
   return L;
 }
@@ -94,7 +97,23 @@ __device__ __forceinline__ void set_error(WsHeader *h, int code, volatile int *a
   *abort_flag = 1;
 }
 
-__device__ __forceinline__ void epi_bar() { asm volatile("bar.sync 1, 128;" ::: "memory"); }
+
+// (a0, a1) * c + (b0, b1) in one packed FP32 instruction (round to nearest)
+__device__ __forceinline__ void fma2(float a0, float a1, float c, float b0, float b1, float &d0,
+                                     float &d1) {
+  unsigned long long pa, pc, pb, pd;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(pa) : "f"(a0), "f"(a1));
+  asm("mov.b64 %0, {%1, %1};" : "=l"(pc) : "f"(c));
+  asm("mov.b64 %0, {%1, %2};" : "=l"(pb) : "f"(b0), "f"(b1));
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(pd) : "l"(pa), "l"(pc), "l"(pb));
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(d0), "=f"(d1) : "l"(pd));
+}
+// three-input minimum (NaN inputs are ignored, as by fminf)
+__device__ __forceinline__ float min3f(float a, float b, float c) {
+  float d;
+  asm("min.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
+  return d;
+}
 
 __device__ __forceinline__ int64_t level_tile(const FilterArgs &a, int64_t j) {
   return a.level_tiles == a.x_tiles ? j : (j * a.x_tiles) / a.level_tiles;
@@ -136,8 +155,8 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     mbar_init(a_full, 1);
     mbar_init(acc_full, 1);
     mbar_init(acc_full + 1, 1);
-    mbar_init(acc_empty, 4);
-    mbar_init(acc_empty + 1, 4);
+    mbar_init(acc_empty, kEpiWarps);
+    mbar_init(acc_empty + 1, kEpiWarps);
     mbar_init(drain, 1);
     *abort_flag = 0;
     *epi_stop = 0;
@@ -221,84 +240,107 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       mbar_wait_bounded(drain, 0, abort_flag);
     }
   } else {
-    // ---------------- epilogue: one query per thread ----------------
-    const int quarter = warp & 3;             // TMEM lanes this warp may access
+    // ---------------- epilogue: one query per thread, half the columns per warp ----------------
+    const int e = warp - 2;                   // 0..7
+    const int quarter = warp & 3;             // TMEM lanes this warp may access (warp % 4)
+    const int half = e >> 2;                  // columns [half*128, half*128 + 128) of each tile
     const int r = quarter * 32 + lane;        // query row within the tile
-    const int tid_e = threadIdx.x - 64;       // 0..127 among epilogue threads
     const int64_t q = (int64_t)qt * kBM + r;
     const bool valid = q < a.n;
     const float m2 = a.qinfo[(size_t)qt * kBM + r].y;
+    // rows past m carry ||x||^2 = +inf, so theta stays finite: FLT_MAX when there is no bound yet
     float theta = -INFINITY;
-    if (valid) theta = a.r_in ? __fadd_ru(a.r_in[q], m2) : INFINITY;
-    uint2 *region = a.cand + (size_t)(valid ? q : 0) * a.pool + (size_t)s * a.region;
+    if (valid) theta = a.r_in ? fminf(__fadd_ru(a.r_in[q], m2), FLT_MAX) : FLT_MAX;
+    uint2 *region = a.cand + (size_t)(valid ? q : 0) * a.pool +
+                    (size_t)(2 * s + half) * a.region;
     const int cap = a.region;
     int cnt = 0;
-    const uint32_t lane_base = tmem_base + ((uint32_t)(quarter * 32) << 16);
+    const uint32_t lane_base = tmem_base + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(half * kHalfN);
     const float inv_sq = *a.inv_sq;
+    float *nxw = nxs + e * 2 * kHalfN;        // this warp's ||x||^2 staging, two buffers
+    // prefetch ||x||^2 (4 rows per lane) and the block scale of the first tile
+    float4 pre_nx = make_float4(0.f, 0.f, 0.f, 0.f);
+    float pre_inv = 1.f;
+    if (ntiles > 0) {
+      const int64_t t0 = level_tile(a, j_begin);
+      pre_nx = *reinterpret_cast<const float4 *>(a.xnorm + t0 * kBN + half * kHalfN + lane * 4);
+      pre_inv = a.xinv[t0];
+    }
 
     for (int lt = 0; lt < ntiles; lt++) {
       const int b = lt & 1;
       const int64_t tile = level_tile(a, j_begin + lt);
-      // Stop decision, uniform across the 128 epilogue threads: one thread snapshots
-      // the abort flag before the barrier and all read the snapshot after it.  The
-      // snapshot of the next tile is written only after everyone passed the second
-      // barrier of this tile, so no thread can see two different values.
-      if (tid_e == 0) *epi_stop = *abort_flag;
-      epi_bar();
-      if (*epi_stop) break;
-      // stage ||x||^2 of the tile's 256 rows (NaN past m)
-      nxs[b * kBN + tid_e] = a.xnorm[tile * kBN + tid_e];
-      nxs[b * kBN + 128 + tid_e] = a.xnorm[tile * kBN + 128 + tid_e];
-      const float cscale = -2.0f * inv_sq * a.xinv[tile];  // exact power of two
-      epi_bar();
+      // any role that gave up ends this warp's loop too (warp-uniform decision)
+      if (__any_sync(0xffffffffu, *abort_flag != 0)) break;
+      float *nxt = nxw + b * kHalfN;
+      *reinterpret_cast<float4 *>(nxt + lane * 4) = pre_nx;
+      const float cscale = -2.0f * inv_sq * pre_inv;  // exact power of two
+      __syncwarp();
+      if (lt + 1 < ntiles) {
+        const int64_t tn = level_tile(a, j_begin + lt + 1);
+        pre_nx = *reinterpret_cast<const float4 *>(a.xnorm + tn * kBN + half * kHalfN + lane * 4);
+        pre_inv = a.xinv[tn];
+      }
       // tcgen05.ld is warp-collective: the whole warp proceeds or none of it
       const bool got = __all_sync(0xffffffffu, mbar_wait_bounded(acc_full + b, (lt >> 1) & 1,
                                                                  abort_flag));
       if (!got) {
         set_error(a.hdr, ERR_TIMEOUT_EPILOGUE, abort_flag);
-        continue;  // reach the next barrier, where every epilogue thread stops
+        break;
       }
       tc_fence_after();
-      const float *nxt = nxs + b * kBN;
-      const uint32_t row0 = (uint32_t)(tile * kBN);
+      const uint32_t row0 = (uint32_t)(tile * kBN + half * kHalfN);
 #pragma unroll 1
-      for (int ch = 0; ch < kBN / 32; ch += 2) {
+      for (int ch = 0; ch < kHalfN; ch += 64) {
         uint32_t va[32], vb[32];
-        tmem_ld_32x32b_x32(lane_base + (uint32_t)(b * kBN + ch * 32), va);
-        tmem_ld_32x32b_x32(lane_base + (uint32_t)(b * kBN + ch * 32 + 32), vb);
+        tmem_ld_32x32b_x32(lane_base + (uint32_t)(b * kBN + ch), va);
+        tmem_ld_32x32b_x32(lane_base + (uint32_t)(b * kBN + ch + 32), vb);
         tmem_ld_wait();
-        if (ch == kBN / 32 - 2) {
+        if (ch + 64 == kHalfN) {
           // the accumulator is in registers: hand the buffer back to the MMA warp
           tc_fence_before();
           __syncwarp();
           if (lane == 0) mbar_arrive(acc_empty + b);
         }
+        // v = acc * cscale + ||x||^2, two columns per packed FMA
         float v[64];
+        const float4 *nx4 = reinterpret_cast<const float4 *>(nxt + ch);
 #pragma unroll
-        for (int i = 0; i < 32; i++) {
-          v[i] = __fmaf_rn(__uint_as_float(va[i]), cscale, nxt[ch * 32 + i]);
-          v[32 + i] = __fmaf_rn(__uint_as_float(vb[i]), cscale, nxt[ch * 32 + 32 + i]);
+        for (int i = 0; i < 16; i++) {
+          const float4 nx = nx4[i];
+          const uint32_t *src = i < 8 ? va + 4 * i : vb + 4 * (i - 8);
+          fma2(__uint_as_float(src[0]), __uint_as_float(src[1]), cscale, nx.x, nx.y, v[4 * i],
+               v[4 * i + 1]);
+          fma2(__uint_as_float(src[2]), __uint_as_float(src[3]), cscale, nx.z, nx.w,
+               v[4 * i + 2], v[4 * i + 3]);
         }
-        // min over the 64 values as a tree (NaN loses in fminf)
-        float mn[32];
+        // minimum of each group of 8 columns (three-input min)
+        float gmin[8];
 #pragma unroll
-        for (int i = 0; i < 32; i++) mn[i] = fminf(v[i], v[32 + i]);
+        for (int g = 0; g < 8; g++) {
+          const float *w = v + 8 * g;
+          gmin[g] = min3f(min3f(w[0], w[1], w[2]), min3f(w[3], w[4], w[5]), fminf(w[6], w[7]));
+        }
+        const float all = min3f(min3f(gmin[0], gmin[1], gmin[2]), min3f(gmin[3], gmin[4], gmin[5]),
+                                fminf(gmin[6], gmin[7]));
+        if (__any_sync(0xffffffffu, all <= theta)) {
 #pragma unroll
-        for (int w = 16; w >= 1; w >>= 1)
+          for (int g = 0; g < 8; g++) {
+            if (__any_sync(0xffffffffu, gmin[g] <= theta)) {
 #pragma unroll
-          for (int i = 0; i < w; i++) mn[i] = fminf(mn[i], mn[i + w]);
-        if (mn[0] <= theta) {
-#pragma unroll
-          for (int i = 0; i < 64; i++) {
-            if (v[i] <= theta) {
-              if (cnt < cap) region[cnt] = make_uint2(row0 + ch * 32 + i, __float_as_uint(v[i]));
-              cnt++;
+              for (int i = 0; i < 8; i++) {
+                const float vi = v[8 * g + i];
+                if (vi <= theta) {
+                  if (cnt < cap) region[cnt] = make_uint2(row0 + ch + 8 * g + i, __float_as_uint(vi));
+                  cnt++;
+                }
+              }
             }
           }
         }
       }
     }
-    if (valid) a.ccount[(size_t)q * a.max_slices + s] = cnt;
+    if (valid) a.ccount[(size_t)q * 2 * a.max_slices + 2 * s + half] = cnt;
   }
 
   tc_fence_before();
@@ -334,7 +376,7 @@ __global__ void __launch_bounds__(256) tc_prep_x_kernel(const float *__restrict_
   bool bad = false;
   for (int rr = warp; rr < kBN; rr += 8) {
     const int64_t row = tile * kBN + rr;
-    float nrm = NAN;
+    float nrm = INFINITY;  // rows past m: v = +inf never passes a finite threshold
     if (row < m) {
       const float *x = X + row * d;
       float ss = 0.f, mx = 0.f;
@@ -522,7 +564,8 @@ struct LevelSelArgs {
   const uint2 *cand;
   const int *ccount;
   int64_t n;
-  int k, pool, region, slices, max_slices;
+  int k, pool, region;
+  int slices, max_slices;  // regions of the level and the count-array stride
   float *r_out;  // (n) k-th smallest v of the level, +inf when fewer than k
 };
 
@@ -582,7 +625,7 @@ __global__ void __launch_bounds__(kSelThreads) tc_final_select_kernel(const SelA
   if (threadIdx.x == 0) s_nsurv = 0;
   float theta = INFINITY;
   if (cnt >= a.k) theta = __fadd_ru(block_kth(cs, cnt, a.k, hist, &s_prefix, &s_rank),
-                                    a.qinfo[q].y);
+                                    a.qinfo[q].y);  // +inf when fewer than k: keep everything
   __syncthreads();
   // survivors -> exact distance with the reference arithmetic
   for (int e = threadIdx.x; e < cnt; e += blockDim.x) {
@@ -722,7 +765,7 @@ bool tc_make_plan(int64_t n, int64_t m, int d, int k, int slices, int pool, TcPl
     if (s < 1) s = 1;
     lv.tiles_per_slice = (lv.tiles + s - 1) / s;
     lv.slices = (int)((lv.tiles + lv.tiles_per_slice - 1) / lv.tiles_per_slice);
-    lv.region = P.cand_cap / lv.slices;
+    lv.region = P.cand_cap / (2 * lv.slices);
     if (lv.slices > max_s) max_s = lv.slices;
   }
   P.max_slices = max_s;
@@ -741,7 +784,7 @@ bool tc_make_plan(int64_t n, int64_t m, int d, int k, int slices, int pool, TcPl
   P.off_qinfo = off;    off = al256(off + (size_t)q_rows * 8);
   P.off_rlev = off;     off = al256(off + (size_t)n * 4);
   P.off_cand = off;     off = al256(off + (size_t)n * P.cand_cap * 8);
-  P.off_ccount = off;   off = al256(off + (size_t)n * max_s * 4);
+  P.off_ccount = off;   off = al256(off + (size_t)n * 2 * max_s * 4);
   P.off_flags = off;    off = al256(off + (size_t)n * 4);
   P.off_fbq = off;      off = al256(off + (size_t)n * d * 4);
   P.off_fbd = off;      off = al256(off + (size_t)n * k * 4);
@@ -858,8 +901,8 @@ int tc_run(const float *Q, const float *X, int64_t id_offset, float *out_d, int3
       S.k = p.k;
       S.pool = p.cand_cap;
       S.region = lv.region;
-      S.slices = lv.slices;
-      S.max_slices = p.max_slices;
+      S.slices = 2 * lv.slices;  // regions: two column halves per slice
+      S.max_slices = 2 * p.max_slices;
       S.r_out = rlev;
       tc_level_select_kernel<<<(unsigned)p.n, kSelThreads, lsmem, stream>>>(S);
       nl++;
@@ -878,8 +921,8 @@ int tc_run(const float *Q, const float *X, int64_t id_offset, float *out_d, int3
   S.k = p.k;
   S.pool = p.cand_cap;
   S.region = lv.region;
-  S.slices = lv.slices;
-  S.max_slices = p.max_slices;
+  S.slices = 2 * lv.slices;  // regions: two column halves per slice
+  S.max_slices = 2 * p.max_slices;
   S.id_offset = id_offset;
   S.qinfo = qinfo;
   S.cand = cand;
