@@ -50,7 +50,7 @@ constexpr int kMaxKch = 4;          // d <= 256 (query tile resident in shared m
 constexpr int kTcMaxK = 512;
 constexpr int kSelThreads = 256;
 constexpr int kSurvCap = 2048;      // exact re-rank capacity per query
-constexpr int kDefaultPool = 8192;  // candidate entries per query (all regions of a level)
+constexpr int kDefaultPool = 16384;  // candidate entries per query (all regions of a level)
 
 struct FilterArgs {
   const float *xnorm;    // (x_tiles*256) ||x||^2, +inf past m
@@ -953,12 +953,18 @@ int tc_run(const float *Q, const float *X, int64_t id_offset, float *out_d, int3
     int32_t *fi = reinterpret_cast<int32_t *>(ws + p.off_fbi);
     float *pd = reinterpret_cast<float *>(ws + p.off_fbpart_d);
     int32_t *pi = reinterpret_cast<int32_t *>(ws + p.off_fbpart_i);
+    // as many database slices as the partial buffer holds for this many queries
+    const int64_t part_entries = (int64_t)p.fb_slices * p.n * p.k;
+    int64_t fbs = part_entries / ((int64_t)h_fb * p.k);
+    if (fbs > 512) fbs = 512;
+    if (fbs > (p.m + 1023) / 1024) fbs = (p.m + 1023) / 1024;
+    if (fbs < 1) fbs = 1;
     tc_gather_rows<<<256, 256, 0, stream>>>(Q, p.d, fb_list, h_fb, Qf);
-    BFK_TRY(launch_direct(Qf, h_fb, X, p.m, p.d, p.k, id_offset, p.fb_slices, h_fb >= 64 ? 4 : 1,
-                          p.fb_slices > 1 ? pd : fd, p.fb_slices > 1 ? pi : fi, stream));
+    BFK_TRY(launch_direct(Qf, h_fb, X, p.m, p.d, p.k, id_offset, (int)fbs, h_fb >= 64 ? 4 : 1,
+                          fbs > 1 ? pd : fd, fbs > 1 ? pi : fi, stream));
     nl += 2;
-    if (p.fb_slices > 1) {
-      BFK_TRY(launch_merge(pd, pi, h_fb, p.fb_slices, p.k, fd, fi, stream));
+    if (fbs > 1) {
+      BFK_TRY(launch_merge(pd, pi, h_fb, (int)fbs, p.k, fd, fi, stream));
       nl++;
     }
     tc_scatter_rows<<<256, 256, 0, stream>>>(fd, fi, p.k, fb_list, h_fb, out_d, out_i);
