@@ -42,15 +42,17 @@ constexpr int kBN = 256;            // rows per tile (MMA N, accumulator columns
 constexpr int kBK = 64;             // f16 elements per K chunk (128 bytes, one swizzle atom row)
 constexpr int kAChunkBytes = kBM * kBK * 2;   // 16 KB
 constexpr int kBChunkBytes = kBN * kBK * 2;   // 32 KB
-constexpr int kTcThreads = 320;     // warp 0 TMA, warp 1 MMA, warps 2-9 epilogue
-constexpr int kEpiWarps = 8;        // two warps per TMEM lane quarter: one per column half
-constexpr int kHalfN = kBN / 2;     // accumulator columns an epilogue warp reads per tile
+constexpr int kEpiWarps = 16;       // four warps per TMEM lane quarter, one per 64-column group
+constexpr int kColGroups = 4;       // column groups of a tile (regions per slice)
+constexpr int kGroupN = kBN / kColGroups;  // accumulator columns an epilogue warp reads per tile
+constexpr int kTcThreads = 64 + 32 * kEpiWarps;  // warp 0 TMA, warp 1 MMA, 16 epilogue warps
 constexpr int kSmemLimit = 232448;  // 227 KB opt-in per block
 constexpr int kMaxKch = 4;          // d <= 256 (query tile resident in shared memory)
 constexpr int kTcMaxK = 512;
 constexpr int kSelThreads = 256;
 constexpr int kSurvCap = 2048;      // exact re-rank capacity per query
 constexpr int kDefaultPool = 16384;  // candidate entries per query (all regions of a level)
+constexpr int kLevelTarget = 3072;   // expected candidates per query of a filter level
 
 struct FilterArgs {
   const float *xnorm;    // (x_tiles*256) ||x||^2, +inf past m
@@ -62,11 +64,11 @@ struct FilterArgs {
   int64_t x_tiles;       // tiles of the whole database
   int64_t level_tiles;   // tiles of this level (evenly spaced over the database)
   int q_tiles, slices, tiles_per_slice;
-  int region;            // entries per (query, slice, column half) region
+  int region;            // entries per (query, slice, column group) region
   int pool;              // entries per query
-  int max_slices;        // count array stride / 2 (two column halves per slice)
+  int max_slices;        // count array stride / kColGroups
   uint2 *cand;           // (n, pool) (row, v bits)
-  int *ccount;           // (n, 2 * max_slices)
+  int *ccount;           // (n, kColGroups * max_slices)
   WsHeader *hdr;
 };
 
@@ -82,12 +84,12 @@ __host__ __device__ inline TcLayout tc_layout(int kch) {
   L.kch = kch;
   L.a_off = 0;
   L.b_off = (size_t)kch * kAChunkBytes;
-  const size_t fixed = (size_t)kEpiWarps * 2 * kHalfN * 4 + 256;
+  const size_t fixed = (size_t)kEpiWarps * 2 * kGroupN * 4 + 256;
   size_t ns = ((size_t)kSmemLimit - 1024 - L.b_off - fixed) / kBChunkBytes;
   if (ns > 6) ns = 6;
   L.ns = (int)ns;
   L.nx_off = L.b_off + (size_t)L.ns * kBChunkBytes;
-  L.bar_off = L.nx_off + (size_t)kEpiWarps * 2 * kHalfN * 4;
+  L.bar_off = L.nx_off + (size_t)kEpiWarps * 2 * kGroupN * 4;
   L.total = L.bar_off + 256 + 1024;  // + alignment slack
   return L;
 }
@@ -119,7 +121,8 @@ __device__ __forceinline__ int64_t level_tile(const FilterArgs &a, int64_t j) {
   return a.level_tiles == a.x_tiles ? j : (j * a.x_tiles) / a.level_tiles;
 }
 
-__global__ void __launch_bounds__(kTcThreads, 1)
+// 576 threads at one block per SM: 112 registers a thread
+__global__ void __maxnreg__(112)
     knn_tc_filter_kernel(const __grid_constant__ CUtensorMap tmap_q,
                          const __grid_constant__ CUtensorMap tmap_x, const FilterArgs a, int kch) {
   extern __shared__ __align__(1024) unsigned char smem_raw[];
@@ -240,10 +243,10 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       mbar_wait_bounded(drain, 0, abort_flag);
     }
   } else {
-    // ---------------- epilogue: one query per thread, half the columns per warp ----------------
-    const int e = warp - 2;                   // 0..7
+    // ------------- epilogue: one query per thread, 64 columns of each tile per warp -------------
+    const int e = warp - 2;                   // 0..15
     const int quarter = warp & 3;             // TMEM lanes this warp may access (warp % 4)
-    const int half = e >> 2;                  // columns [half*128, half*128 + 128) of each tile
+    const int cg = e >> 2;                    // columns [cg*64, cg*64 + 64) of each tile
     const int r = quarter * 32 + lane;        // query row within the tile
     const int64_t q = (int64_t)qt * kBM + r;
     const bool valid = q < a.n;
@@ -252,18 +255,18 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     float theta = -INFINITY;
     if (valid) theta = a.r_in ? fminf(__fadd_ru(a.r_in[q], m2), FLT_MAX) : FLT_MAX;
     uint2 *region = a.cand + (size_t)(valid ? q : 0) * a.pool +
-                    (size_t)(2 * s + half) * a.region;
-    const int cap = a.region;
+                    (size_t)(kColGroups * s + cg) * a.region;
+    const int last = a.region - 1;            // a full region keeps overwriting its last slot
     int cnt = 0;
-    const uint32_t lane_base = tmem_base + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(half * kHalfN);
+    const uint32_t taddr0 = tmem_base + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(cg * kGroupN);
     const float inv_sq = *a.inv_sq;
-    float *nxw = nxs + e * 2 * kHalfN;        // this warp's ||x||^2 staging, two buffers
-    // prefetch ||x||^2 (4 rows per lane) and the block scale of the first tile
-    float4 pre_nx = make_float4(0.f, 0.f, 0.f, 0.f);
+    float *nxw = nxs + e * 2 * kGroupN;       // this warp's ||x||^2 staging, two buffers
+    // prefetch ||x||^2 (2 rows per lane) and the block scale of the first tile
+    float2 pre_nx = make_float2(0.f, 0.f);
     float pre_inv = 1.f;
     if (ntiles > 0) {
       const int64_t t0 = level_tile(a, j_begin);
-      pre_nx = *reinterpret_cast<const float4 *>(a.xnorm + t0 * kBN + half * kHalfN + lane * 4);
+      pre_nx = *reinterpret_cast<const float2 *>(a.xnorm + t0 * kBN + cg * kGroupN + lane * 2);
       pre_inv = a.xinv[t0];
     }
 
@@ -272,13 +275,12 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       const int64_t tile = level_tile(a, j_begin + lt);
       // any role that gave up ends this warp's loop too (warp-uniform decision)
       if (__any_sync(0xffffffffu, *abort_flag != 0)) break;
-      float *nxt = nxw + b * kHalfN;
-      *reinterpret_cast<float4 *>(nxt + lane * 4) = pre_nx;
+      float *nxt = nxw + b * kGroupN;
+      *reinterpret_cast<float2 *>(nxt + lane * 2) = pre_nx;
       const float cscale = -2.0f * inv_sq * pre_inv;  // exact power of two
-      __syncwarp();
       if (lt + 1 < ntiles) {
         const int64_t tn = level_tile(a, j_begin + lt + 1);
-        pre_nx = *reinterpret_cast<const float4 *>(a.xnorm + tn * kBN + half * kHalfN + lane * 4);
+        pre_nx = *reinterpret_cast<const float2 *>(a.xnorm + tn * kBN + cg * kGroupN + lane * 2);
         pre_inv = a.xinv[tn];
       }
       // tcgen05.ld is warp-collective: the whole warp proceeds or none of it
@@ -289,58 +291,55 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         break;
       }
       tc_fence_after();
-      const uint32_t row0 = (uint32_t)(tile * kBN + half * kHalfN);
-#pragma unroll 1
-      for (int ch = 0; ch < kHalfN; ch += 64) {
-        uint32_t va[32], vb[32];
-        tmem_ld_32x32b_x32(lane_base + (uint32_t)(b * kBN + ch), va);
-        tmem_ld_32x32b_x32(lane_base + (uint32_t)(b * kBN + ch + 32), vb);
-        tmem_ld_wait();
-        if (ch + 64 == kHalfN) {
-          // the accumulator is in registers: hand the buffer back to the MMA warp
-          tc_fence_before();
-          __syncwarp();
-          if (lane == 0) mbar_arrive(acc_empty + b);
-        }
-        // v = acc * cscale + ||x||^2, two columns per packed FMA
-        float v[64];
-        const float4 *nx4 = reinterpret_cast<const float4 *>(nxt + ch);
+      uint32_t va[32], vb[32];
+      tmem_ld_32x32b_x32(taddr0 + (uint32_t)(b * kBN), va);
+      tmem_ld_32x32b_x32(taddr0 + (uint32_t)(b * kBN + 32), vb);
+      tmem_ld_wait();
+      // this warp's columns are in registers: release them to the MMA warp right away
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(acc_empty + b);
+      // v = acc * cscale + ||x||^2, two columns per packed FMA
+      float v[64];
+      const float4 *nx4 = reinterpret_cast<const float4 *>(nxt);
 #pragma unroll
-        for (int i = 0; i < 16; i++) {
-          const float4 nx = nx4[i];
-          const uint32_t *src = i < 8 ? va + 4 * i : vb + 4 * (i - 8);
-          fma2(__uint_as_float(src[0]), __uint_as_float(src[1]), cscale, nx.x, nx.y, v[4 * i],
-               v[4 * i + 1]);
-          fma2(__uint_as_float(src[2]), __uint_as_float(src[3]), cscale, nx.z, nx.w,
-               v[4 * i + 2], v[4 * i + 3]);
-        }
-        // minimum of each group of 8 columns (three-input min)
-        float gmin[8];
+      for (int i = 0; i < 16; i++) {
+        const float4 nx = nx4[i];
+        const uint32_t *src = i < 8 ? va + 4 * i : vb + 4 * (i - 8);
+        fma2(__uint_as_float(src[0]), __uint_as_float(src[1]), cscale, nx.x, nx.y, v[4 * i],
+             v[4 * i + 1]);
+        fma2(__uint_as_float(src[2]), __uint_as_float(src[3]), cscale, nx.z, nx.w, v[4 * i + 2],
+             v[4 * i + 3]);
+      }
+      // minimum of each group of 8 columns (three-input min)
+      float gmin[8];
+#pragma unroll
+      for (int g = 0; g < 8; g++) {
+        const float *w = v + 8 * g;
+        gmin[g] = min3f(min3f(w[0], w[1], w[2]), min3f(w[3], w[4], w[5]), fminf(w[6], w[7]));
+      }
+      const float all = min3f(min3f(gmin[0], gmin[1], gmin[2]), min3f(gmin[3], gmin[4], gmin[5]),
+                              fminf(gmin[6], gmin[7]));
+      if (__any_sync(0xffffffffu, all <= theta)) {
+        const uint32_t row0 = (uint32_t)(tile * kBN + cg * kGroupN);
 #pragma unroll
         for (int g = 0; g < 8; g++) {
-          const float *w = v + 8 * g;
-          gmin[g] = min3f(min3f(w[0], w[1], w[2]), min3f(w[3], w[4], w[5]), fminf(w[6], w[7]));
-        }
-        const float all = min3f(min3f(gmin[0], gmin[1], gmin[2]), min3f(gmin[3], gmin[4], gmin[5]),
-                                fminf(gmin[6], gmin[7]));
-        if (__any_sync(0xffffffffu, all <= theta)) {
+          if (__any_sync(0xffffffffu, gmin[g] <= theta)) {
 #pragma unroll
-          for (int g = 0; g < 8; g++) {
-            if (__any_sync(0xffffffffu, gmin[g] <= theta)) {
-#pragma unroll
-              for (int i = 0; i < 8; i++) {
-                const float vi = v[8 * g + i];
-                if (vi <= theta) {
-                  if (cnt < cap) region[cnt] = make_uint2(row0 + ch + 8 * g + i, __float_as_uint(vi));
-                  cnt++;
-                }
-              }
+            for (int i = 0; i < 8; i++) {
+              // predicated append: no branch per element
+              const float vi = v[8 * g + i];
+              const bool pass = vi <= theta;
+              uint2 *dst = region + min(cnt, last);
+              if (pass) *dst = make_uint2(row0 + 8 * g + i, __float_as_uint(vi));
+              cnt += pass ? 1 : 0;
             }
           }
         }
       }
+      __syncwarp();  // the staging buffer of this tile is reused two tiles later
     }
-    if (valid) a.ccount[(size_t)q * 2 * a.max_slices + 2 * s + half] = cnt;
+    if (valid) a.ccount[(size_t)q * kColGroups * a.max_slices + kColGroups * s + cg] = cnt;
   }
 
   tc_fence_before();
@@ -740,8 +739,10 @@ bool tc_make_plan(int64_t n, int64_t m, int d, int k, int slices, int pool, TcPl
   P.cand_cap = pool > 0 ? pool : kDefaultPool;
   if (P.cand_cap < 2 * k) P.cand_cap = 2 * k;
   if ((size_t)P.cand_cap * 8 + kSurvCap * 8 + (size_t)d * 4 > (size_t)kSmemLimit - 4096) return false;
-  // level sizes: each level's expected candidates ~ target = pool / 2
-  const int64_t target = P.cand_cap / 2;
+  // level sizes: each level's expected candidates ~ target (the pool holds 5x that)
+  int64_t target = kLevelTarget;
+  if (target < 4 * (int64_t)k) target = 4 * (int64_t)k;
+  if (target > P.cand_cap / 4) target = P.cand_cap / 4;
   int64_t ratio = target / k;
   if (ratio < 4) ratio = 4;
   int64_t sizes[kMaxLevels];
@@ -765,7 +766,7 @@ bool tc_make_plan(int64_t n, int64_t m, int d, int k, int slices, int pool, TcPl
     if (s < 1) s = 1;
     lv.tiles_per_slice = (lv.tiles + s - 1) / s;
     lv.slices = (int)((lv.tiles + lv.tiles_per_slice - 1) / lv.tiles_per_slice);
-    lv.region = P.cand_cap / (2 * lv.slices);
+    lv.region = P.cand_cap / (kColGroups * lv.slices);
     if (lv.slices > max_s) max_s = lv.slices;
   }
   P.max_slices = max_s;
@@ -784,7 +785,7 @@ bool tc_make_plan(int64_t n, int64_t m, int d, int k, int slices, int pool, TcPl
   P.off_qinfo = off;    off = al256(off + (size_t)q_rows * 8);
   P.off_rlev = off;     off = al256(off + (size_t)n * 4);
   P.off_cand = off;     off = al256(off + (size_t)n * P.cand_cap * 8);
-  P.off_ccount = off;   off = al256(off + (size_t)n * 2 * max_s * 4);
+  P.off_ccount = off;   off = al256(off + (size_t)n * kColGroups * max_s * 4);
   P.off_flags = off;    off = al256(off + (size_t)n * 4);
   P.off_fbq = off;      off = al256(off + (size_t)n * d * 4);
   P.off_fbd = off;      off = al256(off + (size_t)n * k * 4);
@@ -901,8 +902,8 @@ int tc_run(const float *Q, const float *X, int64_t id_offset, float *out_d, int3
       S.k = p.k;
       S.pool = p.cand_cap;
       S.region = lv.region;
-      S.slices = 2 * lv.slices;  // regions: two column halves per slice
-      S.max_slices = 2 * p.max_slices;
+      S.slices = kColGroups * lv.slices;  // regions: column groups of every slice
+      S.max_slices = kColGroups * p.max_slices;
       S.r_out = rlev;
       tc_level_select_kernel<<<(unsigned)p.n, kSelThreads, lsmem, stream>>>(S);
       nl++;
@@ -921,8 +922,8 @@ int tc_run(const float *Q, const float *X, int64_t id_offset, float *out_d, int3
   S.k = p.k;
   S.pool = p.cand_cap;
   S.region = lv.region;
-  S.slices = 2 * lv.slices;  // regions: two column halves per slice
-  S.max_slices = 2 * p.max_slices;
+  S.slices = kColGroups * lv.slices;  // regions: column groups of every slice
+  S.max_slices = kColGroups * p.max_slices;
   S.id_offset = id_offset;
   S.qinfo = qinfo;
   S.cand = cand;
