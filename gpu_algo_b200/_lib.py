@@ -32,6 +32,7 @@ STATUS = {
 EXPORTS = (
     "bfk_version",
     "bfk_status_string",
+    "bfk_last_error",
     "bfk_workspace_size",
     "bfk_search",
     "bfk_merge",
@@ -66,7 +67,13 @@ class Stats(ctypes.Structure):
 class BfkError(RuntimeError):
     def __init__(self, status: int, what: str):
         self.status = status
-        super().__init__(f"{what}: {STATUS.get(status, status)} ({status_string(status)})")
+        msg = f"{what}: {STATUS.get(status, status)} ({status_string(status)})"
+        if status == 4:
+            try:
+                msg += f" [{load().bfk_last_error().decode()}]"
+            except Exception:  # pragma: no cover
+                pass
+        super().__init__(msg)
 
 
 _lock = threading.Lock()
@@ -90,6 +97,8 @@ def load() -> ctypes.CDLL:
         lib.bfk_version.argtypes = [i32p, i32p]
         lib.bfk_status_string.restype = ctypes.c_char_p
         lib.bfk_status_string.argtypes = [i32]
+        lib.bfk_last_error.restype = ctypes.c_char_p
+        lib.bfk_last_error.argtypes = []
         lib.bfk_workspace_size.restype = i32
         lib.bfk_workspace_size.argtypes = [i64, i64, i32, i32, ctypes.POINTER(Opts),
                                            ctypes.POINTER(u64)]

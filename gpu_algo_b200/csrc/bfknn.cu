@@ -1,4 +1,5 @@
 // C ABI of libbfknn: argument validation, workspace layout, engine dispatch.
+#include <cstdio>
 #include <cstring>
 #include <utility>
 #include <vector>
@@ -91,7 +92,14 @@ bfk_status_t validate(int64_t n, int64_t m, int32_t d, int32_t k, int64_t id_off
   return BFK_OK;
 }
 
-bfk_status_t cuda_status(cudaError_t e) { return e == cudaSuccess ? BFK_OK : BFK_ERR_CUDA; }
+bfk_status_t cuda_status_at(cudaError_t e, const char *file, int line) {
+  if (e == cudaSuccess) return BFK_OK;
+  bfk::note_cuda_error(e, file, line, "launch");
+  return BFK_ERR_CUDA;
+}
+#define cuda_status(e) cuda_status_at((e), __FILE__, __LINE__)
+
+thread_local char g_last_error[256] = "no error";
 
 // Per-thread record of main-kernel timings (BFK_FLAG_TIME_MAIN) and of the
 // number of kernels the last call launched.
@@ -121,7 +129,17 @@ thread_local CallRecord g_calls;
 
 }  // namespace
 
+namespace bfk {
+void note_cuda_error(cudaError_t e, const char *file, int line, const char *what) {
+  const char *base = std::strrchr(file, '/');
+  std::snprintf(g_last_error, sizeof(g_last_error), "%s:%d %s: %s (%d)", base ? base + 1 : file,
+                line, what, cudaGetErrorString(e), (int)e);
+}
+}  // namespace bfk
+
 extern "C" {
+
+const char *bfk_last_error(void) { return g_last_error; }
 
 bfk_status_t bfk_version(int32_t *major, int32_t *minor) {
   if (!major || !minor) return BFK_ERR_INVALID_ARGUMENT;
@@ -199,7 +217,7 @@ bfk_status_t bfk_search(const float *Q, int64_t n, const float *X, int64_t m, in
   if (workspace_bytes < p.total) return BFK_ERR_WORKSPACE;
   WsHeader *hdr = reinterpret_cast<WsHeader *>(ws);
   cudaError_t e = cudaMemsetAsync(hdr, 0, sizeof(WsHeader), stream);
-  if (e != cudaSuccess) return BFK_ERR_CUDA;
+  if (e != cudaSuccess) return cuda_status(e);
   if (m == 0) {
     // nothing to search: every slot is padding
     g_calls.launches = 1;
@@ -216,7 +234,7 @@ bfk_status_t bfk_search(const float *Q, int64_t n, const float *X, int64_t m, in
   int32_t *pi = reinterpret_cast<int32_t *>(ws + p.off_part_i);
   e = launch_direct(Q, n, X, m, d, k, id_offset, p.slices, p.tq, pd, pi, stream);
   if (t1) cudaEventRecord(t1, stream);
-  if (e != cudaSuccess) return BFK_ERR_CUDA;
+  if (e != cudaSuccess) return cuda_status(e);
   g_calls.launches = 2;
   return cuda_status(launch_merge(pd, pi, n, p.slices, k, out_dists, out_ids, stream));
 }
@@ -243,7 +261,7 @@ bfk_status_t bfk_kernel_attrs(int32_t engine, int32_t d, int32_t k, bfk_attrs_t 
   if (engine == BFK_ENGINE_TC_F16) {
     if (!tc_supported(d, k)) return BFK_ERR_UNSUPPORTED;
     fn = tc_kernel_ptr(d, k);
-    threads = 320;
+    threads = tc_threads();
     dyn = tc_smem_bytes(d, k);
   } else if (engine == BFK_ENGINE_DIRECT || engine == BFK_ENGINE_AUTO) {
     const int tq = k <= 512 ? 4 : 1;

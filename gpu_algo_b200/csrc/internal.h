@@ -6,6 +6,10 @@
 
 namespace bfk {
 
+// Records the last failing CUDA call of this thread (reported by bfk_last_error).
+void note_cuda_error(cudaError_t e, const char *file, int line, const char *what);
+#define BFK_NOTE(e, what) ::bfk::note_cuda_error((e), __FILE__, __LINE__, (what))
+
 // direct.cu -- exact SIMT engine
 size_t direct_smem_bytes(int tq, int k);
 const void *direct_kernel_ptr(int tq);
@@ -53,5 +57,6 @@ int tc_run(const float *Q, const float *X, int64_t id_offset, float *out_d, int3
            int *launches);
 const void *tc_kernel_ptr(int d, int k);
 size_t tc_smem_bytes(int d, int k);
+int tc_threads();
 
 }  // namespace bfk

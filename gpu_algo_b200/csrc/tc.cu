@@ -121,8 +121,8 @@ __device__ __forceinline__ int64_t level_tile(const FilterArgs &a, int64_t j) {
   return a.level_tiles == a.x_tiles ? j : (j * a.x_tiles) / a.level_tiles;
 }
 
-// 576 threads at one block per SM: 112 registers a thread
-__global__ void __maxnreg__(112)
+// 576 threads in one block: the launch admits at most 96 registers a thread
+__global__ void __maxnreg__(96)
     knn_tc_filter_kernel(const __grid_constant__ CUtensorMap tmap_q,
                          const __grid_constant__ CUtensorMap tmap_x, const FilterArgs a, int kch) {
   extern __shared__ __align__(1024) unsigned char smem_raw[];
@@ -291,48 +291,53 @@ __global__ void __maxnreg__(112)
         break;
       }
       tc_fence_after();
-      uint32_t va[32], vb[32];
-      tmem_ld_32x32b_x32(taddr0 + (uint32_t)(b * kBN), va);
-      tmem_ld_32x32b_x32(taddr0 + (uint32_t)(b * kBN + 32), vb);
-      tmem_ld_wait();
-      // this warp's columns are in registers: release them to the MMA warp right away
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(acc_empty + b);
-      // v = acc * cscale + ||x||^2, two columns per packed FMA
-      float v[64];
-      const float4 *nx4 = reinterpret_cast<const float4 *>(nxt);
+      const uint32_t row0 = (uint32_t)(tile * kBN + cg * kGroupN);
+#pragma unroll 1
+      for (int hh = 0; hh < 2; hh++) {
+        // 32 columns at a time keeps the register footprint small (18 warps share the file)
+        uint32_t va[32];
+        tmem_ld_32x32b_x32(taddr0 + (uint32_t)(b * kBN + hh * 32), va);
+        tmem_ld_wait();
+        if (hh == 1) {
+          // this warp's columns are in registers: release them to the MMA warp
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(acc_empty + b);
+        } else {
+          __syncwarp();  // the ||x||^2 staging written above is visible to every lane
+        }
+        // v = acc * cscale + ||x||^2, two columns per packed FMA
+        float v[32];
+        const float4 *nx4 = reinterpret_cast<const float4 *>(nxt + hh * 32);
 #pragma unroll
-      for (int i = 0; i < 16; i++) {
-        const float4 nx = nx4[i];
-        const uint32_t *src = i < 8 ? va + 4 * i : vb + 4 * (i - 8);
-        fma2(__uint_as_float(src[0]), __uint_as_float(src[1]), cscale, nx.x, nx.y, v[4 * i],
-             v[4 * i + 1]);
-        fma2(__uint_as_float(src[2]), __uint_as_float(src[3]), cscale, nx.z, nx.w, v[4 * i + 2],
-             v[4 * i + 3]);
-      }
-      // minimum of each group of 8 columns (three-input min)
-      float gmin[8];
+        for (int i = 0; i < 8; i++) {
+          const float4 nx = nx4[i];
+          fma2(__uint_as_float(va[4 * i]), __uint_as_float(va[4 * i + 1]), cscale, nx.x, nx.y,
+               v[4 * i], v[4 * i + 1]);
+          fma2(__uint_as_float(va[4 * i + 2]), __uint_as_float(va[4 * i + 3]), cscale, nx.z, nx.w,
+               v[4 * i + 2], v[4 * i + 3]);
+        }
+        // minimum of each group of 8 columns (three-input min)
+        float gmin[4];
 #pragma unroll
-      for (int g = 0; g < 8; g++) {
-        const float *w = v + 8 * g;
-        gmin[g] = min3f(min3f(w[0], w[1], w[2]), min3f(w[3], w[4], w[5]), fminf(w[6], w[7]));
-      }
-      const float all = min3f(min3f(gmin[0], gmin[1], gmin[2]), min3f(gmin[3], gmin[4], gmin[5]),
-                              fminf(gmin[6], gmin[7]));
-      if (__any_sync(0xffffffffu, all <= theta)) {
-        const uint32_t row0 = (uint32_t)(tile * kBN + cg * kGroupN);
+        for (int g = 0; g < 4; g++) {
+          const float *w = v + 8 * g;
+          gmin[g] = min3f(min3f(w[0], w[1], w[2]), min3f(w[3], w[4], w[5]), fminf(w[6], w[7]));
+        }
+        const float all = fminf(min3f(gmin[0], gmin[1], gmin[2]), gmin[3]);
+        if (__any_sync(0xffffffffu, all <= theta)) {
 #pragma unroll
-        for (int g = 0; g < 8; g++) {
-          if (__any_sync(0xffffffffu, gmin[g] <= theta)) {
+          for (int g = 0; g < 4; g++) {
+            if (__any_sync(0xffffffffu, gmin[g] <= theta)) {
 #pragma unroll
-            for (int i = 0; i < 8; i++) {
-              // predicated append: no branch per element
-              const float vi = v[8 * g + i];
-              const bool pass = vi <= theta;
-              uint2 *dst = region + min(cnt, last);
-              if (pass) *dst = make_uint2(row0 + 8 * g + i, __float_as_uint(vi));
-              cnt += pass ? 1 : 0;
+              for (int i = 0; i < 8; i++) {
+                // predicated append: no branch per element
+                const float vi = v[8 * g + i];
+                const bool pass = vi <= theta;
+                uint2 *dst = region + min(cnt, last);
+                if (pass) *dst = make_uint2(row0 + hh * 32 + 8 * g + i, __float_as_uint(vi));
+                cnt += pass ? 1 : 0;
+              }
             }
           }
         }
@@ -362,7 +367,9 @@ __device__ __forceinline__ float pow2_scale_for(float maxabs) {
   return ldexpf(1.f, p);
 }
 
-// grid (x_tiles), block 256 (8 warps x 32 rows)
+// grid (x_tiles), block 256 (8 warps x 32 rows).  VEC: d % 4 == 0, rows read as
+// float4 (one row per warp instruction for d = 128) with four rows in flight.
+template <bool VEC>
 __global__ void __launch_bounds__(256) tc_prep_x_kernel(const float *__restrict__ X, int64_t m,
                                                         int d, int d_pad, __half *__restrict__ Xh,
                                                         float *__restrict__ xnorm,
@@ -373,36 +380,60 @@ __global__ void __launch_bounds__(256) tc_prep_x_kernel(const float *__restrict_
   const int64_t tile = blockIdx.x;
   float wmax = 0.f, wrn = 0.f;
   bool bad = false;
-  for (int rr = warp; rr < kBN; rr += 8) {
-    const int64_t row = tile * kBN + rr;
-    float nrm = INFINITY;  // rows past m: v = +inf never passes a finite threshold
-    if (row < m) {
-      const float *x = X + row * d;
-      float ss = 0.f, mx = 0.f;
-      for (int c = lane; c < d; c += 32) {
-        const float v = x[c];
-        ss = __fmaf_rn(v, v, ss);
-        mx = fmaxf(mx, fabsf(v));
+  const int d4 = d >> 2;
+  for (int r0 = warp * 32; r0 < warp * 32 + 32; r0 += 4) {
+    float ss[4], mx[4];
+#pragma unroll
+    for (int u = 0; u < 4; u++) {
+      ss[u] = 0.f;
+      mx[u] = 0.f;
+      const int64_t row = tile * kBN + r0 + u;
+      if (row < m) {
+        if (VEC) {
+          const float4 *x4 = reinterpret_cast<const float4 *>(X + row * d);
+          for (int c = lane; c < d4; c += 32) {
+            const float4 v = __ldg(x4 + c);
+            ss[u] = __fmaf_rn(v.x, v.x, ss[u]);
+            ss[u] = __fmaf_rn(v.y, v.y, ss[u]);
+            ss[u] = __fmaf_rn(v.z, v.z, ss[u]);
+            ss[u] = __fmaf_rn(v.w, v.w, ss[u]);
+            mx[u] = fmaxf(mx[u], fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w))));
+          }
+        } else {
+          const float *x = X + row * d;
+          for (int c = lane; c < d; c += 32) {
+            const float v = __ldg(x + c);
+            ss[u] = __fmaf_rn(v, v, ss[u]);
+            mx[u] = fmaxf(mx[u], fabsf(v));
+          }
+        }
       }
+    }
+#pragma unroll
+    for (int u = 0; u < 4; u++) {
 #pragma unroll
       for (int o = 16; o > 0; o >>= 1) {
-        ss += __shfl_xor_sync(0xffffffffu, ss, o);
-        mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+        ss[u] += __shfl_xor_sync(0xffffffffu, ss[u], o);
+        mx[u] = fmaxf(mx[u], __shfl_xor_sync(0xffffffffu, mx[u], o));
       }
-      nrm = ss;
-      if (!isfinite(ss)) bad = true;
-      wmax = fmaxf(wmax, mx);
-      wrn = fmaxf(wrn, sqrtf(ss));
+      const int64_t row = tile * kBN + r0 + u;
+      // rows past m: v = +inf never passes a finite threshold
+      const float nrm = row < m ? ss[u] : INFINITY;
+      if (row < m) {
+        if (!isfinite(ss[u])) bad = true;
+        wmax = fmaxf(wmax, mx[u]);
+        wrn = fmaxf(wrn, sqrtf(ss[u]));
+      }
+      if (lane == u) xnorm[row] = nrm;
     }
-    if (lane == 0) xnorm[row] = nrm;
   }
   if (lane == 0) { s_max[warp] = wmax; s_rn[warp] = wrn; }
   if (bad && lane == 0) atomicOr(&hdr->nonfinite, 1);
   __syncthreads();
   if (threadIdx.x == 0) {
-    float mx = 0.f, rn = 0.f;
-    for (int w = 0; w < 8; w++) { mx = fmaxf(mx, s_max[w]); rn = fmaxf(rn, s_rn[w]); }
-    const float sc = pow2_scale_for(mx);
+    float mxb = 0.f, rn = 0.f;
+    for (int w = 0; w < 8; w++) { mxb = fmaxf(mxb, s_max[w]); rn = fmaxf(rn, s_rn[w]); }
+    const float sc = pow2_scale_for(mxb);
     s_scale = sc;
     xinv[tile] = 1.f / sc;
     // sqrt of an FP32 sum of d squares: (1 + 2^-10) covers its rounding for d <= 4096;
@@ -414,9 +445,23 @@ __global__ void __launch_bounds__(256) tc_prep_x_kernel(const float *__restrict_
   for (int rr = warp; rr < kBN; rr += 8) {
     const int64_t row = tile * kBN + rr;
     if (row >= m) break;
-    const float *x = X + row * d;
     __half *xh = Xh + row * d_pad;
-    for (int c = lane; c < d_pad; c += 32) xh[c] = __float2half_rn(c < d ? x[c] * sc : 0.f);
+    if (VEC) {
+      // four halves (8 bytes) per lane and step; columns past d are zero
+      const float4 *x4 = reinterpret_cast<const float4 *>(X + row * d);
+      for (int c = lane; c < (d_pad >> 2); c += 32) {
+        float4 v = c < d4 ? __ldg(x4 + c) : make_float4(0.f, 0.f, 0.f, 0.f);
+        __half2 lo = __floats2half2_rn(v.x * sc, v.y * sc);
+        __half2 hi = __floats2half2_rn(v.z * sc, v.w * sc);
+        uint2 pk;
+        pk.x = *reinterpret_cast<uint32_t *>(&lo);
+        pk.y = *reinterpret_cast<uint32_t *>(&hi);
+        reinterpret_cast<uint2 *>(xh)[c] = pk;
+      }
+    } else {
+      const float *x = X + row * d;
+      for (int c = lane; c < d_pad; c += 32) xh[c] = __float2half_rn(c < d ? x[c] * sc : 0.f);
+    }
   }
 }
 
@@ -508,50 +553,119 @@ __device__ void bitonic_sort_u64(uint64_t *keys, int P) {
   __syncthreads();
 }
 
-// Gather a query's candidates of one level into shared memory (compacted).
-// Returns the number gathered; *s_over is set when a region lost entries.
-__device__ int gather_level(const uint2 *cand, const int *ccount, int64_t q, int pool, int region,
-                            int slices, int max_slices, uint2 *out, int *s_total, int *s_over) {
-  if (threadIdx.x == 0) { *s_total = 0; *s_over = 0; }
-  __syncthreads();
-  for (int sl = 0; sl < slices; sl++) {
-    int c = ccount[(size_t)q * max_slices + sl];
-    if (c > region) {
-      if (threadIdx.x == 0) *s_over = 1;
-      c = region;
-    }
-    const int base = *s_total;
-    const uint2 *src = cand + (size_t)q * pool + (size_t)sl * region;
-    for (int e = threadIdx.x; e < c; e += blockDim.x) out[base + e] = src[e];
-    __syncthreads();
-    if (threadIdx.x == 0) *s_total = base + c;
-    __syncthreads();
+// Candidate regions of one query, read in place (no staging copy): counts are
+// clamped to the region size; `over` records that a region lost entries.
+struct QueryRegions {
+  const uint2 *base;   // this query's pool
+  int region;          // entries per region
+  int nreg;            // regions of the level
+  int total;
+  bool over;
+};
+
+__device__ QueryRegions load_regions(const uint2 *cand, const int *ccount, int64_t q, int pool,
+                                     int region, int nreg, int stride, int *s_cnt, int *s_off,
+                                     int *s_misc) {
+  // s_cnt[i] = entries of region i, s_off = exclusive prefix (nreg <= 256)
+  for (int i = threadIdx.x; i < nreg; i += blockDim.x) {
+    const int c = ccount[(size_t)q * stride + i];
+    s_cnt[i] = c;
   }
-  return *s_total;
+  __syncthreads();
+  if (threadIdx.x < 32) {
+    // warp 0: exclusive scan of the clamped counts, 8 regions per lane
+    const int lane = threadIdx.x;
+    int loc[8], sum = 0, over = 0;
+#pragma unroll
+    for (int j = 0; j < 8; j++) {
+      const int i = lane * 8 + j;
+      int c = i < nreg ? s_cnt[i] : 0;
+      if (c > region) { over = 1; c = region; }
+      loc[j] = c;
+      sum += c;
+    }
+    int incl = sum;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int t = __shfl_up_sync(0xffffffffu, incl, o);
+      if (lane >= o) incl += t;
+    }
+    int run = incl - sum;
+#pragma unroll
+    for (int j = 0; j < 8; j++) {
+      const int i = lane * 8 + j;
+      if (i < nreg) { s_cnt[i] = loc[j]; s_off[i] = run; }
+      run += loc[j];
+    }
+    over = __any_sync(0xffffffffu, over);
+    if (lane == 31) { s_misc[0] = incl; s_misc[1] = over; }
+  }
+  __syncthreads();
+  QueryRegions R;
+  R.base = cand + (size_t)q * pool;
+  R.region = region;
+  R.nreg = nreg;
+  R.total = s_misc[0];
+  R.over = s_misc[1] != 0;
+  return R;
 }
 
-// k-th smallest v (as float) among cnt entries, by radix select on order keys.
-__device__ float block_kth(const uint2 *cs, int cnt, int k, int *hist, uint32_t *s_prefix,
-                           int *s_rank) {
+// entry e (0 <= e < total) of the compacted candidate list
+__device__ __forceinline__ uint2 region_entry(const QueryRegions &R, const int *s_cnt,
+                                              const int *s_off, int e) {
+  // binary search for the region holding e (regions are few: <= 256)
+  int lo = 0, hi = R.nreg - 1;
+  while (lo < hi) {
+    const int mid = (lo + hi + 1) >> 1;
+    if (s_off[mid] <= e) lo = mid;
+    else hi = mid - 1;
+  }
+  return R.base[(size_t)lo * R.region + (e - s_off[lo])];
+}
+
+// k-th smallest v among the query's candidates (radix select, 8 bits a pass,
+// reading the candidates from global memory / L2 in every pass)
+__device__ float block_kth(const QueryRegions &R, const int *s_cnt, const int *s_off, int k,
+                           int *hist, uint32_t *s_prefix, int *s_rank) {
   if (threadIdx.x == 0) { *s_prefix = 0u; *s_rank = k; }
   uint32_t mask = 0u;
   for (int shift = 24; shift >= 0; shift -= 8) {
     for (int b = threadIdx.x; b < 256; b += blockDim.x) hist[b] = 0;
     __syncthreads();
     const uint32_t prefix = *s_prefix;
-    for (int e = threadIdx.x; e < cnt; e += blockDim.x) {
-      const uint32_t key = f2ord(__uint_as_float(cs[e].y));
-      if ((key & mask) == prefix) atomicAdd(&hist[(key >> shift) & 255], 1);
+    for (int rg = 0; rg < R.nreg; rg++) {
+      const uint2 *src = R.base + (size_t)rg * R.region;
+      const int c = s_cnt[rg];
+      for (int e = threadIdx.x; e < c; e += blockDim.x) {
+        const uint32_t key = f2ord(__uint_as_float(src[e].y));
+        if ((key & mask) == prefix) atomicAdd(&hist[(key >> shift) & 255], 1);
+      }
     }
     __syncthreads();
-    if (threadIdx.x == 0) {
-      int need = *s_rank, b = 0;
-      for (; b < 255; b++) {
-        if (hist[b] >= need) break;
-        need -= hist[b];
+    if (threadIdx.x < 32) {
+      // warp 0 finds the bin holding the rank: 8 bins per lane + a warp scan
+      const int lane = threadIdx.x;
+      int h[8], sum = 0;
+#pragma unroll
+      for (int j = 0; j < 8; j++) { h[j] = hist[lane * 8 + j]; sum += h[j]; }
+      int incl = sum;
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const int t = __shfl_up_sync(0xffffffffu, incl, o);
+        if (lane >= o) incl += t;
       }
-      *s_rank = need;
-      *s_prefix = prefix | ((uint32_t)b << shift);
+      const int need = *s_rank;
+      const int excl = incl - sum;
+      const bool mine = excl < need && incl >= need;
+      if (mine) {
+        int left = need - excl, b = 0;
+        for (; b < 7; b++) {
+          if (h[b] >= left) break;
+          left -= h[b];
+        }
+        *s_rank = left;
+        *s_prefix = prefix | ((uint32_t)(lane * 8 + b) << shift);
+      }
     }
     __syncthreads();
     mask |= 255u << shift;
@@ -564,32 +678,29 @@ struct LevelSelArgs {
   const int *ccount;
   int64_t n;
   int k, pool, region;
-  int slices, max_slices;  // regions of the level and the count-array stride
-  float *r_out;  // (n) k-th smallest v of the level, +inf when fewer than k
+  int nreg, stride;  // regions of the level and the count-array stride
+  float *r_out;      // (n) k-th smallest v of the level, +inf when fewer than k
 };
 
 // one block per query: R_q for the next level
 __global__ void __launch_bounds__(kSelThreads) tc_level_select_kernel(const LevelSelArgs a) {
-  extern __shared__ __align__(1024) unsigned char smem_raw[];
-  uint2 *cs = reinterpret_cast<uint2 *>(smem_raw);
-  __shared__ int hist[256];
-  __shared__ int s_total, s_over, s_rank;
+  __shared__ int hist[256], s_cnt[256], s_off[256], s_misc[2], s_rank;
   __shared__ uint32_t s_prefix;
   const int64_t q = blockIdx.x;
-  const int cnt = gather_level(a.cand, a.ccount, q, a.pool, a.region, a.slices, a.max_slices, cs,
-                               &s_total, &s_over);
+  const QueryRegions R = load_regions(a.cand, a.ccount, q, a.pool, a.region, a.nreg, a.stride,
+                                      s_cnt, s_off, s_misc);
   // entries lost to a full region only make R larger than it could be: still a
   // valid bound, since R is the k-th smallest over real rows that were kept
-  float R = INFINITY;
-  if (cnt >= a.k) R = block_kth(cs, cnt, a.k, hist, &s_prefix, &s_rank);
-  if (threadIdx.x == 0) a.r_out[q] = R;
+  float r = INFINITY;
+  if (R.total >= a.k) r = block_kth(R, s_cnt, s_off, a.k, hist, &s_prefix, &s_rank);
+  if (threadIdx.x == 0) a.r_out[q] = r;
 }
 
 struct SelArgs {
   const float *Q;
   const float *X;
   int64_t n, m;
-  int d, k, pool, region, slices, max_slices;
+  int d, k, pool, region, nreg, stride;
   int64_t id_offset;
   const float2 *qinfo;
   const uint2 *cand;
@@ -600,20 +711,18 @@ struct SelArgs {
   int32_t *out_i;
 };
 
-// dynamic smem: pool * 8 (candidates) + kSurvCap * 8 (survivor keys) + d * 4 (query)
+// one block per query; dynamic smem: kSurvCap * 8 (survivor keys) + d * 4 (query)
 __global__ void __launch_bounds__(kSelThreads) tc_final_select_kernel(const SelArgs a) {
   extern __shared__ __align__(1024) unsigned char smem_raw[];
-  uint2 *cs = reinterpret_cast<uint2 *>(smem_raw);
-  uint64_t *keys = reinterpret_cast<uint64_t *>(cs + a.pool);
+  uint64_t *keys = reinterpret_cast<uint64_t *>(smem_raw);
   float *qs = reinterpret_cast<float *>(keys + kSurvCap);
-  __shared__ int hist[256];
-  __shared__ int s_total, s_over, s_rank, s_nsurv;
+  __shared__ int hist[256], s_cnt[256], s_off[256], s_misc[2], s_rank, s_nsurv;
   __shared__ uint32_t s_prefix;
   const int64_t q = blockIdx.x;
-  const int cnt = gather_level(a.cand, a.ccount, q, a.pool, a.region, a.slices, a.max_slices, cs,
-                               &s_total, &s_over);
+  const QueryRegions R = load_regions(a.cand, a.ccount, q, a.pool, a.region, a.nreg, a.stride,
+                                      s_cnt, s_off, s_misc);
   // a region that lost entries, or non-finite inputs (the margin needs finite norms)
-  if (s_over || a.hdr->nonfinite) {
+  if (R.over || a.hdr->nonfinite) {
     if (threadIdx.x == 0) {
       const int slot = atomicAdd(&a.hdr->fallback, 1);
       a.fb_list[slot] = (int)q;
@@ -622,21 +731,26 @@ __global__ void __launch_bounds__(kSelThreads) tc_final_select_kernel(const SelA
   }
   for (int c = threadIdx.x; c < a.d; c += blockDim.x) qs[c] = a.Q[q * a.d + c];
   if (threadIdx.x == 0) s_nsurv = 0;
-  float theta = INFINITY;
-  if (cnt >= a.k) theta = __fadd_ru(block_kth(cs, cnt, a.k, hist, &s_prefix, &s_rank),
-                                    a.qinfo[q].y);  // +inf when fewer than k: keep everything
+  float theta = INFINITY;  // fewer than k candidates: keep them all
+  if (R.total >= a.k)
+    theta = __fadd_ru(block_kth(R, s_cnt, s_off, a.k, hist, &s_prefix, &s_rank), a.qinfo[q].y);
   __syncthreads();
   // survivors -> exact distance with the reference arithmetic
-  for (int e = threadIdx.x; e < cnt; e += blockDim.x) {
-    const float v = __uint_as_float(cs[e].y);
-    if (v <= theta) {
-      const int slot = atomicAdd(&s_nsurv, 1);
-      if (slot < kSurvCap) {
-        const int64_t row = cs[e].x;
-        const float *x = a.X + row * a.d;
-        float acc = 0.f;
-        for (int c = 0; c < a.d; c++) acc = dist_step(qs[c], x[c], acc);
-        keys[slot] = acc == acc ? pair_key(acc, (int32_t)(a.id_offset + row)) : ~0ull;
+  for (int rg = 0; rg < R.nreg; rg++) {
+    const uint2 *src = R.base + (size_t)rg * R.region;
+    const int c = s_cnt[rg];
+    for (int e = threadIdx.x; e < c; e += blockDim.x) {
+      const uint2 ent = src[e];
+      const float v = __uint_as_float(ent.y);
+      if (v <= theta) {
+        const int slot = atomicAdd(&s_nsurv, 1);
+        if (slot < kSurvCap) {
+          const int64_t row = ent.x;
+          const float *x = a.X + row * a.d;
+          float acc = 0.f;
+          for (int cc = 0; cc < a.d; cc++) acc = dist_step(qs[cc], x[cc], acc);
+          keys[slot] = acc == acc ? pair_key(acc, (int32_t)(a.id_offset + row)) : ~0ull;
+        }
       }
     }
   }
@@ -661,8 +775,8 @@ __global__ void __launch_bounds__(kSelThreads) tc_final_select_kernel(const SelA
   }
   if (threadIdx.x == 0) {
     atomicAdd(&a.hdr->survivors, (unsigned long long)ns);
-    atomicAdd(&a.hdr->candidates, (unsigned long long)cnt);
-    atomicMax(&a.hdr->max_cand, cnt);
+    atomicAdd(&a.hdr->candidates, (unsigned long long)R.total);
+    atomicMax(&a.hdr->max_cand, R.total);
   }
 }
 
@@ -701,6 +815,8 @@ size_t tc_smem_bytes(int d, int) { return tc_layout(kch_for(d)).total; }
 
 const void *tc_kernel_ptr(int, int) { return (const void *)knn_tc_filter_kernel; }
 
+int tc_threads() { return kTcThreads; }
+
 static int num_sms() {
   int dev = 0, sms = 148;
   if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
@@ -738,7 +854,7 @@ bool tc_make_plan(int64_t n, int64_t m, int d, int k, int slices, int pool, TcPl
   P.x_tiles = (m + kBN - 1) / kBN;
   P.cand_cap = pool > 0 ? pool : kDefaultPool;
   if (P.cand_cap < 2 * k) P.cand_cap = 2 * k;
-  if ((size_t)P.cand_cap * 8 + kSurvCap * 8 + (size_t)d * 4 > (size_t)kSmemLimit - 4096) return false;
+
   // level sizes: each level's expected candidates ~ target (the pool holds 5x that)
   int64_t target = kLevelTarget;
   if (target < 4 * (int64_t)k) target = 4 * (int64_t)k;
@@ -843,30 +959,38 @@ int tc_run(const float *Q, const float *X, int64_t id_offset, float *out_d, int3
   const int64_t q_rows = (int64_t)p.q_tiles * kBM;
   int nl = 0;
 
-#define BFK_TRY(x)                    \
-  do {                                \
-    if ((x) != cudaSuccess) return 1; \
+#define BFK_TRY(x)                         \
+  do {                                     \
+    const cudaError_t e_ = (x);            \
+    if (e_ != cudaSuccess) {               \
+      BFK_NOTE(e_, #x);                    \
+      return 1;                            \
+    }                                      \
   } while (0)
 
   BFK_TRY(cudaMemsetAsync(hdr, 0, sizeof(WsHeader), stream));
   // pass 0: prep
   tc_qmax_kernel<<<592, 256, 0, stream>>>(Q, p.n * p.d, hdr);
-  tc_prep_x_kernel<<<(unsigned)p.x_tiles, 256, 0, stream>>>(X, p.m, p.d, p.d_pad, Xh, xnorm, xinv, hdr);
+  if ((p.d & 3) == 0 && (reinterpret_cast<uintptr_t>(X) & 15) == 0)
+    tc_prep_x_kernel<true><<<(unsigned)p.x_tiles, 256, 0, stream>>>(X, p.m, p.d, p.d_pad, Xh, xnorm,
+                                                                     xinv, hdr);
+  else
+    tc_prep_x_kernel<false><<<(unsigned)p.x_tiles, 256, 0, stream>>>(X, p.m, p.d, p.d_pad, Xh, xnorm,
+                                                                      xinv, hdr);
   tc_prep_q_kernel<<<(unsigned)(q_rows / 8), 256, 0, stream>>>(Q, p.n, p.d, p.d_pad, q_rows, Qh,
                                                                 qinfo, inv_sq, hdr);
   nl += 3;
   BFK_TRY(cudaGetLastError());
 
   CUtensorMap tq, tx;
-  if (!make_tmap(&tq, Qh, q_rows, p.d_pad, kBM)) return 1;
-  if (!make_tmap(&tx, Xh, p.m, p.d_pad, kBN)) return 1;
+  if (!make_tmap(&tq, Qh, q_rows, p.d_pad, kBM) || !make_tmap(&tx, Xh, p.m, p.d_pad, kBN)) {
+    BFK_NOTE(cudaErrorInvalidValue, "cuTensorMapEncodeTiled");
+    return 1;
+  }
   const int kch = p.d_pad / kBK;
   const size_t smem = tc_smem_bytes(p.d, p.k);
   BFK_TRY(cudaFuncSetAttribute((const void *)knn_tc_filter_kernel,
                                cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
-  const size_t lsmem = (size_t)p.cand_cap * 8;
-  BFK_TRY(cudaFuncSetAttribute((const void *)tc_level_select_kernel,
-                               cudaFuncAttributeMaxDynamicSharedMemorySize, (int)lsmem));
   FilterArgs A{};
   A.xnorm = xnorm;
   A.xinv = xinv;
@@ -902,10 +1026,10 @@ int tc_run(const float *Q, const float *X, int64_t id_offset, float *out_d, int3
       S.k = p.k;
       S.pool = p.cand_cap;
       S.region = lv.region;
-      S.slices = kColGroups * lv.slices;  // regions: column groups of every slice
-      S.max_slices = kColGroups * p.max_slices;
+      S.nreg = kColGroups * lv.slices;  // regions: column groups of every slice
+      S.stride = kColGroups * p.max_slices;
       S.r_out = rlev;
-      tc_level_select_kernel<<<(unsigned)p.n, kSelThreads, lsmem, stream>>>(S);
+      tc_level_select_kernel<<<(unsigned)p.n, kSelThreads, 0, stream>>>(S);
       nl++;
       BFK_TRY(cudaGetLastError());
     }
@@ -922,8 +1046,8 @@ int tc_run(const float *Q, const float *X, int64_t id_offset, float *out_d, int3
   S.k = p.k;
   S.pool = p.cand_cap;
   S.region = lv.region;
-  S.slices = kColGroups * lv.slices;  // regions: column groups of every slice
-  S.max_slices = kColGroups * p.max_slices;
+  S.nreg = kColGroups * lv.slices;  // regions: column groups of every slice
+  S.stride = kColGroups * p.max_slices;
   S.id_offset = id_offset;
   S.qinfo = qinfo;
   S.cand = cand;
@@ -932,7 +1056,7 @@ int tc_run(const float *Q, const float *X, int64_t id_offset, float *out_d, int3
   S.hdr = hdr;
   S.out_d = out_d;
   S.out_i = out_i;
-  const size_t ssmem = (size_t)p.cand_cap * 8 + kSurvCap * 8 + (size_t)p.d * 4;
+  const size_t ssmem = (size_t)kSurvCap * 8 + (size_t)p.d * 4;
   BFK_TRY(cudaFuncSetAttribute((const void *)tc_final_select_kernel,
                                cudaFuncAttributeMaxDynamicSharedMemorySize, (int)ssmem));
   tc_final_select_kernel<<<(unsigned)p.n, kSelThreads, ssmem, stream>>>(S);

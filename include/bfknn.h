@@ -91,6 +91,10 @@ BFK_API bfk_status_t bfk_version(int32_t *major, int32_t *minor);
 /* Human-readable status.  No reference counterpart (the reference raises CuPy errors). */
 BFK_API const char *bfk_status_string(int32_t status);
 
+/* The last failing CUDA call of the calling thread ("file:line call: error (code)").
+ * No reference counterpart. */
+BFK_API const char *bfk_last_error(void);
+
 /*
  * Device-memory workspace `bfk_search` needs for this shape (bytes, a multiple
  * of 256).  Replaces the per-call CuPy allocations of the reference runners
