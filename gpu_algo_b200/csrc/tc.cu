@@ -2,7 +2,7 @@
 // per-query thresholds, then an exact FP32 re-rank of the few survivors.
 //
 // Pass 0 (prep): queries and database rows are scaled by powers of two and
-//   rounded to f16 (rows in 256-row blocks sharing one scale), with their FP32
+//   rounded to f16 (rows in 64-row groups sharing one scale), with their FP32
 //   squared norms and a per-query error margin m, a bound on
 //   |approximate distance - reference distance| (derived in tc_prep_q_kernel).
 // Filter passes (one CTA per (128-query tile, slice of a tile set)): TMA
@@ -56,7 +56,7 @@ constexpr int kLevelTarget = 3072;   // expected candidates per query of a filte
 
 struct FilterArgs {
   const float *xnorm;    // (x_tiles*256) ||x||^2, +inf past m
-  const float *xinv;     // (x_tiles) 1/scale of each 256-row block
+  const float *xinv;     // (x_tiles * 4) 1/scale of each 64-row group
   const float2 *qinfo;   // (q_tiles*128) (||q||^2, 2*margin); NaN margin for padding rows
   const float *inv_sq;   // 1/scale of the queries (device scalar)
   const float *r_in;     // (n) threshold of the previous level, null = +inf
@@ -267,7 +267,7 @@ __global__ void __maxnreg__(96)
     if (ntiles > 0) {
       const int64_t t0 = level_tile(a, j_begin);
       pre_nx = *reinterpret_cast<const float2 *>(a.xnorm + t0 * kBN + cg * kGroupN + lane * 2);
-      pre_inv = a.xinv[t0];
+      pre_inv = a.xinv[t0 * kColGroups + cg];
     }
 
     for (int lt = 0; lt < ntiles; lt++) {
@@ -281,7 +281,7 @@ __global__ void __maxnreg__(96)
       if (lt + 1 < ntiles) {
         const int64_t tn = level_tile(a, j_begin + lt + 1);
         pre_nx = *reinterpret_cast<const float2 *>(a.xnorm + tn * kBN + cg * kGroupN + lane * 2);
-        pre_inv = a.xinv[tn];
+        pre_inv = a.xinv[tn * kColGroups + cg];
       }
       // tcgen05.ld is warp-collective: the whole warp proceeds or none of it
       const bool got = __all_sync(0xffffffffu, mbar_wait_bounded(acc_full + b, (lt >> 1) & 1,
@@ -331,12 +331,15 @@ __global__ void __maxnreg__(96)
             if (__any_sync(0xffffffffu, gmin[g] <= theta)) {
 #pragma unroll
               for (int i = 0; i < 8; i++) {
-                // predicated append: no branch per element
+                // one ballot per column; the append runs only for columns some lane keeps
                 const float vi = v[8 * g + i];
-                const bool pass = vi <= theta;
-                uint2 *dst = region + min(cnt, last);
-                if (pass) *dst = make_uint2(row0 + hh * 32 + 8 * g + i, __float_as_uint(vi));
-                cnt += pass ? 1 : 0;
+                const unsigned keep = __ballot_sync(0xffffffffu, vi <= theta);
+                if (keep) {
+                  const bool mine = (keep >> lane) & 1u;
+                  if (mine)
+                    region[min(cnt, last)] = make_uint2(row0 + hh * 32 + 8 * g + i, __float_as_uint(vi));
+                  cnt += mine ? 1 : 0;
+                }
               }
             }
           }
@@ -367,96 +370,100 @@ __device__ __forceinline__ float pow2_scale_for(float maxabs) {
   return ldexpf(1.f, p);
 }
 
-// grid (x_tiles), block 256 (8 warps x 32 rows).  VEC: d % 4 == 0, rows read as
-// float4 (one row per warp instruction for d = 128) with four rows in flight.
+// Database rows -> f16.  Each group of 64 rows (one epilogue warp's columns of a
+// tile) shares a power-of-two scale.  grid (ceil(m / 64)), block 256: eight warps
+// of eight rows each.  VEC (d % 4 == 0, d <= 256): each row is read once, as
+// float4s held in registers between the norm pass and the conversion.
+constexpr int kScaleRows = kBN / kColGroups;  // 64
 template <bool VEC>
 __global__ void __launch_bounds__(256) tc_prep_x_kernel(const float *__restrict__ X, int64_t m,
                                                         int d, int d_pad, __half *__restrict__ Xh,
                                                         float *__restrict__ xnorm,
                                                         float *__restrict__ xinv, WsHeader *hdr) {
   __shared__ float s_max[8], s_rn[8];
-  __shared__ float s_scale;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int64_t tile = blockIdx.x;
+  const int64_t grp = blockIdx.x;
+  const int64_t row_base = grp * kScaleRows + warp * 8;
+  const int d4 = d >> 2;
+  float4 xr[8][2];  // VEC: rows of up to 256 floats, two float4 per lane
+  float ss[8], mx[8];
+#pragma unroll
+  for (int u = 0; u < 8; u++) {
+    ss[u] = 0.f;
+    mx[u] = 0.f;
+    const int64_t row = row_base + u;
+    if (VEC) {
+#pragma unroll
+      for (int h = 0; h < 2; h++) {
+        const int c = lane + 32 * h;
+        float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+        if (row < m && c < d4) v = __ldg(reinterpret_cast<const float4 *>(X + row * d) + c);
+        xr[u][h] = v;
+        ss[u] = __fmaf_rn(v.x, v.x, ss[u]);
+        ss[u] = __fmaf_rn(v.y, v.y, ss[u]);
+        ss[u] = __fmaf_rn(v.z, v.z, ss[u]);
+        ss[u] = __fmaf_rn(v.w, v.w, ss[u]);
+        mx[u] = fmaxf(mx[u], fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w))));
+      }
+    } else if (row < m) {
+      const float *x = X + row * d;
+      for (int c = lane; c < d; c += 32) {
+        const float v = __ldg(x + c);
+        ss[u] = __fmaf_rn(v, v, ss[u]);
+        mx[u] = fmaxf(mx[u], fabsf(v));
+      }
+    }
+  }
   float wmax = 0.f, wrn = 0.f;
   bool bad = false;
-  const int d4 = d >> 2;
-  for (int r0 = warp * 32; r0 < warp * 32 + 32; r0 += 4) {
-    float ss[4], mx[4];
 #pragma unroll
-    for (int u = 0; u < 4; u++) {
-      ss[u] = 0.f;
-      mx[u] = 0.f;
-      const int64_t row = tile * kBN + r0 + u;
-      if (row < m) {
-        if (VEC) {
-          const float4 *x4 = reinterpret_cast<const float4 *>(X + row * d);
-          for (int c = lane; c < d4; c += 32) {
-            const float4 v = __ldg(x4 + c);
-            ss[u] = __fmaf_rn(v.x, v.x, ss[u]);
-            ss[u] = __fmaf_rn(v.y, v.y, ss[u]);
-            ss[u] = __fmaf_rn(v.z, v.z, ss[u]);
-            ss[u] = __fmaf_rn(v.w, v.w, ss[u]);
-            mx[u] = fmaxf(mx[u], fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w))));
-          }
-        } else {
-          const float *x = X + row * d;
-          for (int c = lane; c < d; c += 32) {
-            const float v = __ldg(x + c);
-            ss[u] = __fmaf_rn(v, v, ss[u]);
-            mx[u] = fmaxf(mx[u], fabsf(v));
-          }
-        }
-      }
+  for (int u = 0; u < 8; u++) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      ss[u] += __shfl_xor_sync(0xffffffffu, ss[u], o);
+      mx[u] = fmaxf(mx[u], __shfl_xor_sync(0xffffffffu, mx[u], o));
     }
-#pragma unroll
-    for (int u = 0; u < 4; u++) {
-#pragma unroll
-      for (int o = 16; o > 0; o >>= 1) {
-        ss[u] += __shfl_xor_sync(0xffffffffu, ss[u], o);
-        mx[u] = fmaxf(mx[u], __shfl_xor_sync(0xffffffffu, mx[u], o));
-      }
-      const int64_t row = tile * kBN + r0 + u;
-      // rows past m: v = +inf never passes a finite threshold
-      const float nrm = row < m ? ss[u] : INFINITY;
-      if (row < m) {
-        if (!isfinite(ss[u])) bad = true;
-        wmax = fmaxf(wmax, mx[u]);
-        wrn = fmaxf(wrn, sqrtf(ss[u]));
-      }
-      if (lane == u) xnorm[row] = nrm;
+    const int64_t row = row_base + u;
+    if (row < m) {
+      if (!isfinite(ss[u])) bad = true;
+      wmax = fmaxf(wmax, mx[u]);
+      wrn = fmaxf(wrn, sqrtf(ss[u]));
     }
+    // rows past m: v = +inf never passes a finite threshold
+    if (lane == u) xnorm[row] = row < m ? ss[u] : INFINITY;
   }
   if (lane == 0) { s_max[warp] = wmax; s_rn[warp] = wrn; }
   if (bad && lane == 0) atomicOr(&hdr->nonfinite, 1);
   __syncthreads();
+  float gmax = 0.f, rn = 0.f;
+#pragma unroll
+  for (int w = 0; w < 8; w++) { gmax = fmaxf(gmax, s_max[w]); rn = fmaxf(rn, s_rn[w]); }
+  const float sc = pow2_scale_for(gmax);
   if (threadIdx.x == 0) {
-    float mxb = 0.f, rn = 0.f;
-    for (int w = 0; w < 8; w++) { mxb = fmaxf(mxb, s_max[w]); rn = fmaxf(rn, s_rn[w]); }
-    const float sc = pow2_scale_for(mxb);
-    s_scale = sc;
-    xinv[tile] = 1.f / sc;
+    xinv[grp] = 1.f / sc;
     // sqrt of an FP32 sum of d squares: (1 + 2^-10) covers its rounding for d <= 4096;
     // the bound only grows, and non-negative floats order like their bit patterns
     if (isfinite(rn)) atomicMax(&hdr->rx_bits, __float_as_uint(rn * (1.f + 0.0009765625f)));
   }
-  __syncthreads();
-  const float sc = s_scale;
-  for (int rr = warp; rr < kBN; rr += 8) {
-    const int64_t row = tile * kBN + rr;
+#pragma unroll
+  for (int u = 0; u < 8; u++) {
+    const int64_t row = row_base + u;
     if (row >= m) break;
     __half *xh = Xh + row * d_pad;
     if (VEC) {
       // four halves (8 bytes) per lane and step; columns past d are zero
-      const float4 *x4 = reinterpret_cast<const float4 *>(X + row * d);
-      for (int c = lane; c < (d_pad >> 2); c += 32) {
-        float4 v = c < d4 ? __ldg(x4 + c) : make_float4(0.f, 0.f, 0.f, 0.f);
-        __half2 lo = __floats2half2_rn(v.x * sc, v.y * sc);
-        __half2 hi = __floats2half2_rn(v.z * sc, v.w * sc);
-        uint2 pk;
-        pk.x = *reinterpret_cast<uint32_t *>(&lo);
-        pk.y = *reinterpret_cast<uint32_t *>(&hi);
-        reinterpret_cast<uint2 *>(xh)[c] = pk;
+#pragma unroll
+      for (int h = 0; h < 2; h++) {
+        const int c = lane + 32 * h;
+        if (c < (d_pad >> 2)) {
+          const float4 v = xr[u][h];
+          __half2 lo = __floats2half2_rn(v.x * sc, v.y * sc);
+          __half2 hi = __floats2half2_rn(v.z * sc, v.w * sc);
+          uint2 pk;
+          pk.x = *reinterpret_cast<uint32_t *>(&lo);
+          pk.y = *reinterpret_cast<uint32_t *>(&hi);
+          reinterpret_cast<uint2 *>(xh)[c] = pk;
+        }
       }
     } else {
       const float *x = X + row * d;
@@ -512,7 +519,7 @@ __global__ void __launch_bounds__(256) tc_prep_q_kernel(const float *__restrict_
     if (!isfinite(ss)) atomicOr(&hdr->nonfinite, 1);
     // Error margin.  With u = 2^-11 the f16 unit roundoff, qn >= ||q||, Rx >= max ||x||:
     //   e_q = u qn + sqrt(d) 2^-25 / s_q        (f16 rounding of q, incl. subnormals)
-    //   e_x = (u + sqrt(d) 2^-38) Rx             (rows scaled to [2^13, 2^14) per block)
+    //   e_x = (u + sqrt(d) 2^-38) Rx             (row groups scaled to [2^13, 2^14))
     //   dot rounding  <= e_q Rx + qn e_x + e_q e_x
     //   accumulation  <= (d_pad + 16) 2^-22 (qn + e_q)(Rx + e_x)   (tensor-core FP32 sums)
     //   FP32 terms    <= 2 (d + 8) 2^-24 (qn + Rx)^2  (norms, the fused epilogue step,
@@ -823,21 +830,22 @@ static int num_sms() {
   return sms > 0 ? sms : 148;
 }
 
-// slices for a level of `tiles` tiles: whole waves of CTAs, at most `max_s`
+// slices for a level of `tiles` tiles: the count (at most `max_s`) whose last wave
+// of CTAs is fullest, keeping at least 16 tiles per slice where possible
 static int choose_slices(int q_tiles, int64_t tiles, int sms, int max_s) {
   int best = 1;
-  double best_eff = -1.0;
+  double best_score = -1.0;
   for (int s = 1; s <= max_s && s <= tiles; s++) {
-    const int64_t ctas = (int64_t)q_tiles * s;
     const int64_t tps = (tiles + s - 1) / s;
     const int64_t used = (tiles + tps - 1) / tps;  // slices that get tiles
     if (used != s) continue;
+    if (s > 1 && tps < 16) break;
+    const int64_t ctas = (int64_t)q_tiles * s;
     const int64_t waves = (ctas + sms - 1) / sms;
-    const double eff = (double)ctas / (double)(waves * sms);
-    // prefer fuller waves; among similar, fewer slices (larger regions)
-    if (eff > best_eff + 0.03) { best_eff = eff; best = s; }
-    if (waves >= 4 && eff > 0.9) break;
-    if (tps < 8) break;
+    // work per wave slot, counting the last slice's shorter share of tiles
+    const double eff = (double)tiles * q_tiles / ((double)waves * sms * tps);
+    const double score = eff - 0.0005 * s;  // among equals, fewer and longer slices
+    if (score > best_score) { best_score = score; best = s; }
   }
   return best;
 }
@@ -896,7 +904,7 @@ bool tc_make_plan(int64_t n, int64_t m, int d, int k, int slices, int pool, TcPl
   size_t off = sizeof(WsHeader);
   P.off_xh = off;       off = al256(off + (size_t)m * P.d_pad * 2);
   P.off_xnorm = off;    off = al256(off + (size_t)P.x_tiles * kBN * 4);
-  P.off_xscale = off;   off = al256(off + (size_t)P.x_tiles * 4 + 16);
+  P.off_xscale = off;   off = al256(off + (size_t)P.x_tiles * kColGroups * 4 + 16);
   P.off_qh = off;       off = al256(off + (size_t)q_rows * P.d_pad * 2);
   P.off_qinfo = off;    off = al256(off + (size_t)q_rows * 8);
   P.off_rlev = off;     off = al256(off + (size_t)n * 4);
@@ -949,7 +957,7 @@ int tc_run(const float *Q, const float *X, int64_t id_offset, float *out_d, int3
   __half *Xh = reinterpret_cast<__half *>(ws + p.off_xh);
   float *xnorm = reinterpret_cast<float *>(ws + p.off_xnorm);
   float *xinv = reinterpret_cast<float *>(ws + p.off_xscale);
-  float *inv_sq = xinv + p.x_tiles;  // one float after the block scales
+  float *inv_sq = xinv + p.x_tiles * kColGroups;  // one float after the group scales
   __half *Qh = reinterpret_cast<__half *>(ws + p.off_qh);
   float2 *qinfo = reinterpret_cast<float2 *>(ws + p.off_qinfo);
   float *rlev = reinterpret_cast<float *>(ws + p.off_rlev);
@@ -971,12 +979,11 @@ int tc_run(const float *Q, const float *X, int64_t id_offset, float *out_d, int3
   BFK_TRY(cudaMemsetAsync(hdr, 0, sizeof(WsHeader), stream));
   // pass 0: prep
   tc_qmax_kernel<<<592, 256, 0, stream>>>(Q, p.n * p.d, hdr);
-  if ((p.d & 3) == 0 && (reinterpret_cast<uintptr_t>(X) & 15) == 0)
-    tc_prep_x_kernel<true><<<(unsigned)p.x_tiles, 256, 0, stream>>>(X, p.m, p.d, p.d_pad, Xh, xnorm,
-                                                                     xinv, hdr);
+  const unsigned groups = (unsigned)(p.x_tiles * kColGroups);  // 64-row scale groups
+  if ((p.d & 3) == 0 && p.d <= 256 && (reinterpret_cast<uintptr_t>(X) & 15) == 0)
+    tc_prep_x_kernel<true><<<groups, 256, 0, stream>>>(X, p.m, p.d, p.d_pad, Xh, xnorm, xinv, hdr);
   else
-    tc_prep_x_kernel<false><<<(unsigned)p.x_tiles, 256, 0, stream>>>(X, p.m, p.d, p.d_pad, Xh, xnorm,
-                                                                      xinv, hdr);
+    tc_prep_x_kernel<false><<<groups, 256, 0, stream>>>(X, p.m, p.d, p.d_pad, Xh, xnorm, xinv, hdr);
   tc_prep_q_kernel<<<(unsigned)(q_rows / 8), 256, 0, stream>>>(Q, p.n, p.d, p.d_pad, q_rows, Qh,
                                                                 qinfo, inv_sq, hdr);
   nl += 3;
