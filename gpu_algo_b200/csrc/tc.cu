@@ -375,7 +375,7 @@ __device__ __forceinline__ float pow2_scale_for(float maxabs) {
 // of eight rows each.  VEC (d % 4 == 0, d <= 256): each row is read once, as
 // float4s held in registers between the norm pass and the conversion.
 constexpr int kScaleRows = kBN / kColGroups;  // 64
-template <bool VEC>
+template <bool VEC, int W4>
 __global__ void __launch_bounds__(256) tc_prep_x_kernel(const float *__restrict__ X, int64_t m,
                                                         int d, int d_pad, __half *__restrict__ Xh,
                                                         float *__restrict__ xnorm,
@@ -385,7 +385,7 @@ __global__ void __launch_bounds__(256) tc_prep_x_kernel(const float *__restrict_
   const int64_t grp = blockIdx.x;
   const int64_t row_base = grp * kScaleRows + warp * 8;
   const int d4 = d >> 2;
-  float4 xr[8][2];  // VEC: rows of up to 256 floats, two float4 per lane
+  float4 xr[8][W4];  // VEC: rows of up to 128 * W4 floats, W4 float4 per lane
   float ss[8], mx[8];
 #pragma unroll
   for (int u = 0; u < 8; u++) {
@@ -394,7 +394,7 @@ __global__ void __launch_bounds__(256) tc_prep_x_kernel(const float *__restrict_
     const int64_t row = row_base + u;
     if (VEC) {
 #pragma unroll
-      for (int h = 0; h < 2; h++) {
+      for (int h = 0; h < W4; h++) {
         const int c = lane + 32 * h;
         float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
         if (row < m && c < d4) v = __ldg(reinterpret_cast<const float4 *>(X + row * d) + c);
@@ -453,7 +453,7 @@ __global__ void __launch_bounds__(256) tc_prep_x_kernel(const float *__restrict_
     if (VEC) {
       // four halves (8 bytes) per lane and step; columns past d are zero
 #pragma unroll
-      for (int h = 0; h < 2; h++) {
+      for (int h = 0; h < W4; h++) {
         const int c = lane + 32 * h;
         if (c < (d_pad >> 2)) {
           const float4 v = xr[u][h];
@@ -560,8 +560,8 @@ __device__ void bitonic_sort_u64(uint64_t *keys, int P) {
   __syncthreads();
 }
 
-// Candidate regions of one query, read in place (no staging copy): counts are
-// clamped to the region size; `over` records that a region lost entries.
+// Candidate regions of one query: counts clamped to the region size, their
+// exclusive prefix offsets, and whether a region lost entries.
 struct QueryRegions {
   const uint2 *base;   // this query's pool
   int region;          // entries per region
@@ -573,14 +573,10 @@ struct QueryRegions {
 __device__ QueryRegions load_regions(const uint2 *cand, const int *ccount, int64_t q, int pool,
                                      int region, int nreg, int stride, int *s_cnt, int *s_off,
                                      int *s_misc) {
-  // s_cnt[i] = entries of region i, s_off = exclusive prefix (nreg <= 256)
-  for (int i = threadIdx.x; i < nreg; i += blockDim.x) {
-    const int c = ccount[(size_t)q * stride + i];
-    s_cnt[i] = c;
-  }
+  for (int i = threadIdx.x; i < nreg; i += blockDim.x) s_cnt[i] = ccount[(size_t)q * stride + i];
   __syncthreads();
   if (threadIdx.x < 32) {
-    // warp 0: exclusive scan of the clamped counts, 8 regions per lane
+    // warp 0: exclusive scan of the clamped counts, 8 regions per lane (nreg <= 256)
     const int lane = threadIdx.x;
     int loc[8], sum = 0, over = 0;
 #pragma unroll
@@ -617,67 +613,111 @@ __device__ QueryRegions load_regions(const uint2 *cand, const int *ccount, int64
   return R;
 }
 
-// entry e (0 <= e < total) of the compacted candidate list
-__device__ __forceinline__ uint2 region_entry(const QueryRegions &R, const int *s_cnt,
-                                              const int *s_off, int e) {
-  // binary search for the region holding e (regions are few: <= 256)
-  int lo = 0, hi = R.nreg - 1;
-  while (lo < hi) {
-    const int mid = (lo + hi + 1) >> 1;
-    if (s_off[mid] <= e) lo = mid;
-    else hi = mid - 1;
+constexpr int kSelStage = 6144;  // candidates staged in shared memory (more: read in place)
+constexpr int kSelBins = 1024;
+
+// Copy the candidates into shared memory, one warp per region, and return the
+// block-wide min and max of v (smem staging when total <= kSelStage).
+__device__ void stage_candidates(const QueryRegions &R, const int *s_cnt, const int *s_off,
+                                 uint2 *cs, float *s_red, float *vmin, float *vmax) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nw = blockDim.x >> 5;
+  const bool stage = R.total <= kSelStage;
+  float lo = INFINITY, hi = -INFINITY;
+  for (int rg = warp; rg < R.nreg; rg += nw) {
+    const uint2 *src = R.base + (size_t)rg * R.region;
+    const int c = s_cnt[rg], o = s_off[rg];
+    for (int e = lane; e < c; e += 32) {
+      const uint2 ent = src[e];
+      const float v = __uint_as_float(ent.y);
+      lo = fminf(lo, v);
+      hi = fmaxf(hi, v);
+      if (stage) cs[o + e] = ent;
+    }
   }
-  return R.base[(size_t)lo * R.region + (e - s_off[lo])];
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    lo = fminf(lo, __shfl_xor_sync(0xffffffffu, lo, o));
+    hi = fmaxf(hi, __shfl_xor_sync(0xffffffffu, hi, o));
+  }
+  if (lane == 0) { s_red[warp] = lo; s_red[32 + warp] = hi; }
+  __syncthreads();
+  lo = INFINITY;
+  hi = -INFINITY;
+  for (int w = 0; w < nw; w++) { lo = fminf(lo, s_red[w]); hi = fmaxf(hi, s_red[32 + w]); }
+  *vmin = lo;
+  *vmax = hi;
+  __syncthreads();
 }
 
-// k-th smallest v among the query's candidates (radix select, 8 bits a pass,
-// reading the candidates from global memory / L2 in every pass)
-__device__ float block_kth(const QueryRegions &R, const int *s_cnt, const int *s_off, int k,
-                           int *hist, uint32_t *s_prefix, int *s_rank) {
-  if (threadIdx.x == 0) { *s_prefix = 0u; *s_rank = k; }
-  uint32_t mask = 0u;
-  for (int shift = 24; shift >= 0; shift -= 8) {
-    for (int b = threadIdx.x; b < 256; b += blockDim.x) hist[b] = 0;
-    __syncthreads();
-    const uint32_t prefix = *s_prefix;
-    for (int rg = 0; rg < R.nreg; rg++) {
+// Apply f(entry) to every candidate (shared-memory copy when staged).
+template <class F>
+__device__ __forceinline__ void for_each_candidate(const QueryRegions &R, const int *s_cnt,
+                                                   const uint2 *cs, F f) {
+  if (R.total <= kSelStage) {
+    for (int e = threadIdx.x; e < R.total; e += blockDim.x) f(cs[e]);
+  } else {
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nw = blockDim.x >> 5;
+    for (int rg = warp; rg < R.nreg; rg += nw) {
       const uint2 *src = R.base + (size_t)rg * R.region;
       const int c = s_cnt[rg];
-      for (int e = threadIdx.x; e < c; e += blockDim.x) {
-        const uint32_t key = f2ord(__uint_as_float(src[e].y));
-        if ((key & mask) == prefix) atomicAdd(&hist[(key >> shift) & 255], 1);
-      }
+      for (int e = lane; e < c; e += 32) f(src[e]);
     }
-    __syncthreads();
-    if (threadIdx.x < 32) {
-      // warp 0 finds the bin holding the rank: 8 bins per lane + a warp scan
-      const int lane = threadIdx.x;
-      int h[8], sum = 0;
-#pragma unroll
-      for (int j = 0; j < 8; j++) { h[j] = hist[lane * 8 + j]; sum += h[j]; }
-      int incl = sum;
-#pragma unroll
-      for (int o = 1; o < 32; o <<= 1) {
-        const int t = __shfl_up_sync(0xffffffffu, incl, o);
-        if (lane >= o) incl += t;
-      }
-      const int need = *s_rank;
-      const int excl = incl - sum;
-      const bool mine = excl < need && incl >= need;
-      if (mine) {
-        int left = need - excl, b = 0;
-        for (; b < 7; b++) {
-          if (h[b] >= left) break;
-          left -= h[b];
-        }
-        *s_rank = left;
-        *s_prefix = prefix | ((uint32_t)(lane * 8 + b) << shift);
-      }
-    }
-    __syncthreads();
-    mask |= 255u << shift;
   }
-  return ord2f(*s_prefix);
+}
+
+// An upper bound R >= the k-th smallest v that is itself the value of a
+// candidate ranked >= k: values are binned linearly over [vmin, vmax]; R is the
+// largest v in the bins up to the one where the running count reaches k.
+// Any such R is a valid threshold (at least k candidates have v <= R).
+__device__ float block_kth_bound(const QueryRegions &R, const int *s_cnt, const uint2 *cs, int k,
+                                 float vmin, float vmax, int *hist, float *s_red, int *s_bin) {
+  const float span = vmax - vmin;
+  const float scale = span > 0.f ? (float)(kSelBins - 1) / span : 0.f;
+  for (int b = threadIdx.x; b < kSelBins; b += blockDim.x) hist[b] = 0;
+  __syncthreads();
+  auto bin_of = [&](float v) {
+    int b = (int)((v - vmin) * scale);
+    return b < 0 ? 0 : (b > kSelBins - 1 ? kSelBins - 1 : b);
+  };
+  for_each_candidate(R, s_cnt, cs, [&](uint2 ent) { atomicAdd(&hist[bin_of(__uint_as_float(ent.y))], 1); });
+  __syncthreads();
+  if (threadIdx.x < 32) {
+    // warp 0: first bin where the running count reaches k (32 bins per lane)
+    const int lane = threadIdx.x;
+    int sum = 0;
+    for (int j = 0; j < kSelBins / 32; j++) sum += hist[lane * (kSelBins / 32) + j];
+    int incl = sum;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int t = __shfl_up_sync(0xffffffffu, incl, o);
+      if (lane >= o) incl += t;
+    }
+    const int excl = incl - sum;
+    if (excl < k && incl >= k) {
+      int run = excl, b = lane * (kSelBins / 32);
+      for (;; b++) {
+        run += hist[b];
+        if (run >= k) break;
+      }
+      *s_bin = b;
+    }
+  }
+  __syncthreads();
+  const int kb = *s_bin;
+  float mx = -INFINITY;
+  for_each_candidate(R, s_cnt, cs, [&](uint2 ent) {
+    const float v = __uint_as_float(ent.y);
+    if (bin_of(v) <= kb) mx = fmaxf(mx, v);
+  });
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (lane == 0) s_red[64 + warp] = mx;
+  __syncthreads();
+  float r = -INFINITY;
+  for (int w = 0; w < (int)(blockDim.x >> 5); w++) r = fmaxf(r, s_red[64 + w]);
+  __syncthreads();
+  return r;
 }
 
 struct LevelSelArgs {
@@ -686,20 +726,26 @@ struct LevelSelArgs {
   int64_t n;
   int k, pool, region;
   int nreg, stride;  // regions of the level and the count-array stride
-  float *r_out;      // (n) k-th smallest v of the level, +inf when fewer than k
+  float *r_out;      // (n) threshold for the next level, +inf when fewer than k candidates
 };
 
-// one block per query: R_q for the next level
+// one block per query: R_q for the next level; dynamic smem kSelStage * 8
 __global__ void __launch_bounds__(kSelThreads) tc_level_select_kernel(const LevelSelArgs a) {
-  __shared__ int hist[256], s_cnt[256], s_off[256], s_misc[2], s_rank;
-  __shared__ uint32_t s_prefix;
+  extern __shared__ __align__(1024) unsigned char smem_raw[];
+  uint2 *cs = reinterpret_cast<uint2 *>(smem_raw);
+  __shared__ int hist[kSelBins], s_cnt[256], s_off[256], s_misc[2], s_bin;
+  __shared__ float s_red[96];
   const int64_t q = blockIdx.x;
   const QueryRegions R = load_regions(a.cand, a.ccount, q, a.pool, a.region, a.nreg, a.stride,
                                       s_cnt, s_off, s_misc);
   // entries lost to a full region only make R larger than it could be: still a
-  // valid bound, since R is the k-th smallest over real rows that were kept
+  // valid bound, since R is taken over real rows that were kept
   float r = INFINITY;
-  if (R.total >= a.k) r = block_kth(R, s_cnt, s_off, a.k, hist, &s_prefix, &s_rank);
+  if (R.total >= a.k) {
+    float vmin, vmax;
+    stage_candidates(R, s_cnt, s_off, cs, s_red, &vmin, &vmax);
+    r = block_kth_bound(R, s_cnt, cs, a.k, vmin, vmax, hist, s_red, &s_bin);
+  }
   if (threadIdx.x == 0) a.r_out[q] = r;
 }
 
@@ -718,13 +764,15 @@ struct SelArgs {
   int32_t *out_i;
 };
 
-// one block per query; dynamic smem: kSurvCap * 8 (survivor keys) + d * 4 (query)
+// one block per query; dynamic smem: kSelStage * 8 (staged candidates) +
+// kSurvCap * 8 (survivor keys) + d * 4 (query)
 __global__ void __launch_bounds__(kSelThreads) tc_final_select_kernel(const SelArgs a) {
   extern __shared__ __align__(1024) unsigned char smem_raw[];
-  uint64_t *keys = reinterpret_cast<uint64_t *>(smem_raw);
+  uint2 *cs = reinterpret_cast<uint2 *>(smem_raw);
+  uint64_t *keys = reinterpret_cast<uint64_t *>(cs + kSelStage);
   float *qs = reinterpret_cast<float *>(keys + kSurvCap);
-  __shared__ int hist[256], s_cnt[256], s_off[256], s_misc[2], s_rank, s_nsurv;
-  __shared__ uint32_t s_prefix;
+  __shared__ int hist[kSelBins], s_cnt[256], s_off[256], s_misc[2], s_bin, s_nsurv;
+  __shared__ float s_red[96];
   const int64_t q = blockIdx.x;
   const QueryRegions R = load_regions(a.cand, a.ccount, q, a.pool, a.region, a.nreg, a.stride,
                                       s_cnt, s_off, s_misc);
@@ -738,29 +786,27 @@ __global__ void __launch_bounds__(kSelThreads) tc_final_select_kernel(const SelA
   }
   for (int c = threadIdx.x; c < a.d; c += blockDim.x) qs[c] = a.Q[q * a.d + c];
   if (threadIdx.x == 0) s_nsurv = 0;
+  float vmin, vmax;
+  stage_candidates(R, s_cnt, s_off, cs, s_red, &vmin, &vmax);
   float theta = INFINITY;  // fewer than k candidates: keep them all
   if (R.total >= a.k)
-    theta = __fadd_ru(block_kth(R, s_cnt, s_off, a.k, hist, &s_prefix, &s_rank), a.qinfo[q].y);
+    theta = __fadd_ru(block_kth_bound(R, s_cnt, cs, a.k, vmin, vmax, hist, s_red, &s_bin),
+                      a.qinfo[q].y);
   __syncthreads();
   // survivors -> exact distance with the reference arithmetic
-  for (int rg = 0; rg < R.nreg; rg++) {
-    const uint2 *src = R.base + (size_t)rg * R.region;
-    const int c = s_cnt[rg];
-    for (int e = threadIdx.x; e < c; e += blockDim.x) {
-      const uint2 ent = src[e];
-      const float v = __uint_as_float(ent.y);
-      if (v <= theta) {
-        const int slot = atomicAdd(&s_nsurv, 1);
-        if (slot < kSurvCap) {
-          const int64_t row = ent.x;
-          const float *x = a.X + row * a.d;
-          float acc = 0.f;
-          for (int cc = 0; cc < a.d; cc++) acc = dist_step(qs[cc], x[cc], acc);
-          keys[slot] = acc == acc ? pair_key(acc, (int32_t)(a.id_offset + row)) : ~0ull;
-        }
+  for_each_candidate(R, s_cnt, cs, [&](uint2 ent) {
+    const float v = __uint_as_float(ent.y);
+    if (v <= theta) {
+      const int slot = atomicAdd(&s_nsurv, 1);
+      if (slot < kSurvCap) {
+        const int64_t row = ent.x;
+        const float *x = a.X + row * a.d;
+        float acc = 0.f;
+        for (int cc = 0; cc < a.d; cc++) acc = dist_step(qs[cc], x[cc], acc);
+        keys[slot] = acc == acc ? pair_key(acc, (int32_t)(a.id_offset + row)) : ~0ull;
       }
     }
-  }
+  });
   __syncthreads();
   const int ns = s_nsurv;
   if (ns > kSurvCap) {
@@ -980,10 +1026,13 @@ int tc_run(const float *Q, const float *X, int64_t id_offset, float *out_d, int3
   // pass 0: prep
   tc_qmax_kernel<<<592, 256, 0, stream>>>(Q, p.n * p.d, hdr);
   const unsigned groups = (unsigned)(p.x_tiles * kColGroups);  // 64-row scale groups
-  if ((p.d & 3) == 0 && p.d <= 256 && (reinterpret_cast<uintptr_t>(X) & 15) == 0)
-    tc_prep_x_kernel<true><<<groups, 256, 0, stream>>>(X, p.m, p.d, p.d_pad, Xh, xnorm, xinv, hdr);
+  const bool vec = (p.d & 3) == 0 && (reinterpret_cast<uintptr_t>(X) & 15) == 0;
+  if (vec && p.d_pad <= 128)
+    tc_prep_x_kernel<true, 1><<<groups, 256, 0, stream>>>(X, p.m, p.d, p.d_pad, Xh, xnorm, xinv, hdr);
+  else if (vec && p.d_pad <= 256)
+    tc_prep_x_kernel<true, 2><<<groups, 256, 0, stream>>>(X, p.m, p.d, p.d_pad, Xh, xnorm, xinv, hdr);
   else
-    tc_prep_x_kernel<false><<<groups, 256, 0, stream>>>(X, p.m, p.d, p.d_pad, Xh, xnorm, xinv, hdr);
+    tc_prep_x_kernel<false, 1><<<groups, 256, 0, stream>>>(X, p.m, p.d, p.d_pad, Xh, xnorm, xinv, hdr);
   tc_prep_q_kernel<<<(unsigned)(q_rows / 8), 256, 0, stream>>>(Q, p.n, p.d, p.d_pad, q_rows, Qh,
                                                                 qinfo, inv_sq, hdr);
   nl += 3;
@@ -998,6 +1047,9 @@ int tc_run(const float *Q, const float *X, int64_t id_offset, float *out_d, int3
   const size_t smem = tc_smem_bytes(p.d, p.k);
   BFK_TRY(cudaFuncSetAttribute((const void *)knn_tc_filter_kernel,
                                cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+  const size_t lsmem = (size_t)kSelStage * 8;
+  BFK_TRY(cudaFuncSetAttribute((const void *)tc_level_select_kernel,
+                               cudaFuncAttributeMaxDynamicSharedMemorySize, (int)lsmem));
   FilterArgs A{};
   A.xnorm = xnorm;
   A.xinv = xinv;
@@ -1036,7 +1088,7 @@ int tc_run(const float *Q, const float *X, int64_t id_offset, float *out_d, int3
       S.nreg = kColGroups * lv.slices;  // regions: column groups of every slice
       S.stride = kColGroups * p.max_slices;
       S.r_out = rlev;
-      tc_level_select_kernel<<<(unsigned)p.n, kSelThreads, 0, stream>>>(S);
+      tc_level_select_kernel<<<(unsigned)p.n, kSelThreads, lsmem, stream>>>(S);
       nl++;
       BFK_TRY(cudaGetLastError());
     }
@@ -1063,7 +1115,7 @@ int tc_run(const float *Q, const float *X, int64_t id_offset, float *out_d, int3
   S.hdr = hdr;
   S.out_d = out_d;
   S.out_i = out_i;
-  const size_t ssmem = (size_t)kSurvCap * 8 + (size_t)p.d * 4;
+  const size_t ssmem = (size_t)kSelStage * 8 + (size_t)kSurvCap * 8 + (size_t)p.d * 4;
   BFK_TRY(cudaFuncSetAttribute((const void *)tc_final_select_kernel,
                                cudaFuncAttributeMaxDynamicSharedMemorySize, (int)ssmem));
   tc_final_select_kernel<<<(unsigned)p.n, kSelThreads, ssmem, stream>>>(S);
