@@ -35,7 +35,8 @@ struct TcPlan {
   int64_t n, m;
   int d, k;
   int d_pad;        // d rounded up to 64 (f16 K chunks of 128 bytes)
-  int q_tiles;      // ceil(n / 128)
+  int q_tiles;      // ceil(n / 128), rounded up to even when pair
+  bool pair;        // CTA pairs issue tcgen05.mma.cta_group::2 (M = 256)
   int64_t x_tiles;  // ceil(m / 256)
   int levels;       // filter passes; the last one reads every tile
   LevelPlan level[kMaxLevels];

@@ -77,18 +77,20 @@ struct FilterArgs {
 // ---------------------------------------------------------------------------
 struct TcLayout {
   int kch, ns;
+  uint32_t bchunk;  // bytes of one row-tile K chunk in this CTA (half of it in a CTA pair)
   size_t a_off, b_off, nx_off, bar_off, total;
 };
-__host__ __device__ inline TcLayout tc_layout(int kch) {
+__host__ __device__ inline TcLayout tc_layout(int kch, bool pair) {
   TcLayout L{};
   L.kch = kch;
+  L.bchunk = pair ? kBChunkBytes / 2 : kBChunkBytes;
   L.a_off = 0;
   L.b_off = (size_t)kch * kAChunkBytes;
   const size_t fixed = (size_t)kEpiWarps * 2 * kGroupN * 4 + 256;
-  size_t ns = ((size_t)kSmemLimit - 1024 - L.b_off - fixed) / kBChunkBytes;
-  if (ns > 6) ns = 6;
+  size_t ns = ((size_t)kSmemLimit - 1024 - L.b_off - fixed) / L.bchunk;
+  if (ns > 12) ns = 12;
   L.ns = (int)ns;
-  L.nx_off = L.b_off + (size_t)L.ns * kBChunkBytes;
+  L.nx_off = L.b_off + (size_t)L.ns * L.bchunk;
   L.bar_off = L.nx_off + (size_t)kEpiWarps * 2 * kGroupN * 4;
   L.total = L.bar_off + 256 + 1024;  // + alignment slack
   return L;
@@ -121,7 +123,12 @@ __device__ __forceinline__ int64_t level_tile(const FilterArgs &a, int64_t j) {
   return a.level_tiles == a.x_tiles ? j : (j * a.x_tiles) / a.level_tiles;
 }
 
-// 576 threads in one block: the launch admits at most 96 registers a thread
+// 576 threads in one block: the launch admits at most 96 registers a thread.
+// PAIR: the kernel runs as clusters of two CTAs on two SMs.  The even CTA issues
+// tcgen05.mma.cta_group::2 with M = 256 (its query tile and its peer's) and
+// N = 256 rows, each CTA holding its query tile and half of each row tile; the
+// accumulator of each CTA's 128 queries lands in its own tensor memory.
+template <bool PAIR>
 __global__ void __maxnreg__(96)
     knn_tc_filter_kernel(const __grid_constant__ CUtensorMap tmap_q,
                          const __grid_constant__ CUtensorMap tmap_x, const FilterArgs a, int kch) {
@@ -129,7 +136,7 @@ __global__ void __maxnreg__(96)
   // align the dynamic smem base to 1024 bytes (swizzle atoms)
   unsigned char *smem = reinterpret_cast<unsigned char *>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
-  const TcLayout L = tc_layout(kch);
+  const TcLayout L = tc_layout(kch, PAIR);
   unsigned char *sA = smem + L.a_off;
   unsigned char *sB = smem + L.b_off;
   float *nxs = reinterpret_cast<float *>(smem + L.nx_off);
@@ -145,8 +152,12 @@ __global__ void __maxnreg__(96)
   volatile int *epi_stop = abort_flag + 1;  // the epilogue's copy of abort_flag, one per tile
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int qt = blockIdx.x % a.q_tiles;
-  const int s = blockIdx.x / a.q_tiles;
+  // CTA pairs: blocks (2p, 2p+1) form a cluster and take query tiles (2qp, 2qp+1)
+  const uint32_t rank = PAIR ? cluster_ctarank() : 0u;
+  const int unit = PAIR ? (int)(blockIdx.x >> 1) : (int)blockIdx.x;
+  const int units_per_slice = PAIR ? a.q_tiles / 2 : a.q_tiles;
+  const int qt = PAIR ? 2 * (unit % units_per_slice) + (int)rank : unit % units_per_slice;
+  const int s = unit / units_per_slice;
   const int64_t j_begin = (int64_t)s * a.tiles_per_slice;
   int64_t j_end = j_begin + a.tiles_per_slice;
   if (j_end > a.level_tiles) j_end = a.level_tiles;
@@ -158,19 +169,27 @@ __global__ void __maxnreg__(96)
     mbar_init(a_full, 1);
     mbar_init(acc_full, 1);
     mbar_init(acc_full + 1, 1);
-    mbar_init(acc_empty, kEpiWarps);
-    mbar_init(acc_empty + 1, kEpiWarps);
+    // both CTAs' epilogues release the pair's accumulator on the even CTA's barrier
+    mbar_init(acc_empty, PAIR ? 2 * kEpiWarps : kEpiWarps);
+    mbar_init(acc_empty + 1, PAIR ? 2 * kEpiWarps : kEpiWarps);
     mbar_init(drain, 1);
     *abort_flag = 0;
     *epi_stop = 0;
     fence_mbar_init();
   }
   if (warp == 1) {
-    tmem_alloc(tmem_slot, 512);
-    tmem_relinquish();
+    if (PAIR) {
+      tmem_alloc_pair(tmem_slot, 512);
+      tmem_relinquish_pair();
+    } else {
+      tmem_alloc(tmem_slot, 512);
+      tmem_relinquish();
+    }
   }
   tc_fence_before();
   __syncthreads();
+  // the peer signals this CTA's barriers: both must be initialised first
+  if (PAIR) cluster_sync_all();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
 
@@ -179,13 +198,18 @@ __global__ void __maxnreg__(96)
     if (lane == 0 && ntiles > 0) {
       tma_prefetch_desc(&tmap_q);
       tma_prefetch_desc(&tmap_x);
-      mbar_arrive_expect_tx(a_full, (uint32_t)(kch * kAChunkBytes));
-      for (int c = 0; c < kch; c++)
-        tma_load_2d(sA + c * kAChunkBytes, &tmap_q, a_full, c * kBK, qt * kBM);
+      // in a pair, only the even CTA arms the barriers; both CTAs' copies count on them
+      if (rank == 0) mbar_arrive_expect_tx(a_full, (uint32_t)((PAIR ? 2 : 1) * kch * kAChunkBytes));
+      for (int c = 0; c < kch; c++) {
+        if (PAIR) tma_load_2d_pair(sA + c * kAChunkBytes, &tmap_q, a_full, c * kBK, qt * kBM);
+        else tma_load_2d(sA + c * kAChunkBytes, &tmap_q, a_full, c * kBK, qt * kBM);
+      }
       uint32_t it = 0;
       bool ok = true;
+      const uint32_t bchunk = L.bchunk;
       for (int lt = 0; lt < ntiles && ok; lt++) {
-        const int32_t row0 = (int32_t)(level_tile(a, j_begin + lt) * kBN);
+        // a pair's CTAs load rows [0, 128) and [128, 256) of the tile
+        const int32_t row0 = (int32_t)(level_tile(a, j_begin + lt) * kBN) + (int32_t)(rank * (kBN / 2));
         for (int c = 0; c < kch; c++, it++) {
           const uint32_t st = it % ns, ph = (it / ns) & 1;
           if (!mbar_wait_bounded(empty + st, ph ^ 1, abort_flag)) {
@@ -193,20 +217,25 @@ __global__ void __maxnreg__(96)
             ok = false;
             break;
           }
-          mbar_arrive_expect_tx(full + st, kBChunkBytes);
-          tma_load_2d(sB + st * kBChunkBytes, &tmap_x, full + st, c * kBK, row0);
+          if (rank == 0) mbar_arrive_expect_tx(full + st, (PAIR ? 2 : 1) * bchunk);
+          if (PAIR) tma_load_2d_pair(sB + st * bchunk, &tmap_x, full + st, c * kBK, row0);
+          else tma_load_2d(sB + st * bchunk, &tmap_x, full + st, c * kBK, row0);
         }
       }
-      // every issued copy must land before the CTA may exit
-      const uint32_t first = it > (uint32_t)ns ? it - ns : 0;
-      for (uint32_t i = first; i < it; i++)
-        mbar_wait_bounded(full + (i % ns), (i / ns) & 1, abort_flag);
-      mbar_wait_bounded(a_full, 0, abort_flag);
+      // every issued copy must land before the CTA may exit; in a pair the even
+      // CTA's barriers count the peer's copies too, and the peer waits for it below
+      if (rank == 0) {
+        const uint32_t first = it > (uint32_t)ns ? it - ns : 0;
+        for (uint32_t i = first; i < it; i++)
+          mbar_wait_bounded(full + (i % ns), (i / ns) & 1, abort_flag);
+        mbar_wait_bounded(a_full, 0, abort_flag);
+      }
     }
   } else if (warp == 1) {
     // ---------------- MMA issuer ----------------
-    if (lane == 0 && ntiles > 0) {
-      constexpr uint32_t idesc = idesc_f16_f32(kBM, kBN);
+    if (lane == 0 && ntiles > 0 && rank == 0) {
+      constexpr uint32_t idesc = idesc_f16_f32(PAIR ? 2 * kBM : kBM, kBN);
+      const uint32_t bchunk = L.bchunk;
       const uint32_t a_addr = smem_u32(sA), b_addr = smem_u32(sB);
       bool ok = mbar_wait_bounded(a_full, 0, abort_flag);
       if (!ok) set_error(a.hdr, ERR_TIMEOUT_MMA, abort_flag);
@@ -231,15 +260,21 @@ __global__ void __maxnreg__(96)
 #pragma unroll
           for (int kk = 0; kk < kBK / 16; kk++) {
             const uint64_t ad = umma_desc_k_sw128(a_addr + c * kAChunkBytes + kk * 32);
-            const uint64_t bd = umma_desc_k_sw128(b_addr + st * kBChunkBytes + kk * 32);
-            tc_mma_f16(d_tmem, ad, bd, idesc, (c | kk) != 0);
+            const uint64_t bd = umma_desc_k_sw128(b_addr + st * bchunk + kk * 32);
+            if (PAIR) tc_mma_f16_pair(d_tmem, ad, bd, idesc, (c | kk) != 0);
+            else tc_mma_f16(d_tmem, ad, bd, idesc, (c | kk) != 0);
           }
-          tc_commit(empty + st);
+          if (PAIR) tc_commit_pair_mc(empty + st, 0x3);  // frees the stage in both CTAs
+          else tc_commit(empty + st);
         }
-        if (ok) tc_commit(acc_full + b);
+        if (ok) {
+          if (PAIR) tc_commit_pair_mc(acc_full + b, 0x3);  // both epilogues
+          else tc_commit(acc_full + b);
+        }
       }
       // all issued MMAs must finish before tensor memory is released
-      tc_commit(drain);
+      if (PAIR) tc_commit_pair(drain);
+      else tc_commit(drain);
       mbar_wait_bounded(drain, 0, abort_flag);
     }
   } else {
@@ -302,7 +337,10 @@ __global__ void __maxnreg__(96)
           // this warp's columns are in registers: release them to the MMA warp
           tc_fence_before();
           __syncwarp();
-          if (lane == 0) mbar_arrive(acc_empty + b);
+          if (lane == 0) {
+        if (PAIR) mbar_arrive_cluster(acc_empty + b, 0);
+        else mbar_arrive(acc_empty + b);
+      }
         } else {
           __syncwarp();  // the ||x||^2 staging written above is visible to every lane
         }
@@ -352,8 +390,13 @@ __global__ void __maxnreg__(96)
 
   tc_fence_before();
   __syncthreads();
+  // neither CTA of a pair leaves while the pair's MMAs may still touch its memory
+  if (PAIR) cluster_sync_all();
   tc_fence_after();
-  if (warp == 1) tmem_dealloc(tmem_base, 512);
+  if (warp == 1) {
+    if (PAIR) tmem_dealloc_pair(tmem_base, 512);
+    else tmem_dealloc(tmem_base, 512);
+  }
 }
 
 // ---------------------------------------------------------------------------
@@ -860,13 +903,13 @@ static int kch_for(int d) { return (d + kBK - 1) / kBK; }
 
 bool tc_supported(int d, int k) {
   if (d <= 0 || d > kMaxKch * kBK || k <= 0 || k > kTcMaxK) return false;
-  const TcLayout L = tc_layout(kch_for(d));
+  const TcLayout L = tc_layout(kch_for(d), false);
   return L.ns >= 2 && L.total <= (size_t)kSmemLimit;
 }
 
-size_t tc_smem_bytes(int d, int) { return tc_layout(kch_for(d)).total; }
+size_t tc_smem_bytes(int d, int) { return tc_layout(kch_for(d), true).total; }
 
-const void *tc_kernel_ptr(int, int) { return (const void *)knn_tc_filter_kernel; }
+const void *tc_kernel_ptr(int, int) { return (const void *)knn_tc_filter_kernel<true>; }
 
 int tc_threads() { return kTcThreads; }
 
@@ -905,6 +948,9 @@ bool tc_make_plan(int64_t n, int64_t m, int d, int k, int slices, int pool, TcPl
   P.k = k;
   P.d_pad = kch_for(d) * kBK;
   P.q_tiles = (int)((n + kBM - 1) / kBM);
+  // CTA pairs (M = 256) once there are two query tiles; the tile count is then even
+  P.pair = P.q_tiles >= 2;
+  if (P.pair) P.q_tiles += P.q_tiles & 1;
   P.x_tiles = (m + kBN - 1) / kBN;
   P.cand_cap = pool > 0 ? pool : kDefaultPool;
   if (P.cand_cap < 2 * k) P.cand_cap = 2 * k;
@@ -931,6 +977,7 @@ bool tc_make_plan(int64_t n, int64_t m, int d, int k, int slices, int pool, TcPl
     LevelPlan &lv = P.level[l];
     lv.tiles = sizes[nl - 1 - l];
     const bool last = l == nl - 1;
+    // slices fill the SMs with CTAs (a pair counts as two)
     int s = (last && slices > 0) ? slices : choose_slices(P.q_tiles, lv.tiles, sms, 64);
     if (s > lv.tiles) s = (int)lv.tiles;
     if (s < 1) s = 1;
@@ -1039,14 +1086,17 @@ int tc_run(const float *Q, const float *X, int64_t id_offset, float *out_d, int3
   BFK_TRY(cudaGetLastError());
 
   CUtensorMap tq, tx;
-  if (!make_tmap(&tq, Qh, q_rows, p.d_pad, kBM) || !make_tmap(&tx, Xh, p.m, p.d_pad, kBN)) {
+  // a CTA of a pair loads half of every row tile
+  if (!make_tmap(&tq, Qh, q_rows, p.d_pad, kBM) ||
+      !make_tmap(&tx, Xh, p.m, p.d_pad, p.pair ? kBN / 2 : kBN)) {
     BFK_NOTE(cudaErrorInvalidValue, "cuTensorMapEncodeTiled");
     return 1;
   }
   const int kch = p.d_pad / kBK;
-  const size_t smem = tc_smem_bytes(p.d, p.k);
-  BFK_TRY(cudaFuncSetAttribute((const void *)knn_tc_filter_kernel,
-                               cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+  const size_t smem = tc_layout(kch, p.pair).total;
+  const void *filter = p.pair ? (const void *)knn_tc_filter_kernel<true>
+                              : (const void *)knn_tc_filter_kernel<false>;
+  BFK_TRY(cudaFuncSetAttribute(filter, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
   const size_t lsmem = (size_t)kSelStage * 8;
   BFK_TRY(cudaFuncSetAttribute((const void *)tc_level_select_kernel,
                                cudaFuncAttributeMaxDynamicSharedMemorySize, (int)lsmem));
@@ -1072,8 +1122,24 @@ int tc_run(const float *Q, const float *X, int64_t id_offset, float *out_d, int3
     A.tiles_per_slice = (int)lv.tiles_per_slice;
     A.region = lv.region;
     if (last && t0) cudaEventRecord(t0, stream);
-    knn_tc_filter_kernel<<<(unsigned)(p.q_tiles * lv.slices), kTcThreads, smem, stream>>>(tq, tx,
-                                                                                          A, kch);
+    if (p.pair) {
+      cudaLaunchConfig_t cfg = {};
+      cfg.gridDim = dim3((unsigned)(p.q_tiles * lv.slices));
+      cfg.blockDim = dim3(kTcThreads);
+      cfg.dynamicSmemBytes = smem;
+      cfg.stream = stream;
+      cudaLaunchAttribute attr[1];
+      attr[0].id = cudaLaunchAttributeClusterDimension;
+      attr[0].val.clusterDim.x = 2;
+      attr[0].val.clusterDim.y = 1;
+      attr[0].val.clusterDim.z = 1;
+      cfg.attrs = attr;
+      cfg.numAttrs = 1;
+      BFK_TRY(cudaLaunchKernelEx(&cfg, knn_tc_filter_kernel<true>, tq, tx, A, kch));
+    } else {
+      knn_tc_filter_kernel<false><<<(unsigned)(p.q_tiles * lv.slices), kTcThreads, smem, stream>>>(
+          tq, tx, A, kch);
+    }
     if (last && t1) cudaEventRecord(t1, stream);
     nl++;
     BFK_TRY(cudaGetLastError());
