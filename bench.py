@@ -49,6 +49,8 @@ def parse_args(argv=None):
     ap.add_argument("--rows", type=int, default=None, help="override the database size")
     ap.add_argument("--queries", type=int, default=None, help="override the query count")
     ap.add_argument("--engine", default="auto", choices=["auto", "direct", "tc_f16"])
+    ap.add_argument("--cta-pair", action="store_true",
+                    help="TC engine: CTA pairs (tcgen05.mma.cta_group::2)")
     ap.add_argument("--cpu-sample", type=int, default=32,
                     help="queries in the bounded CPU-baseline sample")
     ap.add_argument("--no-cpu-baseline", action="store_true")
@@ -200,7 +202,8 @@ def main(argv=None) -> int:
     torch.cuda.synchronize()
 
     def local_search(Q_, X_, k_, id_offset, time_main=False):
-        return engine.search(Q_, X_, k_, engine=a.engine, id_offset=id_offset, time_main=time_main)
+        return engine.search(Q_, X_, k_, engine=a.engine, id_offset=id_offset, time_main=time_main,
+                             cta_pair=a.cta_pair)
 
     def step(time_main=False):
         return sharded_search(Qd, Xd, k, r0,

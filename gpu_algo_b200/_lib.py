@@ -129,6 +129,7 @@ def check(status: int, what: str) -> None:
 
 
 FLAG_TIME_MAIN = 1
+FLAG_CTA_PAIR = 2
 
 
 def make_opts(engine: str | int = "auto", slices: int = 0, max_candidates: int = 0,

@@ -50,7 +50,8 @@ struct TcPlan {
   int fb_slices;
 };
 bool tc_supported(int d, int k);
-bool tc_make_plan(int64_t n, int64_t m, int d, int k, int slices, int cand_cap, TcPlan *p);
+bool tc_make_plan(int64_t n, int64_t m, int d, int k, int slices, int cand_cap, bool pair,
+                  TcPlan *p);
 // Returns 0 ok, 1 CUDA error, 2 device timeout.  t0/t1 (may be null) are
 // recorded around the main kernel; *launches counts the kernels launched.
 int tc_run(const float *Q, const float *X, int64_t id_offset, float *out_d, int32_t *out_i,

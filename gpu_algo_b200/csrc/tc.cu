@@ -956,7 +956,7 @@ static int choose_slices(int q_tiles, int64_t tiles, int sms, int max_s) {
   return best;
 }
 
-bool tc_make_plan(int64_t n, int64_t m, int d, int k, int slices, int pool, TcPlan *p) {
+bool tc_make_plan(int64_t n, int64_t m, int d, int k, int slices, int pool, bool pair, TcPlan *p) {
   if (!tc_supported(d, k) || n <= 0 || m <= 0) return false;
   TcPlan P{};
   P.n = n;
@@ -965,8 +965,8 @@ bool tc_make_plan(int64_t n, int64_t m, int d, int k, int slices, int pool, TcPl
   P.k = k;
   P.d_pad = kch_for(d) * kBK;
   P.q_tiles = (int)((n + kBM - 1) / kBM);
-  // CTA pairs (M = 256) once there are two query tiles; the tile count is then even
-  P.pair = P.q_tiles >= 2;
+  // CTA pairs (M = 256) on request, given two query tiles; the tile count is then even
+  P.pair = pair && P.q_tiles >= 2;
   if (P.pair) P.q_tiles += P.q_tiles & 1;
   P.x_tiles = (m + kBN - 1) / kBN;
   P.cand_cap = pool > 0 ? pool : kDefaultPool;

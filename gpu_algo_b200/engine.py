@@ -57,7 +57,7 @@ def workspace_size(n: int, m: int, d: int, k: int, opts: _lib.Opts) -> int:
 
 def search(Q, X, k: int, *, engine: str = "auto", slices: int = 0, max_candidates: int = 0,
            id_offset: int = 0, out: tuple[torch.Tensor, torch.Tensor] | None = None,
-           ws: torch.Tensor | None = None, time_main: bool = False):
+           ws: torch.Tensor | None = None, time_main: bool = False, cta_pair: bool = False):
     """Exact k-NN on the GPU.  Returns (dists, ids) device tensors."""
     Q = as_device_f32(Q, "Q")
     X = as_device_f32(X, "X")
@@ -72,7 +72,8 @@ def search(Q, X, k: int, *, engine: str = "auto", slices: int = 0, max_candidate
         raise ValueError("k must be positive")
     lib = _lib.load()
     opts = _lib.make_opts(engine, slices, max_candidates,
-                          _lib.FLAG_TIME_MAIN if time_main else 0)
+                          (_lib.FLAG_TIME_MAIN if time_main else 0) |
+                          (_lib.FLAG_CTA_PAIR if cta_pair else 0))
     with torch.cuda.device(Q.device):
         stream = torch.cuda.current_stream()
         if out is None:

@@ -49,6 +49,7 @@ typedef enum {
 } bfk_engine_t;
 
 #define BFK_FLAG_TIME_MAIN 1 /* time the main kernel of every call with CUDA events      */
+#define BFK_FLAG_CTA_PAIR 2  /* TC engine: CTA pairs (tcgen05.mma.cta_group::2, M = 256)  */
 
 typedef struct {
   int32_t engine;         /* bfk_engine_t                                                */

@@ -184,3 +184,14 @@ def test_bf_dropin_runners(plumbing):
     torch.cuda.synchronize()
     np.testing.assert_array_equal(out_ids.cpu().numpy(), gi[:200])
     assert attrs["num_regs"] > 0 and "kernel_variant" in attrs
+
+
+def test_tc_cta_pair_bit_exact(plumbing):
+    X, Q, gd, gi = plumbing
+    d_, i_ = engine.search(dev(Q), dev(X), 10, engine="tc_f16", cta_pair=True)
+    torch.cuda.synchronize()
+    assert_exact(d_.cpu().numpy(), i_.cpu().numpy(), gd, gi, "cta pair")
+    # an odd number of query tiles pads the pair with an empty tile
+    d_, i_ = engine.search(dev(Q[:300]), dev(X), 10, engine="tc_f16", cta_pair=True)
+    torch.cuda.synchronize()
+    assert_exact(d_.cpu().numpy(), i_.cpu().numpy(), gd[:300], gi[:300], "cta pair, 3 tiles")
