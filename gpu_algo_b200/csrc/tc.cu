@@ -86,12 +86,12 @@ __host__ __device__ inline TcLayout tc_layout(int kch, bool pair) {
   L.bchunk = pair ? kBChunkBytes / 2 : kBChunkBytes;
   L.a_off = 0;
   L.b_off = (size_t)kch * kAChunkBytes;
-  const size_t fixed = (size_t)kEpiWarps * 2 * (kGroupN + 8) * 4 + 256;
+  const size_t fixed = (size_t)kEpiWarps * 2 * kGroupN * 4 + 256;
   size_t ns = ((size_t)kSmemLimit - 1024 - L.b_off - fixed) / L.bchunk;
   if (ns > 12) ns = 12;
   L.ns = (int)ns;
   L.nx_off = L.b_off + (size_t)L.ns * L.bchunk;
-  L.bar_off = L.nx_off + (size_t)kEpiWarps * 2 * (kGroupN + 8) * 4;
+  L.bar_off = L.nx_off + (size_t)kEpiWarps * 2 * kGroupN * 4;
   L.total = L.bar_off + 256 + 1024;  // + alignment slack
   return L;
 }
@@ -112,22 +112,11 @@ __device__ __forceinline__ void fma2(float a0, float a1, float c, float b0, floa
   asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(pd) : "l"(pa), "l"(pc), "l"(pb));
   asm("mov.b64 {%0, %1}, %2;" : "=f"(d0), "=f"(d1) : "l"(pd));
 }
-// three-input minimum / maximum (NaN inputs are ignored, as by fminf / fmaxf)
+// three-input minimum (NaN inputs are ignored, as by fminf)
 __device__ __forceinline__ float min3f(float a, float b, float c) {
   float d;
   asm("min.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
   return d;
-}
-__device__ __forceinline__ float max3f(float a, float b, float c) {
-  float d;
-  asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
-  return d;
-}
-// max over 8 accumulator values (raw FP32 bits)
-__device__ __forceinline__ float max8u(const uint32_t *a) {
-  return max3f(max3f(__uint_as_float(a[0]), __uint_as_float(a[1]), __uint_as_float(a[2])),
-               max3f(__uint_as_float(a[3]), __uint_as_float(a[4]), __uint_as_float(a[5])),
-               fmaxf(__uint_as_float(a[6]), __uint_as_float(a[7])));
 }
 
 __device__ __forceinline__ int64_t level_tile(const FilterArgs &a, int64_t j) {
@@ -307,7 +296,6 @@ __global__ void __maxnreg__(96)
     const uint32_t taddr0 = tmem_base + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(cg * kGroupN);
     const float inv_sq = *a.inv_sq;
     float *nxw = nxs + e * 2 * kGroupN;       // this warp's ||x||^2 staging, two buffers
-    float *gnw = nxs + kEpiWarps * 2 * kGroupN + e * 2 * 8;  // per-group minimum ||x||^2
     // prefetch ||x||^2 (2 rows per lane) and the block scale of the first tile
     float2 pre_nx = make_float2(0.f, 0.f);
     float pre_inv = 1.f;
@@ -324,13 +312,7 @@ __global__ void __maxnreg__(96)
       if (__any_sync(0xffffffffu, *abort_flag != 0)) break;
       float *nxt = nxw + b * kGroupN;
       *reinterpret_cast<float2 *>(nxt + lane * 2) = pre_nx;
-      // minimum ||x||^2 of each group of 8 columns (lanes 4g .. 4g+3 hold group g)
-      float gm = fminf(pre_nx.x, pre_nx.y);
-      gm = fminf(gm, __shfl_xor_sync(0xffffffffu, gm, 1));
-      gm = fminf(gm, __shfl_xor_sync(0xffffffffu, gm, 2));
-      float *gnt = gnw + b * 8;
-      if ((lane & 3) == 0) gnt[lane >> 2] = gm;
-      const float cscale = -2.0f * inv_sq * pre_inv;  // exact power of two, negative
+      const float cscale = -2.0f * inv_sq * pre_inv;  // exact power of two
       if (lt + 1 < ntiles) {
         const int64_t tn = level_tile(a, j_begin + lt + 1);
         pre_nx = *reinterpret_cast<const float2 *>(a.xnorm + tn * kBN + cg * kGroupN + lane * 2);
@@ -344,57 +326,58 @@ __global__ void __maxnreg__(96)
         break;
       }
       tc_fence_after();
-      uint32_t va[32], vb[32];
-      tmem_ld_32x32b_x32(taddr0 + (uint32_t)(b * kBN), va);
-      tmem_ld_32x32b_x32(taddr0 + (uint32_t)(b * kBN + 32), vb);
-      tmem_ld_wait();
-      // this warp's columns are in registers: release them to the MMA warp
-      tc_fence_before();
-      __syncwarp();  // also publishes the ||x||^2 staging to every lane
-      if (lane == 0) {
+      const uint32_t row0 = (uint32_t)(tile * kBN + cg * kGroupN);
+#pragma unroll 1
+      for (int hh = 0; hh < 2; hh++) {
+        // 32 columns at a time keeps the register footprint small (18 warps share the file)
+        uint32_t va[32];
+        tmem_ld_32x32b_x32(taddr0 + (uint32_t)(b * kBN + hh * 32), va);
+        tmem_ld_wait();
+        if (hh == 1) {
+          // this warp's columns are in registers: release them to the MMA warp
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) {
         if (PAIR) mbar_arrive_cluster(acc_empty + b, 0);
         else mbar_arrive(acc_empty + b);
       }
-      // Group bound: cscale < 0, so cscale * max(acc) + min ||x||^2 <= every
-      // v = cscale * acc + ||x||^2 of the group, exactly and after rounding
-      // (fused multiply-add rounds monotonically).  A group whose bound exceeds
-      // theta holds no candidate.
-      const float4 gn0 = reinterpret_cast<const float4 *>(gnt)[0];
-      const float4 gn1 = reinterpret_cast<const float4 *>(gnt)[1];
-      float gb[8];
-      gb[0] = __fmaf_rn(cscale, max8u(va), gn0.x);
-      gb[1] = __fmaf_rn(cscale, max8u(va + 8), gn0.y);
-      gb[2] = __fmaf_rn(cscale, max8u(va + 16), gn0.z);
-      gb[3] = __fmaf_rn(cscale, max8u(va + 24), gn0.w);
-      gb[4] = __fmaf_rn(cscale, max8u(vb), gn1.x);
-      gb[5] = __fmaf_rn(cscale, max8u(vb + 8), gn1.y);
-      gb[6] = __fmaf_rn(cscale, max8u(vb + 16), gn1.z);
-      gb[7] = __fmaf_rn(cscale, max8u(vb + 24), gn1.w);
-      const float all = min3f(min3f(gb[0], gb[1], gb[2]), min3f(gb[3], gb[4], gb[5]),
-                              fminf(gb[6], gb[7]));
-      if (__any_sync(0xffffffffu, all <= theta)) {
-        const uint32_t row0 = (uint32_t)(tile * kBN + cg * kGroupN);
-        const float4 *nx4 = reinterpret_cast<const float4 *>(nxt);
+        } else {
+          __syncwarp();  // the ||x||^2 staging written above is visible to every lane
+        }
+        // v = acc * cscale + ||x||^2, two columns per packed FMA
+        float v[32];
+        const float4 *nx4 = reinterpret_cast<const float4 *>(nxt + hh * 32);
 #pragma unroll
-        for (int g = 0; g < 8; g++) {
-          if (__any_sync(0xffffffffu, gb[g] <= theta)) {
-            // exact values of the group's columns
-            const uint32_t *acc = g < 4 ? va + 8 * g : vb + 8 * (g - 4);
-            const float4 n0 = nx4[2 * g], n1 = nx4[2 * g + 1];
-            float v[8];
-            fma2(__uint_as_float(acc[0]), __uint_as_float(acc[1]), cscale, n0.x, n0.y, v[0], v[1]);
-            fma2(__uint_as_float(acc[2]), __uint_as_float(acc[3]), cscale, n0.z, n0.w, v[2], v[3]);
-            fma2(__uint_as_float(acc[4]), __uint_as_float(acc[5]), cscale, n1.x, n1.y, v[4], v[5]);
-            fma2(__uint_as_float(acc[6]), __uint_as_float(acc[7]), cscale, n1.z, n1.w, v[6], v[7]);
+        for (int i = 0; i < 8; i++) {
+          const float4 nx = nx4[i];
+          fma2(__uint_as_float(va[4 * i]), __uint_as_float(va[4 * i + 1]), cscale, nx.x, nx.y,
+               v[4 * i], v[4 * i + 1]);
+          fma2(__uint_as_float(va[4 * i + 2]), __uint_as_float(va[4 * i + 3]), cscale, nx.z, nx.w,
+               v[4 * i + 2], v[4 * i + 3]);
+        }
+        // minimum of each group of 8 columns (three-input min)
+        float gmin[4];
 #pragma unroll
-            for (int i = 0; i < 8; i++) {
-              // one ballot per column; the append runs only for columns some lane keeps
-              const unsigned keep = __ballot_sync(0xffffffffu, v[i] <= theta);
-              if (keep) {
-                const bool mine = (keep >> lane) & 1u;
-                if (mine)
-                  region[min(cnt, last)] = make_uint2(row0 + 8 * g + i, __float_as_uint(v[i]));
-                cnt += mine ? 1 : 0;
+        for (int g = 0; g < 4; g++) {
+          const float *w = v + 8 * g;
+          gmin[g] = min3f(min3f(w[0], w[1], w[2]), min3f(w[3], w[4], w[5]), fminf(w[6], w[7]));
+        }
+        const float all = fminf(min3f(gmin[0], gmin[1], gmin[2]), gmin[3]);
+        if (__any_sync(0xffffffffu, all <= theta)) {
+#pragma unroll
+          for (int g = 0; g < 4; g++) {
+            if (__any_sync(0xffffffffu, gmin[g] <= theta)) {
+#pragma unroll
+              for (int i = 0; i < 8; i++) {
+                // one ballot per column; the append runs only for columns some lane keeps
+                const float vi = v[8 * g + i];
+                const unsigned keep = __ballot_sync(0xffffffffu, vi <= theta);
+                if (keep) {
+                  const bool mine = (keep >> lane) & 1u;
+                  if (mine)
+                    region[min(cnt, last)] = make_uint2(row0 + hh * 32 + 8 * g + i, __float_as_uint(vi));
+                  cnt += mine ? 1 : 0;
+                }
               }
             }
           }
