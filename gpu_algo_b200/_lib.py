@@ -38,6 +38,7 @@ EXPORTS = (
     "bfk_merge",
     "bfk_kernel_attrs",
     "bfk_search_stats",
+    "bfk_search_noalloc",
 )
 
 
@@ -109,6 +110,8 @@ def load() -> ctypes.CDLL:
         lib.bfk_merge.argtypes = [vp, vp, i64, i32, i32, vp, vp, vp]
         lib.bfk_kernel_attrs.restype = i32
         lib.bfk_kernel_attrs.argtypes = [i32, i32, i32, ctypes.POINTER(Attrs)]
+        lib.bfk_search_noalloc.restype = i32
+        lib.bfk_search_noalloc.argtypes = [vp, i64, vp, i64, i32, i32, i64, vp, vp, vp]
         lib.bfk_search_stats.restype = i32
         lib.bfk_search_stats.argtypes = [vp, i64, i64, i32, i32, ctypes.POINTER(Opts), vp,
                                          ctypes.POINTER(Stats)]

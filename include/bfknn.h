@@ -145,6 +145,25 @@ BFK_API bfk_status_t bfk_kernel_attrs(int32_t engine, int32_t d, int32_t k, bfk_
 BFK_API bfk_status_t bfk_search_stats(const void *workspace, int64_t n, int64_t m, int32_t d, int32_t k,
                               const bfk_opts_t *opts, void *stream, bfk_stats_t *out);
 
+/*
+ * Exact k-NN like bfk_search (exact SIMT engine) for callers that cannot
+ * allocate device memory at search time (inside another allocator's callback,
+ * on a real-time thread that must not block on cudaMalloc, or with only fixed
+ * pre-registered buffers).  No counterpart in the reference.
+ *
+ * It takes no workspace: its scratch is a 16 MiB array inside the library that
+ * every GPU loading the library holds until exit.  Requires
+ * 16 * n * k <= 16 MiB - 256 bytes (n * k <= 1,048,560); larger shapes return
+ * BFK_ERR_UNSUPPORTED.  It allocates nothing.  The first call on each device
+ * looks the array's device address up (cudaGetSymbolAddress); make that first
+ * call outside any stream capture.  All calls share the array: calls that
+ * overlap on the GPU (other streams or threads) race and must be serialised by
+ * the caller.
+ */
+BFK_API bfk_status_t bfk_search_noalloc(const float *Q, int64_t n, const float *X, int64_t m,
+                                        int32_t d, int32_t k, int64_t id_offset,
+                                        float *out_dists, int32_t *out_ids, void *stream);
+
 #ifdef __cplusplus
 }
 #endif
