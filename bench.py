@@ -201,13 +201,12 @@ def main(argv=None) -> int:
     Qd = torch.from_numpy(Q).to(device)
     torch.cuda.synchronize()
 
-    def local_search(Q_, X_, k_, id_offset, time_main=False):
-        return engine.search(Q_, X_, k_, engine=a.engine, id_offset=id_offset, time_main=time_main,
-                             cta_pair=a.cta_pair)
+    # every rank plans its sampling levels for the largest shard
+    plan_rows = shard_range(N, 0, world)[1] - shard_range(N, 0, world)[0]
 
-    def step(time_main=False):
-        return sharded_search(Qd, Xd, k, r0,
-                              local_search=lambda q, x, kk, off: local_search(q, x, kk, off, time_main))
+    def step(time_main=False, Q_=None):
+        return sharded_search(Qd if Q_ is None else Q_, Xd, k, r0, plan_rows=plan_rows,
+                              engine=a.engine, time_main=time_main, cta_pair=a.cta_pair)
 
     def barrier():
         if world > 1:
@@ -250,8 +249,7 @@ def main(argv=None) -> int:
 
         def e2e_step():
             Qd2.copy_(Qh, non_blocking=True)
-            dd, ii = sharded_search(Qd2, Xd, k, r0,
-                                    local_search=lambda q, x, kk, off: local_search(q, x, kk, off))
+            dd, ii = step(Q_=Qd2)
             out_d.copy_(dd, non_blocking=True)
             out_i.copy_(ii, non_blocking=True)
 

@@ -64,7 +64,8 @@ bool opts_ok(const bfk_opts_t *o) {
   for (int i = 0; i < 4; i++)
     if (o->reserved[i] != 0) return false;
   return o->engine >= BFK_ENGINE_AUTO && o->engine <= BFK_ENGINE_TC_F16 && o->slices >= 0 &&
-         o->max_candidates >= 0 && (o->flags & ~(BFK_FLAG_TIME_MAIN | BFK_FLAG_CTA_PAIR)) == 0;
+         o->max_candidates >= 0 && o->plan_rows >= 0 &&
+         (o->flags & ~(BFK_FLAG_TIME_MAIN | BFK_FLAG_CTA_PAIR)) == 0;
 }
 
 int choose_engine(int64_t n, int64_t m, int d, int k, const bfk_opts_t *o) {
@@ -170,7 +171,8 @@ bfk_status_t bfk_workspace_size(int64_t n, int64_t m, int32_t d, int32_t k,
   if (eng == BFK_ENGINE_TC_F16) {
     if (!tc_supported(d, k)) return BFK_ERR_UNSUPPORTED;
     TcPlan p;
-    if (!tc_make_plan(n, m, d, k, opts ? opts->slices : 0, opts ? opts->max_candidates : 0, opts && (opts->flags & BFK_FLAG_CTA_PAIR), &p))
+    if (!tc_make_plan(n, m, d, k, opts ? opts->slices : 0, opts ? opts->max_candidates : 0, opts && (opts->flags & BFK_FLAG_CTA_PAIR),
+                      opts ? opts->plan_rows : 0, &p))
       return BFK_ERR_UNSUPPORTED;
     *bytes = p.total;
   } else {
@@ -203,10 +205,12 @@ bfk_status_t bfk_search(const float *Q, int64_t n, const float *X, int64_t m, in
   if (eng == BFK_ENGINE_TC_F16) {
     if (!tc_supported(d, k)) return BFK_ERR_UNSUPPORTED;
     TcPlan p;
-    if (!tc_make_plan(n, m, d, k, opts ? opts->slices : 0, opts ? opts->max_candidates : 0, opts && (opts->flags & BFK_FLAG_CTA_PAIR), &p))
+    if (!tc_make_plan(n, m, d, k, opts ? opts->slices : 0, opts ? opts->max_candidates : 0, opts && (opts->flags & BFK_FLAG_CTA_PAIR),
+                      opts ? opts->plan_rows : 0, &p))
       return BFK_ERR_UNSUPPORTED;
     if (workspace_bytes < p.total) return BFK_ERR_WORKSPACE;
-    int rc = tc_run(Q, X, id_offset, out_dists, out_ids, ws, p, stream, t0, t1, &g_calls.launches);
+    int rc = tc_run(Q, X, id_offset, out_dists, out_ids, ws, p, stream, t0, t1, &g_calls.launches,
+                    opts ? opts->level_hook : nullptr, opts ? opts->hook_user : nullptr);
     if (rc == 1) return BFK_ERR_CUDA;
     if (rc == 2) return BFK_ERR_DEVICE_TIMEOUT;
     return BFK_OK;
@@ -319,7 +323,8 @@ bfk_status_t bfk_search_stats(const void *workspace, int64_t n, int64_t m, int32
   out->main_kernel_ms = total;
   if (eng == BFK_ENGINE_TC_F16) {
     TcPlan p;
-    if (tc_make_plan(n, m, d, k, opts ? opts->slices : 0, opts ? opts->max_candidates : 0, opts && (opts->flags & BFK_FLAG_CTA_PAIR), &p))
+    if (tc_make_plan(n, m, d, k, opts ? opts->slices : 0, opts ? opts->max_candidates : 0, opts && (opts->flags & BFK_FLAG_CTA_PAIR),
+                      opts ? opts->plan_rows : 0, &p))
       out->slices = p.slices;
   } else {
     out->slices = direct_plan(n, m, d, k, opts ? opts->slices : 0).slices;

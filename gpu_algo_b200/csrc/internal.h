@@ -51,12 +51,13 @@ struct TcPlan {
 };
 bool tc_supported(int d, int k);
 bool tc_make_plan(int64_t n, int64_t m, int d, int k, int slices, int cand_cap, bool pair,
-                  TcPlan *p);
+                  int64_t plan_rows, TcPlan *p);
 // Returns 0 ok, 1 CUDA error, 2 device timeout.  t0/t1 (may be null) are
 // recorded around the main kernel; *launches counts the kernels launched.
+typedef void (*LevelHook)(float *bound, int64_t n, void *user, void *stream);
 int tc_run(const float *Q, const float *X, int64_t id_offset, float *out_d, int32_t *out_i,
            void *ws, const TcPlan &p, cudaStream_t stream, cudaEvent_t t0, cudaEvent_t t1,
-           int *launches);
+           int *launches, LevelHook hook, void *hook_user);
 const void *tc_kernel_ptr(int d, int k);
 size_t tc_smem_bytes(int d, int k);
 int tc_threads();

@@ -59,7 +59,7 @@ struct FilterArgs {
   const float *xinv;     // (x_tiles * 4) 1/scale of each 64-row group
   const float2 *qinfo;   // (q_tiles*128) (||q||^2, 2*margin); NaN margin for padding rows
   const float *inv_sq;   // 1/scale of the queries (device scalar)
-  const float *r_in;     // (n) threshold of the previous level, null = +inf
+  const float *r_in;     // (n) bound B of the previous level (B + margin), null = none
   int64_t n;
   int64_t x_tiles;       // tiles of the whole database
   int64_t level_tiles;   // tiles of this level (evenly spaced over the database)
@@ -285,10 +285,11 @@ __global__ void __maxnreg__(96)
     const int r = quarter * 32 + lane;        // query row within the tile
     const int64_t q = (int64_t)qt * kBM + r;
     const bool valid = q < a.n;
-    const float m2 = a.qinfo[(size_t)qt * kBM + r].y;
-    // rows past m carry ||x||^2 = +inf, so theta stays finite: FLT_MAX when there is no bound yet
+    const float margin = a.qinfo[(size_t)qt * kBM + r].y;
+    // theta = B + margin, B = (k-th smallest v of the previous level) + margin, rounded up.
+    // Rows past m carry ||x||^2 = +inf, so theta stays finite: FLT_MAX when there is no bound.
     float theta = -INFINITY;
-    if (valid) theta = a.r_in ? fminf(__fadd_ru(a.r_in[q], m2), FLT_MAX) : FLT_MAX;
+    if (valid) theta = a.r_in ? fminf(__fadd_ru(a.r_in[q], margin), FLT_MAX) : FLT_MAX;
     uint2 *region = a.cand + (size_t)(valid ? q : 0) * a.pool +
                     (size_t)(kColGroups * s + cg) * a.region;
     const int last = a.region - 1;            // a full region keeps overwriting its last slot
@@ -530,7 +531,7 @@ __global__ void tc_qmax_kernel(const float *__restrict__ Q, int64_t count, WsHea
 }
 
 // grid (q_rows / 8), block 256: one warp per query row.  Writes the f16 query
-// tile rows (zero for padding rows), ||q||^2 and twice the error margin.
+// tile rows (zero for padding rows), ||q||^2 and the error margin.
 __global__ void __launch_bounds__(256) tc_prep_q_kernel(const float *__restrict__ Q, int64_t n,
                                                         int d, int d_pad, int64_t q_rows,
                                                         __half *__restrict__ Qh,
@@ -567,7 +568,7 @@ __global__ void __launch_bounds__(256) tc_prep_q_kernel(const float *__restrict_
     //   accumulation  <= (d_pad + 16) 2^-22 (qn + e_q)(Rx + e_x)   (tensor-core FP32 sums)
     //   FP32 terms    <= 2 (d + 8) 2^-24 (qn + Rx)^2  (norms, the fused epilogue step,
     //                                                  and the reference's own rounding)
-    //   margin = 2 (dot rounding + accumulation) + FP32 terms;  stored: 2 * margin.
+    //   margin = 2 (dot rounding + accumulation) + FP32 terms.
     // Then |(||q||^2 + v) - D| <= margin for every row, v the epilogue value and D
     // the reference kernel's FP32 distance.
     const double u = 1.0 / 2048.0;
@@ -580,7 +581,7 @@ __global__ void __launch_bounds__(256) tc_prep_q_kernel(const float *__restrict_
     const double acc = (double)(d_pad + 16) * ldexp(1.0, -22) * (qn + eq) * (rx + ex);
     const double f32 = 2.0 * (double)(d + 8) * ldexp(1.0, -24) * (qn + rx) * (qn + rx);
     const double margin = 2.0 * (dotr + acc) + f32;
-    qinfo[row] = make_float2(ss, __double2float_ru(2.0 * margin * (1.0 + 1e-6)));
+    qinfo[row] = make_float2(ss, __double2float_ru(margin * (1.0 + 1e-6)));
   }
 }
 
@@ -766,10 +767,11 @@ __device__ float block_kth_bound(const QueryRegions &R, const int *s_cnt, const 
 struct LevelSelArgs {
   const uint2 *cand;
   const int *ccount;
+  const float2 *qinfo;
   int64_t n;
   int k, pool, region;
   int nreg, stride;  // regions of the level and the count-array stride
-  float *r_out;      // (n) threshold for the next level, +inf when fewer than k candidates
+  float *r_out;      // (n) bound B = R + margin for the next level, +inf when fewer than k
 };
 
 // one block per query: R_q for the next level; dynamic smem kSelStage * 8
@@ -789,7 +791,9 @@ __global__ void __launch_bounds__(kSelThreads) tc_level_select_kernel(const Leve
     stage_candidates(R, s_cnt, s_off, cs, s_red, &vmin, &vmax);
     r = block_kth_bound(R, s_cnt, cs, a.k, vmin, vmax, hist, s_red, &s_bin);
   }
-  if (threadIdx.x == 0) a.r_out[q] = r;
+  // B = R + margin bounds the k-th reference distance minus ||q||^2 from above; it is
+  // what other shards of a sharded search may share (their minimum stays a bound)
+  if (threadIdx.x == 0) a.r_out[q] = __fadd_ru(r, a.qinfo[q].y);
 }
 
 struct SelArgs {
@@ -833,7 +837,8 @@ __global__ void __launch_bounds__(kSelThreads) tc_final_select_kernel(const SelA
   stage_candidates(R, s_cnt, s_off, cs, s_red, &vmin, &vmax);
   float theta = INFINITY;  // fewer than k candidates: keep them all
   if (R.total >= a.k)
-    theta = __fadd_ru(block_kth_bound(R, s_cnt, cs, a.k, vmin, vmax, hist, s_red, &s_bin),
+    theta = __fadd_ru(__fadd_ru(block_kth_bound(R, s_cnt, cs, a.k, vmin, vmax, hist, s_red, &s_bin),
+                                a.qinfo[q].y),
                       a.qinfo[q].y);
   __syncthreads();
   // survivors -> exact distance with the reference arithmetic
@@ -939,7 +944,8 @@ static int choose_slices(int q_tiles, int64_t tiles, int sms, int max_s) {
   return best;
 }
 
-bool tc_make_plan(int64_t n, int64_t m, int d, int k, int slices, int pool, bool pair, TcPlan *p) {
+bool tc_make_plan(int64_t n, int64_t m, int d, int k, int slices, int pool, bool pair,
+                  int64_t plan_rows, TcPlan *p) {
   if (!tc_supported(d, k) || n <= 0 || m <= 0) return false;
   TcPlan P{};
   P.n = n;
@@ -961,14 +967,26 @@ bool tc_make_plan(int64_t n, int64_t m, int d, int k, int slices, int pool, bool
   if (target > P.cand_cap / 4) target = P.cand_cap / 4;
   int64_t ratio = target / k;
   if (ratio < 4) ratio = 4;
+  // plan on `basis` tiles (this search's own, or those plan_rows gives, so that the
+  // shards of one sharded search get the same number of levels), then map the
+  // sample sizes onto this search's tiles
+  const int64_t basis = plan_rows > 0 ? (plan_rows + kBN - 1) / kBN : P.x_tiles;
   int64_t sizes[kMaxLevels];
   int nl = 0;
-  sizes[nl++] = P.x_tiles;
+  sizes[nl++] = basis;
   while (nl < kMaxLevels && sizes[nl - 1] * kBN > target) {
     int64_t prev = (sizes[nl - 1] + ratio - 1) / ratio;
     if (prev * kBN < 2 * k) prev = (2 * k + kBN - 1) / kBN;  // the base needs >= k rows
     if (prev >= sizes[nl - 1]) break;
     sizes[nl++] = prev;
+  }
+  sizes[0] = P.x_tiles;
+  for (int l = 1; l < nl; l++) {
+    int64_t s = (sizes[l] * P.x_tiles + basis - 1) / basis;
+    if (s * kBN < 2 * k) s = (2 * k + kBN - 1) / kBN;
+    if (s > sizes[l - 1]) s = sizes[l - 1];
+    if (s < 1) s = 1;
+    sizes[l] = s;
   }
   P.levels = nl;
   const int sms = num_sms();
@@ -1044,7 +1062,7 @@ static bool make_tmap(CUtensorMap *map, const void *base, int64_t rows, int cols
 
 int tc_run(const float *Q, const float *X, int64_t id_offset, float *out_d, int32_t *out_i,
            void *ws_, const TcPlan &p, cudaStream_t stream, cudaEvent_t t0, cudaEvent_t t1,
-           int *launches) {
+           int *launches, LevelHook hook, void *hook_user) {
   unsigned char *ws = static_cast<unsigned char *>(ws_);
   WsHeader *hdr = reinterpret_cast<WsHeader *>(ws);
   __half *Xh = reinterpret_cast<__half *>(ws + p.off_xh);
@@ -1147,6 +1165,7 @@ int tc_run(const float *Q, const float *X, int64_t id_offset, float *out_d, int3
       LevelSelArgs S{};
       S.cand = cand;
       S.ccount = ccount;
+      S.qinfo = qinfo;
       S.n = p.n;
       S.k = p.k;
       S.pool = p.cand_cap;
@@ -1157,6 +1176,8 @@ int tc_run(const float *Q, const float *X, int64_t id_offset, float *out_d, int3
       tc_level_select_kernel<<<(unsigned)p.n, kSelThreads, lsmem, stream>>>(S);
       nl++;
       BFK_TRY(cudaGetLastError());
+      // a sharded search replaces each query's bound by the minimum over all shards
+      if (hook) hook(rlev, p.n, hook_user, stream);
     }
   }
 

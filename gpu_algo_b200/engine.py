@@ -55,10 +55,25 @@ def workspace_size(n: int, m: int, d: int, k: int, opts: _lib.Opts) -> int:
     return int(nb.value)
 
 
+class _DeviceArray:
+    """A raw device float32 vector exposed through __cuda_array_interface__."""
+
+    def __init__(self, ptr: int, n: int):
+        self.__cuda_array_interface__ = {"shape": (n,), "typestr": "<f4", "data": (ptr, False),
+                                         "version": 3, "strides": None, "stream": None}
+
+
 def search(Q, X, k: int, *, engine: str = "auto", slices: int = 0, max_candidates: int = 0,
            id_offset: int = 0, out: tuple[torch.Tensor, torch.Tensor] | None = None,
-           ws: torch.Tensor | None = None, time_main: bool = False, cta_pair: bool = False):
-    """Exact k-NN on the GPU.  Returns (dists, ids) device tensors."""
+           ws: torch.Tensor | None = None, time_main: bool = False, cta_pair: bool = False,
+           bound_hook=None, plan_rows: int = 0):
+    """Exact k-NN on the GPU.  Returns (dists, ids) device tensors.
+
+    ``bound_hook(t)``, if given, is called by the tensor-core engine after each
+    sampling level with ``t``, a float32 CUDA tensor (n,) of per-query bounds
+    that it may lower in place (a sharded search takes the minimum over
+    shards).  ``plan_rows`` makes shards of one search plan the same levels.
+    """
     Q = as_device_f32(Q, "Q")
     X = as_device_f32(X, "X")
     n, d = Q.shape
@@ -74,6 +89,16 @@ def search(Q, X, k: int, *, engine: str = "auto", slices: int = 0, max_candidate
     opts = _lib.make_opts(engine, slices, max_candidates,
                           (_lib.FLAG_TIME_MAIN if time_main else 0) |
                           (_lib.FLAG_CTA_PAIR if cta_pair else 0))
+    opts.plan_rows = int(plan_rows)
+    hook_error = []
+    if bound_hook is not None:
+        def _hook(ptr, count, user, stream_ptr):
+            try:
+                bound_hook(torch.as_tensor(_DeviceArray(ptr, count), device=Q.device))
+            except BaseException as exc:  # re-raised after the search returns
+                hook_error.append(exc)
+        c_hook = _lib.LEVEL_HOOK(_hook)
+        opts.level_hook = c_hook
     with torch.cuda.device(Q.device):
         stream = torch.cuda.current_stream()
         if out is None:
@@ -89,6 +114,8 @@ def search(Q, X, k: int, *, engine: str = "auto", slices: int = 0, max_candidate
         st = lib.bfk_search(Q.data_ptr(), n, X.data_ptr() if m else None, m, d, k, int(id_offset),
                             dists.data_ptr(), ids.data_ptr(), ws.data_ptr(), ws.numel(),
                             ctypes.byref(opts), ctypes.c_void_p(stream.cuda_stream))
+        if hook_error:
+            raise hook_error[0]
         _lib.check(st, "bfk_search")
     return dists, ids
 

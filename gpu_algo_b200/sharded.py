@@ -38,18 +38,37 @@ def gather_lists(d_: torch.Tensor, i_: torch.Tensor, group=None) -> tuple[torch.
 
 def sharded_search(Q, X_shard, k: int, row_begin: int, group=None,
                    local_search: Callable | None = None,
-                   merge_fn: Callable | None = None) -> tuple[torch.Tensor, torch.Tensor]:
+                   merge_fn: Callable | None = None, plan_rows: int = 0,
+                   **search_kwargs) -> tuple[torch.Tensor, torch.Tensor]:
     """Exact k-NN over the union of every rank's shard; result on every rank.
+
+    With the CUDA engine, the ranks also share each query's sampled distance
+    bound after every sampling level (an all-reduce MIN of n floats): the
+    minimum over shards bounds the global k-th distance, so every shard filters
+    with the tightest bound any shard found.  `plan_rows` (the largest shard's
+    row count; looked up with an all-reduce when 0) gives every shard the same
+    sampling levels, so all ranks take the same collective steps.
 
     `local_search(Q, X, k, id_offset)` and `merge_fn(all_d, all_i, k)` default
     to the CUDA engine; tests substitute CPU stand-ins to exercise the
-    orchestration over gloo.
+    orchestration over gloo.  `search_kwargs` go to `engine.search`.
     """
     if local_search is None:
         from .engine import search
+        world = dist.get_world_size(group) if dist.is_initialized() else 1
+        if world > 1 and plan_rows <= 0:
+            sizes = torch.tensor([X_shard.shape[0]], dtype=torch.int64, device=X_shard.device)
+            dist.all_reduce(sizes, op=dist.ReduceOp.MAX, group=group)
+            plan_rows = int(sizes.item())
+
+        def share_bounds(t):
+            # the minimum over shards of each query's bound is still a bound for all
+            dist.all_reduce(t, op=dist.ReduceOp.MIN, group=group)
 
         def local_search(Q_, X_, k_, id_offset):
-            return search(Q_, X_, k_, id_offset=id_offset)
+            return search(Q_, X_, k_, id_offset=id_offset,
+                          bound_hook=share_bounds if world > 1 else None,
+                          plan_rows=plan_rows if world > 1 else 0, **search_kwargs)
     if merge_fn is None:
         from .engine import merge as merge_fn
     d_, i_ = local_search(Q, X_shard, k, row_begin)

@@ -51,12 +51,25 @@ typedef enum {
 #define BFK_FLAG_TIME_MAIN 1 /* time the main kernel of every call with CUDA events      */
 #define BFK_FLAG_CTA_PAIR 2  /* TC engine: CTA pairs (tcgen05.mma.cta_group::2, M = 256)  */
 
+/*
+ * Called by the TC engine after each sampling level with `bound` (device, n
+ * floats): per query an upper bound on (k-th distance - ||q||^2) plus the
+ * query's error margin.  A sharded search replaces every value by its minimum
+ * over all shards, enqueued on `stream`, before returning.  Optional.
+ */
+typedef void (*bfk_level_hook_t)(float *bound, int64_t n, void *user, void *stream);
+
 typedef struct {
   int32_t engine;         /* bfk_engine_t                                                */
   int32_t slices;         /* database slices per query block, 0 = auto                   */
   int32_t max_candidates; /* TC engines: per-query candidate pool, 0 = auto              */
   int32_t flags;          /* BFK_FLAG_*                                                  */
   int32_t reserved[4];    /* must be zero                                                */
+  bfk_level_hook_t level_hook; /* TC engine: see bfk_level_hook_t, NULL = none           */
+  void *hook_user;        /* passed to level_hook                                        */
+  int64_t plan_rows;      /* TC engine: rows the sampling levels are planned for, 0 = m.
+                             Shards of one search pass the same value, so every shard
+                             calls level_hook the same number of times.                */
 } bfk_opts_t;
 
 typedef struct {

@@ -195,3 +195,30 @@ def test_tc_cta_pair_bit_exact(plumbing):
     d_, i_ = engine.search(dev(Q[:300]), dev(X), 10, engine="tc_f16", cta_pair=True)
     torch.cuda.synchronize()
     assert_exact(d_.cpu().numpy(), i_.cpu().numpy(), gd[:300], gi[:300], "cta pair, 3 tiles")
+
+
+def test_shared_bounds_keep_the_merged_result_exact(plumbing):
+    """Emulates a two-shard search on one GPU: shard B filters with the bounds
+    shard A found (what the all-reduce MIN hands every shard); the merge of the
+    two shards' lists must still be the exact top-k of the union."""
+    X, Q, gd, gi = plumbing
+    Qd = dev(Q[:512])
+    half = X.shape[0] // 2
+    XA, XB = dev(X[:half]), dev(X[half:])
+    saved = []
+
+    def record(t):
+        saved.append(t.clone())
+
+    dA, iA = engine.search(Qd, XA, 10, engine="tc_f16", bound_hook=record, plan_rows=half)
+    calls = iter(saved)
+
+    def lower(t):
+        torch.minimum(t, next(calls), out=t)
+
+    dB, iB = engine.search(Qd, XB, 10, engine="tc_f16", bound_hook=lower, plan_rows=half,
+                           id_offset=half)
+    assert len(saved) >= 1  # the sampling levels called the hook
+    md, mi = engine.merge(torch.stack([dA, dB]), torch.stack([iA, iB]), 10)
+    torch.cuda.synchronize()
+    assert_exact(md.cpu().numpy(), mi.cpu().numpy(), gd[:512], gi[:512], "shared bounds")
