@@ -47,7 +47,8 @@ constexpr int kColGroups = 4;       // column groups of a tile (regions per slic
 constexpr int kGroupN = kBN / kColGroups;  // accumulator columns an epilogue warp reads per tile
 constexpr int kTcThreads = 64 + 32 * kEpiWarps;  // warp 0 TMA, warp 1 MMA, 16 epilogue warps
 constexpr int kSmemLimit = 232448;  // 227 KB opt-in per block
-constexpr int kMaxKch = 4;          // d <= 256 (query tile resident in shared memory)
+constexpr int kResidentKch = 4;     // d <= 256: the query tile stays in shared memory
+constexpr int kMaxKch = 16;         // d <= 1024: query K chunks stream with the row chunks
 constexpr int kTcMaxK = 512;
 constexpr int kSelThreads = 256;
 constexpr int kSurvCap = 2048;      // exact re-rank capacity per query
@@ -77,20 +78,24 @@ struct FilterArgs {
 // ---------------------------------------------------------------------------
 struct TcLayout {
   int kch, ns;
+  bool stream_a;    // the query tile's K chunks travel through the stages with the rows'
   uint32_t bchunk;  // bytes of one row-tile K chunk in this CTA (half of it in a CTA pair)
+  uint32_t stage;   // bytes of one stage: [query chunk if stream_a] + row chunk
   size_t a_off, b_off, nx_off, bar_off, total;
 };
 __host__ __device__ inline TcLayout tc_layout(int kch, bool pair) {
   TcLayout L{};
   L.kch = kch;
+  L.stream_a = kch > kResidentKch;
   L.bchunk = pair ? kBChunkBytes / 2 : kBChunkBytes;
+  L.stage = L.bchunk + (L.stream_a ? kAChunkBytes : 0);
   L.a_off = 0;
-  L.b_off = (size_t)kch * kAChunkBytes;
+  L.b_off = L.stream_a ? 0 : (size_t)kch * kAChunkBytes;
   const size_t fixed = (size_t)kEpiWarps * 2 * kGroupN * 4 + 256;
-  size_t ns = ((size_t)kSmemLimit - 1024 - L.b_off - fixed) / L.bchunk;
+  size_t ns = ((size_t)kSmemLimit - 1024 - L.b_off - fixed) / L.stage;
   if (ns > 12) ns = 12;
   L.ns = (int)ns;
-  L.nx_off = L.b_off + (size_t)L.ns * L.bchunk;
+  L.nx_off = L.b_off + (size_t)L.ns * L.stage;
   L.bar_off = L.nx_off + (size_t)kEpiWarps * 2 * kGroupN * 4;
   L.total = L.bar_off + 256 + 1024;  // + alignment slack
   return L;
@@ -199,14 +204,18 @@ __global__ void __maxnreg__(96)
       tma_prefetch_desc(&tmap_q);
       tma_prefetch_desc(&tmap_x);
       // in a pair, only the even CTA arms the barriers; both CTAs' copies count on them
-      if (rank == 0) mbar_arrive_expect_tx(a_full, (uint32_t)((PAIR ? 2 : 1) * kch * kAChunkBytes));
-      for (int c = 0; c < kch; c++) {
-        if (PAIR) tma_load_2d_pair(sA + c * kAChunkBytes, &tmap_q, a_full, c * kBK, qt * kBM);
-        else tma_load_2d(sA + c * kAChunkBytes, &tmap_q, a_full, c * kBK, qt * kBM);
+      if (!L.stream_a) {
+        if (rank == 0) mbar_arrive_expect_tx(a_full, (uint32_t)((PAIR ? 2 : 1) * kch * kAChunkBytes));
+        for (int c = 0; c < kch; c++) {
+          if (PAIR) tma_load_2d_pair(sA + c * kAChunkBytes, &tmap_q, a_full, c * kBK, qt * kBM);
+          else tma_load_2d(sA + c * kAChunkBytes, &tmap_q, a_full, c * kBK, qt * kBM);
+        }
       }
       uint32_t it = 0;
       bool ok = true;
-      const uint32_t bchunk = L.bchunk;
+      const uint32_t bchunk = L.bchunk, stage = L.stage;
+      const uint32_t boff = L.stream_a ? kAChunkBytes : 0;  // row chunk after the query chunk
+      const uint32_t tx = (PAIR ? 2 : 1) * (bchunk + (L.stream_a ? kAChunkBytes : 0));
       for (int lt = 0; lt < ntiles && ok; lt++) {
         // a pair's CTAs load rows [0, 128) and [128, 256) of the tile
         const int32_t row0 = (int32_t)(level_tile(a, j_begin + lt) * kBN) + (int32_t)(rank * (kBN / 2));
@@ -217,9 +226,14 @@ __global__ void __maxnreg__(96)
             ok = false;
             break;
           }
-          if (rank == 0) mbar_arrive_expect_tx(full + st, (PAIR ? 2 : 1) * bchunk);
-          if (PAIR) tma_load_2d_pair(sB + st * bchunk, &tmap_x, full + st, c * kBK, row0);
-          else tma_load_2d(sB + st * bchunk, &tmap_x, full + st, c * kBK, row0);
+          if (rank == 0) mbar_arrive_expect_tx(full + st, tx);
+          unsigned char *sst = sB + st * stage;
+          if (L.stream_a) {
+            if (PAIR) tma_load_2d_pair(sst, &tmap_q, full + st, c * kBK, qt * kBM);
+            else tma_load_2d(sst, &tmap_q, full + st, c * kBK, qt * kBM);
+          }
+          if (PAIR) tma_load_2d_pair(sst + boff, &tmap_x, full + st, c * kBK, row0);
+          else tma_load_2d(sst + boff, &tmap_x, full + st, c * kBK, row0);
         }
       }
       // every issued copy must land before the CTA may exit; in a pair the even
@@ -228,16 +242,17 @@ __global__ void __maxnreg__(96)
         const uint32_t first = it > (uint32_t)ns ? it - ns : 0;
         for (uint32_t i = first; i < it; i++)
           mbar_wait_bounded(full + (i % ns), (i / ns) & 1, abort_flag);
-        mbar_wait_bounded(a_full, 0, abort_flag);
+        if (!L.stream_a) mbar_wait_bounded(a_full, 0, abort_flag);
       }
     }
   } else if (warp == 1) {
     // ---------------- MMA issuer ----------------
     if (lane == 0 && ntiles > 0 && rank == 0) {
       constexpr uint32_t idesc = idesc_f16_f32(PAIR ? 2 * kBM : kBM, kBN);
-      const uint32_t bchunk = L.bchunk;
+      const uint32_t stage = L.stage;
       const uint32_t a_addr = smem_u32(sA), b_addr = smem_u32(sB);
-      bool ok = mbar_wait_bounded(a_full, 0, abort_flag);
+      const uint32_t boff = L.stream_a ? kAChunkBytes : 0;
+      bool ok = L.stream_a || mbar_wait_bounded(a_full, 0, abort_flag);
       if (!ok) set_error(a.hdr, ERR_TIMEOUT_MMA, abort_flag);
       uint32_t it = 0;
       for (int lt = 0; lt < ntiles && ok; lt++) {
@@ -259,8 +274,9 @@ __global__ void __maxnreg__(96)
           tc_fence_after();
 #pragma unroll
           for (int kk = 0; kk < kBK / 16; kk++) {
-            const uint64_t ad = umma_desc_k_sw128(a_addr + c * kAChunkBytes + kk * 32);
-            const uint64_t bd = umma_desc_k_sw128(b_addr + st * bchunk + kk * 32);
+            const uint32_t a_chunk = L.stream_a ? b_addr + st * stage : a_addr + c * kAChunkBytes;
+            const uint64_t ad = umma_desc_k_sw128(a_chunk + kk * 32);
+            const uint64_t bd = umma_desc_k_sw128(b_addr + st * stage + boff + kk * 32);
             if (PAIR) tc_mma_f16_pair(d_tmem, ad, bd, idesc, (c | kk) != 0);
             else tc_mma_f16(d_tmem, ad, bd, idesc, (c | kk) != 0);
           }

@@ -153,6 +153,21 @@ def test_large_k_and_high_d():
         assert_exact(d_, i_, ed, ei, f"d=960 k={k}")
 
 
+@pytest.mark.parametrize("d", [257, 300, 960, 1024])
+def test_tc_streamed_query_tiles_high_d(d):
+    """d > 256: the query tile's K chunks stream through the stages with the rows'."""
+    rng = np.random.Generator(np.random.PCG64(100 + d))
+    X = rng.standard_normal((12_000, d), dtype=np.float32)
+    Q = rng.standard_normal((200, d), dtype=np.float32)
+    assert tc_ok(d, 100)
+    ed, ei = oracle_knn(Q, X, 100)
+    for pair in (True, False):  # the stats below read the last (single-CTA) search
+        d_, i_ = run(Q, X, 100, engine="tc_f16", cta_pair=pair)
+        assert_exact(d_, i_, ed, ei, f"tc d={d} pair={pair}")
+    st = engine.last_stats(dev(Q), dev(X), 100, engine="tc_f16")
+    assert st["engine"] == "tc_f16" and st["device_error"] == 0
+
+
 def test_errors_are_raised():
     Q = torch.zeros((4, 8), device="cuda")
     X = torch.zeros((16, 8), device="cuda")
