@@ -76,6 +76,10 @@ struct FilterArgs {
 // ---------------------------------------------------------------------------
 // shared-memory layout of the filter kernel
 // ---------------------------------------------------------------------------
+// per epilogue warp and accumulator buffer: the group's 64 ||x||^2 values and the
+// minimum of each group of 8 of them
+constexpr int kNxStage = kGroupN + 8;
+
 struct TcLayout {
   int kch, ns;
   bool stream_a;    // the query tile's K chunks travel through the stages with the rows'
@@ -91,12 +95,12 @@ __host__ __device__ inline TcLayout tc_layout(int kch, bool pair) {
   L.stage = L.bchunk + (L.stream_a ? kAChunkBytes : 0);
   L.a_off = 0;
   L.b_off = L.stream_a ? 0 : (size_t)kch * kAChunkBytes;
-  const size_t fixed = (size_t)kEpiWarps * 2 * kGroupN * 4 + 256;
+  const size_t fixed = (size_t)kEpiWarps * 2 * kNxStage * 4 + 256;
   size_t ns = ((size_t)kSmemLimit - 1024 - L.b_off - fixed) / L.stage;
   if (ns > 12) ns = 12;
   L.ns = (int)ns;
   L.nx_off = L.b_off + (size_t)L.ns * L.stage;
-  L.bar_off = L.nx_off + (size_t)kEpiWarps * 2 * kGroupN * 4;
+  L.bar_off = L.nx_off + (size_t)kEpiWarps * 2 * kNxStage * 4;
   L.total = L.bar_off + 256 + 1024;  // + alignment slack
   return L;
 }
@@ -117,16 +121,43 @@ __device__ __forceinline__ void fma2(float a0, float a1, float c, float b0, floa
   asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(pd) : "l"(pa), "l"(pc), "l"(pb));
   asm("mov.b64 {%0, %1}, %2;" : "=f"(d0), "=f"(d1) : "l"(pd));
 }
-// three-input minimum (NaN inputs are ignored, as by fminf)
+// three-input minimum / maximum (NaN inputs are ignored, as by fminf / fmaxf)
 __device__ __forceinline__ float min3f(float a, float b, float c) {
   float d;
   asm("min.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
   return d;
 }
-
-__device__ __forceinline__ int64_t level_tile(const FilterArgs &a, int64_t j) {
-  return a.level_tiles == a.x_tiles ? j : (j * a.x_tiles) / a.level_tiles;
+__device__ __forceinline__ float max3f(float a, float b, float c) {
+  float d;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
+  return d;
 }
+// maximum of 8 accumulator values (FP32 bit patterns)
+__device__ __forceinline__ float max8u(const uint32_t *a) {
+  return max3f(max3f(__uint_as_float(a[0]), __uint_as_float(a[1]), __uint_as_float(a[2])),
+               max3f(__uint_as_float(a[3]), __uint_as_float(a[4]), __uint_as_float(a[5])),
+               fmaxf(__uint_as_float(a[6]), __uint_as_float(a[7])));
+}
+
+// Tile j of a level is floor(j * x_tiles / level_tiles): evenly spaced over the
+// database, every tile for the full level.  A walk steps j by one with the
+// quotient and remainder of x_tiles / level_tiles (one division per walk).
+struct TileWalk {
+  int64_t tile, rem, q, r, div;
+  __device__ __forceinline__ TileWalk(const FilterArgs &a, int64_t j) {
+    div = a.level_tiles;
+    q = a.x_tiles / div;
+    r = a.x_tiles - q * div;
+    const int64_t p = j * a.x_tiles;
+    tile = p / div;
+    rem = p - tile * div;
+  }
+  __device__ __forceinline__ void next() {
+    tile += q;
+    rem += r;
+    if (rem >= div) { rem -= div; tile++; }
+  }
+};
 
 // 576 threads in one block: the launch admits at most 96 registers a thread.
 // PAIR: the kernel runs as clusters of two CTAs on two SMs.  The even CTA issues
@@ -216,9 +247,10 @@ __global__ void __maxnreg__(96)
       const uint32_t bchunk = L.bchunk, stage = L.stage;
       const uint32_t boff = L.stream_a ? kAChunkBytes : 0;  // row chunk after the query chunk
       const uint32_t tx = (PAIR ? 2 : 1) * (bchunk + (L.stream_a ? kAChunkBytes : 0));
-      for (int lt = 0; lt < ntiles && ok; lt++) {
+      TileWalk walk(a, j_begin);
+      for (int lt = 0; lt < ntiles && ok; lt++, walk.next()) {
         // a pair's CTAs load rows [0, 128) and [128, 256) of the tile
-        const int32_t row0 = (int32_t)(level_tile(a, j_begin + lt) * kBN) + (int32_t)(rank * (kBN / 2));
+        const int32_t row0 = (int32_t)(walk.tile * kBN) + (int32_t)(rank * (kBN / 2));
         for (int c = 0; c < kch; c++, it++) {
           const uint32_t st = it % ns, ph = (it / ns) & 1;
           if (!mbar_wait_bounded(empty + st, ph ^ 1, abort_flag)) {
@@ -312,26 +344,34 @@ __global__ void __maxnreg__(96)
     int cnt = 0;
     const uint32_t taddr0 = tmem_base + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(cg * kGroupN);
     const float inv_sq = *a.inv_sq;
-    float *nxw = nxs + e * 2 * kGroupN;       // this warp's ||x||^2 staging, two buffers
+    float *nxw = nxs + e * 2 * kNxStage;      // this warp's ||x||^2 staging, two buffers
     // prefetch ||x||^2 (2 rows per lane) and the block scale of the first tile
     float2 pre_nx = make_float2(0.f, 0.f);
     float pre_inv = 1.f;
+    TileWalk walk(a, j_begin);
     if (ntiles > 0) {
-      const int64_t t0 = level_tile(a, j_begin);
+      const int64_t t0 = walk.tile;
       pre_nx = *reinterpret_cast<const float2 *>(a.xnorm + t0 * kBN + cg * kGroupN + lane * 2);
       pre_inv = a.xinv[t0 * kColGroups + cg];
     }
 
     for (int lt = 0; lt < ntiles; lt++) {
       const int b = lt & 1;
-      const int64_t tile = level_tile(a, j_begin + lt);
-      // any role that gave up ends this warp's loop too (warp-uniform decision)
-      if (__any_sync(0xffffffffu, *abort_flag != 0)) break;
-      float *nxt = nxw + b * kGroupN;
+      const int64_t tile = walk.tile;
+      walk.next();  // the walk is one tile ahead from here on
+      // a role that gives up sets the abort flag, which ends the bounded wait below
+      float *nxt = nxw + b * kNxStage;
       *reinterpret_cast<float2 *>(nxt + lane * 2) = pre_nx;
-      const float cscale = -2.0f * inv_sq * pre_inv;  // exact power of two
+      {
+        // minimum ||x||^2 of each group of 8 columns (lanes 4g .. 4g+3 hold group g)
+        float gm = fminf(pre_nx.x, pre_nx.y);
+        gm = fminf(gm, __shfl_xor_sync(0xffffffffu, gm, 1));
+        gm = fminf(gm, __shfl_xor_sync(0xffffffffu, gm, 2));
+        if ((lane & 3) == 0) nxt[kGroupN + (lane >> 2)] = gm;
+      }
+      const float cscale = -2.0f * inv_sq * pre_inv;  // exact power of two, negative
       if (lt + 1 < ntiles) {
-        const int64_t tn = level_tile(a, j_begin + lt + 1);
+        const int64_t tn = walk.tile;
         pre_nx = *reinterpret_cast<const float2 *>(a.xnorm + tn * kBN + cg * kGroupN + lane * 2);
         pre_inv = a.xinv[tn * kColGroups + cg];
       }
@@ -361,39 +401,50 @@ __global__ void __maxnreg__(96)
         } else {
           __syncwarp();  // the ||x||^2 staging written above is visible to every lane
         }
-        // v = acc * cscale + ||x||^2, two columns per packed FMA
-        float v[32];
-        const float4 *nx4 = reinterpret_cast<const float4 *>(nxt + hh * 32);
-#pragma unroll
-        for (int i = 0; i < 8; i++) {
-          const float4 nx = nx4[i];
-          fma2(__uint_as_float(va[4 * i]), __uint_as_float(va[4 * i + 1]), cscale, nx.x, nx.y,
-               v[4 * i], v[4 * i + 1]);
-          fma2(__uint_as_float(va[4 * i + 2]), __uint_as_float(va[4 * i + 3]), cscale, nx.z, nx.w,
-               v[4 * i + 2], v[4 * i + 3]);
-        }
-        // minimum of each group of 8 columns (three-input min)
-        float gmin[4];
-#pragma unroll
-        for (int g = 0; g < 4; g++) {
-          const float *w = v + 8 * g;
-          gmin[g] = min3f(min3f(w[0], w[1], w[2]), min3f(w[3], w[4], w[5]), fminf(w[6], w[7]));
-        }
-        const float all = fminf(min3f(gmin[0], gmin[1], gmin[2]), gmin[3]);
+        // Group bound: cscale < 0, so cscale * max(acc) + min ||x||^2 <= every
+        // v = cscale * acc + ||x||^2 of the group of 8 columns, exactly and after
+        // rounding (round-to-nearest is monotonic).  Only groups whose bound is <= theta
+        // can hold a candidate; their exact v are computed for the appends.
+        const float4 gn = reinterpret_cast<const float4 *>(nxt + kGroupN)[hh];
+        float gb[4];
+        gb[0] = __fmaf_rn(cscale, max8u(va), gn.x);
+        gb[1] = __fmaf_rn(cscale, max8u(va + 8), gn.y);
+        gb[2] = __fmaf_rn(cscale, max8u(va + 16), gn.z);
+        gb[3] = __fmaf_rn(cscale, max8u(va + 24), gn.w);
+        const float all = fminf(min3f(gb[0], gb[1], gb[2]), gb[3]);
         if (__any_sync(0xffffffffu, all <= theta)) {
+          const float4 *nx4 = reinterpret_cast<const float4 *>(nxt + hh * 32);
 #pragma unroll
           for (int g = 0; g < 4; g++) {
-            if (__any_sync(0xffffffffu, gmin[g] <= theta)) {
+            if (__any_sync(0xffffffffu, gb[g] <= theta)) {
+              const uint32_t *acc = va + 8 * g;
+              const float4 n0 = nx4[2 * g], n1 = nx4[2 * g + 1];
+              float v[8];
+              fma2(__uint_as_float(acc[0]), __uint_as_float(acc[1]), cscale, n0.x, n0.y, v[0], v[1]);
+              fma2(__uint_as_float(acc[2]), __uint_as_float(acc[3]), cscale, n0.z, n0.w, v[2], v[3]);
+              fma2(__uint_as_float(acc[4]), __uint_as_float(acc[5]), cscale, n1.x, n1.y, v[4], v[5]);
+              fma2(__uint_as_float(acc[6]), __uint_as_float(acc[7]), cscale, n1.z, n1.w, v[6], v[7]);
+              if (gb[g] <= theta) {
+                // this lane's kept columns, appended with predicated stores
+                const uint32_t rg = row0 + hh * 32 + 8 * g;
+                if (cnt + 8 <= a.region) {
+                  uint2 *wp = region + cnt;
 #pragma unroll
-              for (int i = 0; i < 8; i++) {
-                // one ballot per column; the append runs only for columns some lane keeps
-                const float vi = v[8 * g + i];
-                const unsigned keep = __ballot_sync(0xffffffffu, vi <= theta);
-                if (keep) {
-                  const bool mine = (keep >> lane) & 1u;
-                  if (mine)
-                    region[min(cnt, last)] = make_uint2(row0 + hh * 32 + 8 * g + i, __float_as_uint(vi));
-                  cnt += mine ? 1 : 0;
+                  for (int i = 0; i < 8; i++) {
+                    const bool keep = v[i] <= theta;
+                    if (keep) *wp = make_uint2(rg + i, __float_as_uint(v[i]));
+                    wp += keep ? 1 : 0;
+                  }
+                  cnt = (int)(wp - region);
+                } else {
+                  // near the end of the region: a full region keeps overwriting its last slot
+#pragma unroll
+                  for (int i = 0; i < 8; i++) {
+                    if (v[i] <= theta) {
+                      region[min(cnt, last)] = make_uint2(rg + i, __float_as_uint(v[i]));
+                      cnt++;
+                    }
+                  }
                 }
               }
             }
@@ -674,24 +725,43 @@ __device__ QueryRegions load_regions(const uint2 *cand, const int *ccount, int64
 }
 
 constexpr int kSelStage = 6144;  // candidates staged in shared memory (more: read in place)
+// the final select reuses the staging area for its warps' 32 x 33 row chunks
+static_assert((kSelThreads / 32) * 32 * 33 * 4 <= kSelStage * 8, "row chunks exceed the staging area");
 constexpr int kSelBins = 1024;
 
-// Copy the candidates into shared memory, one warp per region, and return the
-// block-wide min and max of v (smem staging when total <= kSelStage).
+// Copy the candidates into shared memory and return the block-wide min and max
+// of v (smem staging when total <= kSelStage).  Thread t takes entries t, t + B,
+// ... of the regions' concatenation, four loads in flight at a time; the region
+// of an entry is the last one whose prefix offset is <= its position.
 __device__ void stage_candidates(const QueryRegions &R, const int *s_cnt, const int *s_off,
                                  uint2 *cs, float *s_red, float *vmin, float *vmax) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nw = blockDim.x >> 5;
   const bool stage = R.total <= kSelStage;
   float lo = INFINITY, hi = -INFINITY;
-  for (int rg = warp; rg < R.nreg; rg += nw) {
-    const uint2 *src = R.base + (size_t)rg * R.region;
-    const int c = s_cnt[rg], o = s_off[rg];
-    for (int e = lane; e < c; e += 32) {
-      const uint2 ent = src[e];
-      const float v = __uint_as_float(ent.y);
-      lo = fminf(lo, v);
-      hi = fmaxf(hi, v);
-      if (stage) cs[o + e] = ent;
+  for (int e0 = threadIdx.x; e0 < R.total; e0 += 4 * blockDim.x) {
+    uint2 ent[4];
+#pragma unroll
+    for (int u = 0; u < 4; u++) {
+      const int e = e0 + u * (int)blockDim.x;
+      ent[u] = make_uint2(0u, 0x7fc00000u);  // NaN: ignored by the min and max
+      if (e < R.total) {
+        int a = 0, b = R.nreg - 1;
+        while (a < b) {
+          const int mid = (a + b + 1) >> 1;
+          if (s_off[mid] <= e) a = mid; else b = mid - 1;
+        }
+        ent[u] = R.base[(size_t)a * R.region + (e - s_off[a])];
+      }
+    }
+#pragma unroll
+    for (int u = 0; u < 4; u++) {
+      const int e = e0 + u * (int)blockDim.x;
+      if (e < R.total) {
+        const float v = __uint_as_float(ent[u].y);
+        lo = fminf(lo, v);
+        hi = fmaxf(hi, v);
+        if (stage) cs[e] = ent[u];
+      }
     }
   }
 #pragma unroll
@@ -857,18 +927,11 @@ __global__ void __launch_bounds__(kSelThreads) tc_final_select_kernel(const SelA
                                 a.qinfo[q].y),
                       a.qinfo[q].y);
   __syncthreads();
-  // survivors -> exact distance with the reference arithmetic
+  // survivors: the rows with v <= theta, listed in `keys`
   for_each_candidate(R, s_cnt, cs, [&](uint2 ent) {
-    const float v = __uint_as_float(ent.y);
-    if (v <= theta) {
+    if (__uint_as_float(ent.y) <= theta) {
       const int slot = atomicAdd(&s_nsurv, 1);
-      if (slot < kSurvCap) {
-        const int64_t row = ent.x;
-        const float *x = a.X + row * a.d;
-        float acc = 0.f;
-        for (int cc = 0; cc < a.d; cc++) acc = dist_step(qs[cc], x[cc], acc);
-        keys[slot] = acc == acc ? pair_key(acc, (int32_t)(a.id_offset + row)) : ~0ull;
-      }
+      if (slot < kSurvCap) keys[slot] = ent.x;
     }
   });
   __syncthreads();
@@ -880,6 +943,37 @@ __global__ void __launch_bounds__(kSelThreads) tc_final_select_kernel(const SelA
     }
     return;
   }
+  // Exact distances with the reference arithmetic.  A warp takes 32 survivors
+  // at a time, one per lane; their rows pass through shared memory (the staged
+  // candidates are no longer needed) in chunks of 32 dimensions, loaded with
+  // coalesced reads, and each lane accumulates its own row in dimension order.
+  {
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nw = blockDim.x >> 5;
+    float *tile = reinterpret_cast<float *>(cs) + warp * (32 * 33);
+    for (int b0 = warp * 32; b0 < ns; b0 += nw * 32) {
+      const int nb = min(32, ns - b0);
+      const uint32_t myrow = lane < nb ? (uint32_t)keys[b0 + lane] : 0u;
+      float acc = 0.f;
+      for (int c0 = 0; c0 < a.d; c0 += 32) {
+        const int cw = min(32, a.d - c0);
+        float t[32];
+#pragma unroll
+        for (int j = 0; j < 32; j++) {
+          const uint32_t rj = __shfl_sync(0xffffffffu, myrow, j);
+          t[j] = (j < nb && lane < cw) ? __ldg(a.X + (size_t)rj * a.d + c0 + lane) : 0.f;
+        }
+        __syncwarp();
+#pragma unroll
+        for (int j = 0; j < 32; j++) tile[j * 33 + lane] = t[j];
+        __syncwarp();
+        if (lane < nb)
+          for (int c = 0; c < cw; c++) acc = dist_step(qs[c0 + c], tile[lane * 33 + c], acc);
+      }
+      if (lane < nb)
+        keys[b0 + lane] = acc == acc ? pair_key(acc, (int32_t)(a.id_offset + myrow)) : ~0ull;
+    }
+  }
+  __syncthreads();
   int P = 2;
   while (P < ns) P <<= 1;
   for (int e = ns + threadIdx.x; e < P; e += blockDim.x) keys[e] = ~0ull;
