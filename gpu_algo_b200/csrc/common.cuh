@@ -101,17 +101,30 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t *bar, uint32_t parity) {
       : "memory");
   return ok != 0;
 }
+// try_wait that suspends the thread until the phase completes or `hint_ns` passes,
+// so a waiting warp takes no issue slots from the warps that share its scheduler
+__device__ __forceinline__ bool mbar_try_wait_sleep(uint64_t *bar, uint32_t parity,
+                                                    uint32_t hint_ns) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity), "r"(hint_ns)
+      : "memory");
+  return ok != 0;
+}
+constexpr uint32_t kWaitSliceNs = 20000;  // one suspended try_wait; the limits are checked between
 // Returns false when the limit ran out or `abort_flag` was raised by another role.
 __device__ __forceinline__ bool mbar_wait_bounded(uint64_t *bar, uint32_t parity,
                                                   volatile int *abort_flag) {
   if (mbar_try_wait(bar, parity)) return true;
-  uint64_t t0 = globaltimer_ns();
-  for (uint32_t it = 1;; ++it) {
-    if (mbar_try_wait(bar, parity)) return true;
-    if ((it & 63u) == 0) {
-      if (*abort_flag) return false;
-      if (globaltimer_ns() - t0 > kWaitLimitNs) return false;
-    }
+  const uint64_t t0 = globaltimer_ns();
+  for (;;) {
+    if (mbar_try_wait_sleep(bar, parity, kWaitSliceNs)) return true;
+    if (*abort_flag) return false;
+    if (globaltimer_ns() - t0 > kWaitLimitNs) return false;
   }
 }
 
