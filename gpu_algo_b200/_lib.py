@@ -49,7 +49,7 @@ LEVEL_HOOK = ctypes.CFUNCTYPE(None, ctypes.c_void_p, ctypes.c_int64, ctypes.c_vo
 class Opts(ctypes.Structure):
     _fields_ = [("engine", ctypes.c_int32), ("slices", ctypes.c_int32),
                 ("max_candidates", ctypes.c_int32), ("flags", ctypes.c_int32),
-                ("reserved", ctypes.c_int32 * 4), ("level_hook", LEVEL_HOOK),
+                ("shards", ctypes.c_int32), ("reserved", ctypes.c_int32 * 3), ("level_hook", LEVEL_HOOK),
                 ("hook_user", ctypes.c_void_p), ("plan_rows", ctypes.c_int64)]
 
 

@@ -61,10 +61,10 @@ DirectPlan direct_plan(int64_t n, int64_t m, int d, int k, int slices_req) {
 
 bool opts_ok(const bfk_opts_t *o) {
   if (!o) return true;
-  for (int i = 0; i < 4; i++)
+  for (int i = 0; i < 3; i++)
     if (o->reserved[i] != 0) return false;
   return o->engine >= BFK_ENGINE_AUTO && o->engine <= BFK_ENGINE_TC_F16 && o->slices >= 0 &&
-         o->max_candidates >= 0 && o->plan_rows >= 0 &&
+         o->max_candidates >= 0 && o->plan_rows >= 0 && o->shards >= 0 &&
          (o->flags & ~(BFK_FLAG_TIME_MAIN | BFK_FLAG_CTA_PAIR)) == 0;
 }
 
@@ -210,7 +210,8 @@ bfk_status_t bfk_search(const float *Q, int64_t n, const float *X, int64_t m, in
       return BFK_ERR_UNSUPPORTED;
     if (workspace_bytes < p.total) return BFK_ERR_WORKSPACE;
     int rc = tc_run(Q, X, id_offset, out_dists, out_ids, ws, p, stream, t0, t1, &g_calls.launches,
-                    opts ? opts->level_hook : nullptr, opts ? opts->hook_user : nullptr);
+                    opts ? opts->level_hook : nullptr, opts ? opts->hook_user : nullptr,
+                    opts ? opts->shards : 0);
     if (rc == 1) return BFK_ERR_CUDA;
     if (rc == 2) return BFK_ERR_DEVICE_TIMEOUT;
     return BFK_OK;

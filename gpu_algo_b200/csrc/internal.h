@@ -54,10 +54,12 @@ bool tc_make_plan(int64_t n, int64_t m, int d, int k, int slices, int cand_cap, 
                   int64_t plan_rows, TcPlan *p);
 // Returns 0 ok, 1 CUDA error, 2 device timeout.  t0/t1 (may be null) are
 // recorded around the main kernel; *launches counts the kernels launched.
-typedef void (*LevelHook)(float *bound, int64_t n, void *user, void *stream);
+// `hook` (may be null) is called after every level with the level's bounds;
+// `shards` > 1 shards share them, which doubles the bounds handed to the hook.
+typedef void (*LevelHook)(float *bound, int64_t count, void *user, void *stream);
 int tc_run(const float *Q, const float *X, int64_t id_offset, float *out_d, int32_t *out_i,
            void *ws, const TcPlan &p, cudaStream_t stream, cudaEvent_t t0, cudaEvent_t t1,
-           int *launches, LevelHook hook, void *hook_user);
+           int *launches, LevelHook hook, void *hook_user, int shards);
 const void *tc_kernel_ptr(int d, int k);
 size_t tc_smem_bytes(int d, int k);
 int tc_threads();

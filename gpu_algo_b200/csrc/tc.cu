@@ -61,6 +61,7 @@ struct FilterArgs {
   const float2 *qinfo;   // (q_tiles*128) (||q||^2, 2*margin); NaN margin for padding rows
   const float *inv_sq;   // 1/scale of the queries (device scalar)
   const float *r_in;     // (n) bound B of the previous level (B + margin), null = none
+  bool two_bounds;       // r_in holds (n) B and (n) -B2 (shards sharing bounds)
   int64_t n;
   int64_t x_tiles;       // tiles of the whole database
   int64_t level_tiles;   // tiles of this level (evenly spaced over the database)
@@ -137,6 +138,12 @@ __device__ __forceinline__ float max8u(const uint32_t *a) {
   return max3f(max3f(__uint_as_float(a[0]), __uint_as_float(a[1]), __uint_as_float(a[2])),
                max3f(__uint_as_float(a[3]), __uint_as_float(a[4]), __uint_as_float(a[5])),
                fmaxf(__uint_as_float(a[6]), __uint_as_float(a[7])));
+}
+
+// the bound a level select wrote for query q (both halves when the shards share them)
+__device__ __forceinline__ float read_bound(const float *r, int64_t n, int64_t q, bool two) {
+  const float b = r[q];
+  return two ? fminf(b, -r[n + q]) : b;
 }
 
 // Tile j of a level is floor(j * x_tiles / level_tiles): evenly spaced over the
@@ -337,7 +344,9 @@ __global__ void __maxnreg__(96)
     // theta = B + margin, B = (k-th smallest v of the previous level) + margin, rounded up.
     // Rows past m carry ||x||^2 = +inf, so theta stays finite: FLT_MAX when there is no bound.
     float theta = -INFINITY;
-    if (valid) theta = a.r_in ? fminf(__fadd_ru(a.r_in[q], margin), FLT_MAX) : FLT_MAX;
+    if (valid)
+      theta = a.r_in ? fminf(__fadd_ru(read_bound(a.r_in, a.n, q, a.two_bounds), margin), FLT_MAX)
+                     : FLT_MAX;
     uint2 *region = a.cand + (size_t)(valid ? q : 0) * a.pool +
                     (size_t)(kColGroups * s + cg) * a.region;
     const int last = a.region - 1;            // a full region keeps overwriting its last slot
@@ -795,12 +804,14 @@ __device__ __forceinline__ void for_each_candidate(const QueryRegions &R, const 
   }
 }
 
-// An upper bound R >= the k-th smallest v that is itself the value of a
-// candidate ranked >= k: values are binned linearly over [vmin, vmax]; R is the
-// largest v in the bins up to the one where the running count reaches k.
-// Any such R is a valid threshold (at least k candidates have v <= R).
-__device__ float block_kth_bound(const QueryRegions &R, const int *s_cnt, const uint2 *cs, int k,
-                                 float vmin, float vmax, int *hist, float *s_red, int *s_bin) {
+// Upper bounds R1 >= the k1-th and R2 >= the k2-th smallest v, each itself the
+// value of a candidate of rank >= k1 (k2): values are binned linearly over
+// [vmin, vmax]; R is the largest v in the bins up to the one where the running
+// count reaches k.  Any such R is a valid threshold (at least k candidates have
+// v <= R).  The caller guarantees total >= k1 >= k2 >= 1.
+__device__ float2 block_kth_bounds(const QueryRegions &R, const int *s_cnt, const uint2 *cs,
+                                   int k1, int k2, float vmin, float vmax, int *hist,
+                                   float *s_red, int *s_bin) {
   const float span = vmax - vmin;
   const float scale = span > 0.f ? (float)(kSelBins - 1) / span : 0.f;
   for (int b = threadIdx.x; b < kSelBins; b += blockDim.x) hist[b] = 0;
@@ -812,7 +823,7 @@ __device__ float block_kth_bound(const QueryRegions &R, const int *s_cnt, const 
   for_each_candidate(R, s_cnt, cs, [&](uint2 ent) { atomicAdd(&hist[bin_of(__uint_as_float(ent.y))], 1); });
   __syncthreads();
   if (threadIdx.x < 32) {
-    // warp 0: first bin where the running count reaches k (32 bins per lane)
+    // warp 0: first bins where the running count reaches k1 and k2 (32 bins per lane)
     const int lane = threadIdx.x;
     int sum = 0;
     for (int j = 0; j < kSelBins / 32; j++) sum += hist[lane * (kSelBins / 32) + j];
@@ -823,31 +834,43 @@ __device__ float block_kth_bound(const QueryRegions &R, const int *s_cnt, const 
       if (lane >= o) incl += t;
     }
     const int excl = incl - sum;
-    if (excl < k && incl >= k) {
-      int run = excl, b = lane * (kSelBins / 32);
-      for (;; b++) {
-        run += hist[b];
-        if (run >= k) break;
+#pragma unroll
+    for (int w = 0; w < 2; w++) {
+      const int kk = w == 0 ? k1 : k2;
+      if (excl < kk && incl >= kk) {
+        int run = excl, b = lane * (kSelBins / 32);
+        for (;; b++) {
+          run += hist[b];
+          if (run >= kk) break;
+        }
+        s_bin[w] = b;
       }
-      *s_bin = b;
     }
   }
   __syncthreads();
-  const int kb = *s_bin;
-  float mx = -INFINITY;
+  const int kb1 = s_bin[0], kb2 = s_bin[1];
+  float m1 = -INFINITY, m2 = -INFINITY;
   for_each_candidate(R, s_cnt, cs, [&](uint2 ent) {
     const float v = __uint_as_float(ent.y);
-    if (bin_of(v) <= kb) mx = fmaxf(mx, v);
+    const int b = bin_of(v);
+    if (b <= kb1) m1 = fmaxf(m1, v);
+    if (b <= kb2) m2 = fmaxf(m2, v);
   });
 #pragma unroll
-  for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+  for (int o = 16; o > 0; o >>= 1) {
+    m1 = fmaxf(m1, __shfl_xor_sync(0xffffffffu, m1, o));
+    m2 = fmaxf(m2, __shfl_xor_sync(0xffffffffu, m2, o));
+  }
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  if (lane == 0) s_red[64 + warp] = mx;
+  if (lane == 0) { s_red[64 + warp] = m1; s_red[96 + warp] = m2; }
   __syncthreads();
-  float r = -INFINITY;
-  for (int w = 0; w < (int)(blockDim.x >> 5); w++) r = fmaxf(r, s_red[64 + w]);
+  float r1 = -INFINITY, r2 = -INFINITY;
+  for (int w = 0; w < (int)(blockDim.x >> 5); w++) {
+    r1 = fmaxf(r1, s_red[64 + w]);
+    r2 = fmaxf(r2, s_red[96 + w]);
+  }
   __syncthreads();
-  return r;
+  return make_float2(r1, r2);
 }
 
 struct LevelSelArgs {
@@ -857,29 +880,39 @@ struct LevelSelArgs {
   int64_t n;
   int k, pool, region;
   int nreg, stride;  // regions of the level and the count-array stride
-  float *r_out;      // (n) bound B = R + margin for the next level, +inf when fewer than k
+  int k2;            // shards > 1: ceil(k / shards), else 0
+  float *r_out;      // (n) bound B = R + margin for the next level, +inf when fewer than k;
+                     // k2 > 0: then (n) -(R2 + margin), R2 >= the k2-th smallest v
 };
 
 // one block per query: R_q for the next level; dynamic smem kSelStage * 8
 __global__ void __launch_bounds__(kSelThreads) tc_level_select_kernel(const LevelSelArgs a) {
   extern __shared__ __align__(1024) unsigned char smem_raw[];
   uint2 *cs = reinterpret_cast<uint2 *>(smem_raw);
-  __shared__ int hist[kSelBins], s_cnt[256], s_off[256], s_misc[2], s_bin;
-  __shared__ float s_red[96];
+  __shared__ int hist[kSelBins], s_cnt[256], s_off[256], s_misc[2], s_bin[2];
+  __shared__ float s_red[128];
   const int64_t q = blockIdx.x;
   const QueryRegions R = load_regions(a.cand, a.ccount, q, a.pool, a.region, a.nreg, a.stride,
                                       s_cnt, s_off, s_misc);
   // entries lost to a full region only make R larger than it could be: still a
   // valid bound, since R is taken over real rows that were kept
-  float r = INFINITY;
-  if (R.total >= a.k) {
+  const int k2 = a.k2 > 0 ? a.k2 : a.k;
+  float2 r = make_float2(INFINITY, INFINITY);
+  if (R.total >= k2) {
     float vmin, vmax;
     stage_candidates(R, s_cnt, s_off, cs, s_red, &vmin, &vmax);
-    r = block_kth_bound(R, s_cnt, cs, a.k, vmin, vmax, hist, s_red, &s_bin);
+    r = block_kth_bounds(R, s_cnt, cs, min(a.k, R.total), k2, vmin, vmax, hist, s_red, s_bin);
+    if (R.total < a.k) r.x = INFINITY;
   }
-  // B = R + margin bounds the k-th reference distance minus ||q||^2 from above; it is
-  // what other shards of a sharded search may share (their minimum stays a bound)
-  if (threadIdx.x == 0) a.r_out[q] = __fadd_ru(r, a.qinfo[q].y);
+  // B = R + margin bounds the k-th reference distance minus ||q||^2 from above; the
+  // minimum of B over the shards of a sharded search stays a bound.  So does the
+  // maximum over the shards of R2 + margin: the shards together hold at least
+  // shards * k2 >= k rows below it; it is stored negated, for a MIN reduction.
+  if (threadIdx.x == 0) {
+    const float m = a.qinfo[q].y;
+    a.r_out[q] = __fadd_ru(r.x, m);
+    if (a.k2 > 0) a.r_out[a.n + q] = -__fadd_ru(r.y, m);
+  }
 }
 
 struct SelArgs {
@@ -891,6 +924,8 @@ struct SelArgs {
   const float2 *qinfo;
   const uint2 *cand;
   const int *ccount;
+  const float *r_shared;  // bounds B shared by every shard of a sharded search, or null
+  bool two_bounds;        // r_shared holds (n) B and (n) -B2
   int *fb_list;       // queries left to the SIMT engine
   WsHeader *hdr;
   float *out_d;
@@ -904,8 +939,8 @@ __global__ void __launch_bounds__(kSelThreads) tc_final_select_kernel(const SelA
   uint2 *cs = reinterpret_cast<uint2 *>(smem_raw);
   uint64_t *keys = reinterpret_cast<uint64_t *>(cs + kSelStage);
   float *qs = reinterpret_cast<float *>(keys + kSurvCap);
-  __shared__ int hist[kSelBins], s_cnt[256], s_off[256], s_misc[2], s_bin, s_nsurv;
-  __shared__ float s_red[96];
+  __shared__ int hist[kSelBins], s_cnt[256], s_off[256], s_misc[2], s_bin[2], s_nsurv;
+  __shared__ float s_red[128];
   const int64_t q = blockIdx.x;
   const QueryRegions R = load_regions(a.cand, a.ccount, q, a.pool, a.region, a.nreg, a.stride,
                                       s_cnt, s_off, s_misc);
@@ -922,8 +957,14 @@ __global__ void __launch_bounds__(kSelThreads) tc_final_select_kernel(const SelA
   float vmin, vmax;
   stage_candidates(R, s_cnt, s_off, cs, s_red, &vmin, &vmax);
   float theta = INFINITY;  // fewer than k candidates: keep them all
-  if (R.total >= a.k)
-    theta = __fadd_ru(__fadd_ru(block_kth_bound(R, s_cnt, cs, a.k, vmin, vmax, hist, s_red, &s_bin),
+  if (a.r_shared) {
+    // B bounds the k-th reference distance over every shard (minus ||q||^2), so the
+    // rows of the global top-k in this shard all have v <= B + margin; this shard
+    // then returns fewer than k rows when the others hold the rest
+    theta = __fadd_ru(read_bound(a.r_shared, a.n, q, a.two_bounds), a.qinfo[q].y);
+  } else if (R.total >= a.k)
+    theta = __fadd_ru(__fadd_ru(block_kth_bounds(R, s_cnt, cs, a.k, a.k, vmin, vmax, hist, s_red,
+                                                 s_bin).x,
                                 a.qinfo[q].y),
                       a.qinfo[q].y);
   __syncthreads();
@@ -1128,7 +1169,7 @@ bool tc_make_plan(int64_t n, int64_t m, int d, int k, int slices, int pool, bool
   P.off_xscale = off;   off = al256(off + (size_t)P.x_tiles * kColGroups * 4 + 16);
   P.off_qh = off;       off = al256(off + (size_t)q_rows * P.d_pad * 2);
   P.off_qinfo = off;    off = al256(off + (size_t)q_rows * 8);
-  P.off_rlev = off;     off = al256(off + (size_t)n * 4);
+  P.off_rlev = off;     off = al256(off + (size_t)n * 8);  // two bounds per query
   P.off_cand = off;     off = al256(off + (size_t)n * P.cand_cap * 8);
   P.off_ccount = off;   off = al256(off + (size_t)n * kColGroups * max_s * 4);
   P.off_flags = off;    off = al256(off + (size_t)n * 4);
@@ -1172,7 +1213,7 @@ static bool make_tmap(CUtensorMap *map, const void *base, int64_t rows, int cols
 
 int tc_run(const float *Q, const float *X, int64_t id_offset, float *out_d, int32_t *out_i,
            void *ws_, const TcPlan &p, cudaStream_t stream, cudaEvent_t t0, cudaEvent_t t1,
-           int *launches, LevelHook hook, void *hook_user) {
+           int *launches, LevelHook hook, void *hook_user, int shards) {
   unsigned char *ws = static_cast<unsigned char *>(ws_);
   WsHeader *hdr = reinterpret_cast<WsHeader *>(ws);
   __half *Xh = reinterpret_cast<__half *>(ws + p.off_xh);
@@ -1241,10 +1282,13 @@ int tc_run(const float *Q, const float *X, int64_t id_offset, float *out_d, int3
   A.cand = cand;
   A.ccount = ccount;
   A.hdr = hdr;
+  // shards that share bounds also share a second one per query (see tc_level_select_kernel)
+  const bool two = hook != nullptr && shards > 1;
   for (int l = 0; l < p.levels; l++) {
     const LevelPlan &lv = p.level[l];
     const bool last = l == p.levels - 1;
     A.r_in = l == 0 ? nullptr : rlev;
+    A.two_bounds = two;
     A.level_tiles = lv.tiles;
     A.slices = lv.slices;
     A.tiles_per_slice = (int)lv.tiles_per_slice;
@@ -1271,7 +1315,9 @@ int tc_run(const float *Q, const float *X, int64_t id_offset, float *out_d, int3
     if (last && t1) cudaEventRecord(t1, stream);
     nl++;
     BFK_TRY(cudaGetLastError());
-    if (!last) {
+    // after the last level too when the shards share bounds: the final select then
+    // keeps only rows that can be in the global top-k
+    if (!last || hook) {
       LevelSelArgs S{};
       S.cand = cand;
       S.ccount = ccount;
@@ -1283,11 +1329,12 @@ int tc_run(const float *Q, const float *X, int64_t id_offset, float *out_d, int3
       S.nreg = kColGroups * lv.slices;  // regions: column groups of every slice
       S.stride = kColGroups * p.max_slices;
       S.r_out = rlev;
+      S.k2 = two ? (p.k + shards - 1) / shards : 0;
       tc_level_select_kernel<<<(unsigned)p.n, kSelThreads, lsmem, stream>>>(S);
       nl++;
       BFK_TRY(cudaGetLastError());
       // a sharded search replaces each query's bound by the minimum over all shards
-      if (hook) hook(rlev, p.n, hook_user, stream);
+      if (hook) hook(rlev, two ? 2 * p.n : p.n, hook_user, stream);
     }
   }
 
@@ -1308,6 +1355,8 @@ int tc_run(const float *Q, const float *X, int64_t id_offset, float *out_d, int3
   S.qinfo = qinfo;
   S.cand = cand;
   S.ccount = ccount;
+  S.r_shared = hook ? rlev : nullptr;
+  S.two_bounds = two;
   S.fb_list = fb_list;
   S.hdr = hdr;
   S.out_d = out_d;

@@ -66,13 +66,15 @@ class _DeviceArray:
 def search(Q, X, k: int, *, engine: str = "auto", slices: int = 0, max_candidates: int = 0,
            id_offset: int = 0, out: tuple[torch.Tensor, torch.Tensor] | None = None,
            ws: torch.Tensor | None = None, time_main: bool = False, cta_pair: bool = False,
-           bound_hook=None, plan_rows: int = 0):
+           bound_hook=None, plan_rows: int = 0, shards: int = 0):
     """Exact k-NN on the GPU.  Returns (dists, ids) device tensors.
 
     ``bound_hook(t)``, if given, is called by the tensor-core engine after each
-    sampling level with ``t``, a float32 CUDA tensor (n,) of per-query bounds
-    that it may lower in place (a sharded search takes the minimum over
-    shards).  ``plan_rows`` makes shards of one search plan the same levels.
+    filter level with ``t``, a float32 CUDA tensor of per-query bounds that it
+    may lower in place (a sharded search takes the minimum over shards): (n,)
+    values, or (2n,) when ``shards`` > 1 (the number of shards in that minimum;
+    see ``bfk_level_hook_t``).  ``plan_rows`` makes shards of one search plan
+    the same levels.
     """
     Q = as_device_f32(Q, "Q")
     X = as_device_f32(X, "X")
@@ -90,6 +92,7 @@ def search(Q, X, k: int, *, engine: str = "auto", slices: int = 0, max_candidate
                           (_lib.FLAG_TIME_MAIN if time_main else 0) |
                           (_lib.FLAG_CTA_PAIR if cta_pair else 0))
     opts.plan_rows = int(plan_rows)
+    opts.shards = int(shards)
     hook_error = []
     if bound_hook is not None:
         def _hook(ptr, count, user, stream_ptr):
@@ -121,13 +124,16 @@ def search(Q, X, k: int, *, engine: str = "auto", slices: int = 0, max_candidate
 
 
 def last_stats(Q, X, k: int, *, engine: str = "auto", slices: int = 0,
-               max_candidates: int = 0) -> dict:
-    """Statistics of the last search of this shape on the current stream's workspace."""
+               max_candidates: int = 0, plan_rows: int = 0, shards: int = 0) -> dict:
+    """Statistics of the last search of this shape on the current stream's workspace
+    (pass the search's own engine options)."""
     Q = as_device_f32(Q, "Q")
     X = as_device_f32(X, "X")
     n, d = Q.shape
     m = X.shape[0]
     opts = _lib.make_opts(engine, slices, max_candidates)
+    opts.plan_rows = int(plan_rows)
+    opts.shards = int(shards)
     with torch.cuda.device(Q.device):
         stream = torch.cuda.current_stream()
         ws = workspace(workspace_size(n, m, d, k, opts), Q.device, stream)

@@ -36,39 +36,56 @@ def gather_lists(d_: torch.Tensor, i_: torch.Tensor, group=None) -> tuple[torch.
     return all_d.view(world, n, k), all_i.view(world, n, k)
 
 
+def make_local_search(group=None, plan_rows: int = 0, **search_kwargs) -> Callable:
+    """The per-shard search of `sharded_search` with the CUDA engine.
+
+    Every rank must use the same `plan_rows` (the largest shard's row count);
+    0 looks it up with an all-reduce on the first call.  With more than one
+    rank, the engine's level hook all-reduces (MIN) each query's bounds over
+    `group` after every filter level; `search_kwargs` go to `engine.search`.
+    """
+    from .engine import search
+    world = dist.get_world_size(group) if dist.is_initialized() else 1
+    state = {"plan_rows": int(plan_rows)}
+
+    def share_bounds(t):
+        # both halves of `t` are minimised: see bfk_level_hook_t
+        dist.all_reduce(t, op=dist.ReduceOp.MIN, group=group)
+
+    def local_search(Q_, X_, k_, id_offset):
+        if world > 1 and state["plan_rows"] <= 0:
+            sizes = torch.tensor([X_.shape[0]], dtype=torch.int64, device=X_.device)
+            dist.all_reduce(sizes, op=dist.ReduceOp.MAX, group=group)
+            state["plan_rows"] = int(sizes.item())
+        return search(Q_, X_, k_, id_offset=id_offset,
+                      bound_hook=share_bounds if world > 1 else None,
+                      plan_rows=state["plan_rows"] if world > 1 else 0,
+                      shards=world if world > 1 else 0, **search_kwargs)
+
+    return local_search
+
+
 def sharded_search(Q, X_shard, k: int, row_begin: int, group=None,
                    local_search: Callable | None = None,
                    merge_fn: Callable | None = None, plan_rows: int = 0,
                    **search_kwargs) -> tuple[torch.Tensor, torch.Tensor]:
     """Exact k-NN over the union of every rank's shard; result on every rank.
 
-    With the CUDA engine, the ranks also share each query's sampled distance
-    bound after every sampling level (an all-reduce MIN of n floats): the
-    minimum over shards bounds the global k-th distance, so every shard filters
-    with the tightest bound any shard found.  `plan_rows` (the largest shard's
-    row count; looked up with an all-reduce when 0) gives every shard the same
-    sampling levels, so all ranks take the same collective steps.
+    With the CUDA engine, the ranks also share each query's distance bounds
+    after every filter level (an all-reduce MIN of 2n floats): the minimum over
+    shards of each shard's k-th smallest value, and the maximum over shards of
+    each shard's ceil(k / world)-th smallest value, both bound the global k-th
+    distance, so every shard filters with the tightest bound and keeps about
+    1/world of the candidates.  `plan_rows` (the largest shard's row count;
+    looked up with an all-reduce when 0) gives every shard the same levels, so
+    all ranks take the same collective steps.
 
     `local_search(Q, X, k, id_offset)` and `merge_fn(all_d, all_i, k)` default
     to the CUDA engine; tests substitute CPU stand-ins to exercise the
     orchestration over gloo.  `search_kwargs` go to `engine.search`.
     """
     if local_search is None:
-        from .engine import search
-        world = dist.get_world_size(group) if dist.is_initialized() else 1
-        if world > 1 and plan_rows <= 0:
-            sizes = torch.tensor([X_shard.shape[0]], dtype=torch.int64, device=X_shard.device)
-            dist.all_reduce(sizes, op=dist.ReduceOp.MAX, group=group)
-            plan_rows = int(sizes.item())
-
-        def share_bounds(t):
-            # the minimum over shards of each query's bound is still a bound for all
-            dist.all_reduce(t, op=dist.ReduceOp.MIN, group=group)
-
-        def local_search(Q_, X_, k_, id_offset):
-            return search(Q_, X_, k_, id_offset=id_offset,
-                          bound_hook=share_bounds if world > 1 else None,
-                          plan_rows=plan_rows if world > 1 else 0, **search_kwargs)
+        local_search = make_local_search(group, plan_rows, **search_kwargs)
     if merge_fn is None:
         from .engine import merge as merge_fn
     d_, i_ = local_search(Q, X_shard, k, row_begin)

@@ -52,19 +52,26 @@ typedef enum {
 #define BFK_FLAG_CTA_PAIR 2  /* TC engine: CTA pairs (tcgen05.mma.cta_group::2, M = 256)  */
 
 /*
- * Called by the TC engine after each sampling level with `bound` (device, n
- * floats): per query an upper bound on (k-th distance - ||q||^2) plus the
- * query's error margin.  A sharded search replaces every value by its minimum
- * over all shards, enqueued on `stream`, before returning.  Optional.
+ * Called by the TC engine after each filter level with `bound` (device, `count`
+ * floats).  A sharded search replaces every value by its minimum over all
+ * shards, enqueued on `stream`, before returning.  Optional.
+ *   shards <= 1: count = n, per query an upper bound on (k-th distance - ||q||^2)
+ *                plus the query's error margin;
+ *   shards > 1:  count = 2n, that bound followed by the negated bound that the
+ *                shard's ceil(k / shards)-th smallest value gives (its minimum is
+ *                minus the maximum over the shards, which bounds the k-th
+ *                distance of the union).
  */
-typedef void (*bfk_level_hook_t)(float *bound, int64_t n, void *user, void *stream);
+typedef void (*bfk_level_hook_t)(float *bound, int64_t count, void *user, void *stream);
 
 typedef struct {
   int32_t engine;         /* bfk_engine_t                                                */
   int32_t slices;         /* database slices per query block, 0 = auto                   */
   int32_t max_candidates; /* TC engines: per-query candidate pool, 0 = auto              */
   int32_t flags;          /* BFK_FLAG_*                                                  */
-  int32_t reserved[4];    /* must be zero                                                */
+  int32_t shards;         /* TC engine: shards whose level_hook reduces over all of them
+                             (the process group size), 0 = this search alone          */
+  int32_t reserved[3];    /* must be zero                                                */
   bfk_level_hook_t level_hook; /* TC engine: see bfk_level_hook_t, NULL = none           */
   void *hook_user;        /* passed to level_hook                                        */
   int64_t plan_rows;      /* TC engine: rows the sampling levels are planned for, 0 = m.

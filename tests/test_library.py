@@ -47,7 +47,10 @@ def test_argument_validation_without_gpu(lib):
     assert lib.bfk_workspace_size(-1, 10, 8, 1, ctypes.byref(o), ctypes.byref(nb)) == 1
     assert lib.bfk_workspace_size(10, 10, 8, 0, ctypes.byref(o), ctypes.byref(nb)) == 1
     assert lib.bfk_workspace_size(10, 10, 8, 5000, ctypes.byref(o), ctypes.byref(nb)) == 2
-    o.reserved[3] = 1
+    o.reserved[2] = 1
+    assert lib.bfk_workspace_size(10, 10, 8, 1, ctypes.byref(o), ctypes.byref(nb)) == 1
+    o = _lib.make_opts()
+    o.shards = -1
     assert lib.bfk_workspace_size(10, 10, 8, 1, ctypes.byref(o), ctypes.byref(nb)) == 1
     o = _lib.make_opts("direct")
     assert lib.bfk_workspace_size(1024, 65536, 128, 10, ctypes.byref(o), ctypes.byref(nb)) == 0
