@@ -219,7 +219,10 @@ def main(argv=None) -> int:
     for _ in range(a.warmup):
         step()
     torch.cuda.synchronize()
-    engine.last_stats(Qd, Xd, k, engine=a.engine)  # clear timing records
+    # the stats calls pass the search's own plan options (same workspace size)
+    stat_opts = dict(engine=a.engine, plan_rows=plan_rows if world > 1 else 0,
+                     shards=world if world > 1 else 0)
+    engine.last_stats(Qd, Xd, k, **stat_opts)  # clear timing records
     barrier()
     torch.cuda.synchronize()
     sampler = ClockSampler(local)
@@ -234,7 +237,7 @@ def main(argv=None) -> int:
     barrier()
     clocks = sampler.stop()
     t_ms = ev0.elapsed_time(ev1) / a.steps
-    stats = engine.last_stats(Qd, Xd, k, engine=a.engine)
+    stats = engine.last_stats(Qd, Xd, k, **stat_opts)
     main_ms = stats["main_kernel_ms"] / max(1, stats["timed_calls"])
     tt = torch.tensor([t_ms, main_ms], device=device, dtype=torch.float64)
     if world > 1:

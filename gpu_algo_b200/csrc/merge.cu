@@ -62,9 +62,59 @@ __global__ void __launch_bounds__(kMergeThreads) knn_merge_kernel(
   }
 }
 
+// Merge by rank, for lists * k <= kMergeCap: every key's place in the merged order
+// is its index in its own list plus, in every other list, the number of keys
+// before it (binary searches; equal keys order by list), so one pass places
+// each of the first k keys without a sort.  grid (n), dynamic smem lists*k*8.
+__global__ void __launch_bounds__(kMergeThreads) knn_merge_rank_kernel(
+    const float *__restrict__ cand_d, const int32_t *__restrict__ cand_i, int64_t n, int lists,
+    int k, float *__restrict__ out_d, int32_t *__restrict__ out_i) {
+  extern __shared__ __align__(16) uint64_t keys[];
+  const int64_t qi = blockIdx.x;
+  const int total = lists * k;
+  for (int e = threadIdx.x; e < total; e += blockDim.x) {
+    const int l = e / k, j = e - l * k;
+    const int64_t off = ((int64_t)l * n + qi) * k + j;
+    keys[e] = pair_key(cand_d[off], cand_i[off]);
+  }
+  __syncthreads();
+  for (int e = threadIdx.x; e < total; e += blockDim.x) {
+    const int l = e / k;
+    int rank = e - l * k;
+    const uint64_t key = keys[e];
+    for (int o = 0; o < lists && rank < k; o++) {
+      if (o == l) continue;
+      // keys of list o before this one: < key, or <= key for a list that comes first
+      const uint64_t *b = keys + o * k;
+      int lo = 0, hi = k;
+      if (o < l) {
+        while (lo < hi) { const int mid = (lo + hi) >> 1; if (b[mid] <= key) lo = mid + 1; else hi = mid; }
+      } else {
+        while (lo < hi) { const int mid = (lo + hi) >> 1; if (b[mid] < key) lo = mid + 1; else hi = mid; }
+      }
+      rank += lo;
+    }
+    if (rank < k) {
+      const bool pad = key == ~0ull;
+      out_d[qi * k + rank] = pad ? BFK_PAD_DIST : ord2f((uint32_t)(key >> 32));
+      out_i[qi * k + rank] = pad ? -1 : (int32_t)(uint32_t)(key & 0xffffffffu);
+    }
+  }
+}
+
 cudaError_t launch_merge(const float *cand_d, const int32_t *cand_i, int64_t n, int lists, int k,
                          float *out_d, int32_t *out_i, cudaStream_t stream) {
   if (n == 0) return cudaSuccess;
+  if ((int64_t)lists * k <= kMergeCap) {
+    const size_t rsmem = (size_t)lists * k * sizeof(uint64_t);
+    cudaError_t e = cudaFuncSetAttribute((const void *)knn_merge_rank_kernel,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         (int)(kMergeCap * sizeof(uint64_t)));
+    if (e != cudaSuccess) return e;
+    knn_merge_rank_kernel<<<(unsigned)n, kMergeThreads, rsmem, stream>>>(cand_d, cand_i, n, lists,
+                                                                          k, out_d, out_i);
+    return cudaGetLastError();
+  }
   const size_t smem = (size_t)kMergeCap * sizeof(uint64_t);
   cudaError_t e = cudaFuncSetAttribute((const void *)knn_merge_kernel,
                                        cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);

@@ -143,6 +143,24 @@ def test_merge_kernel_matches_oracle_merge(plumbing):
     assert_exact(md.cpu().numpy(), mi.cpu().numpy(), ed, ei, "merge")
 
 
+@pytest.mark.parametrize("lists,k", [(2, 100), (8, 100), (100, 100), (3, 1000)])
+def test_merge_rank_and_grouped_paths(lists, k):
+    """lists * k <= 8192 merges by rank, larger sets by grouped sorts; ties in
+    distance across lists order by index; padding sits at the end of a list."""
+    rng = np.random.Generator(np.random.PCG64(lists * 1000 + k))
+    n = 64
+    cd = np.sort(rng.integers(0, 50, size=(lists, n, k)).astype(np.float32), axis=2)
+    ci = rng.permutation(lists * n * k).astype(np.int32).reshape(lists, n, k)
+    order = np.lexsort((ci, cd), axis=2)
+    cd = np.take_along_axis(cd, order, axis=2)
+    ci = np.take_along_axis(ci, order, axis=2)
+    cd[0, :, k // 3:] = np.float32(3.402823e38)
+    ci[0, :, k // 3:] = -1
+    ed, ei = oracle_merge(cd, ci, k)
+    md, mi = engine.merge(dev(cd), dev(ci), k)
+    assert_exact(md.cpu().numpy(), mi.cpu().numpy(), ed, ei, f"merge {lists}x{k}")
+
+
 def test_large_k_and_high_d():
     rng = np.random.Generator(np.random.PCG64(11))
     X = rng.standard_normal((20_000, 960), dtype=np.float32)
