@@ -29,6 +29,7 @@
 #include <cuda.h>
 #include <cudaTypedefs.h>
 
+#include <algorithm>
 #include <cfloat>
 #include <cmath>
 
@@ -132,6 +133,14 @@ __device__ __forceinline__ float max3f(float a, float b, float c) {
   float d;
   asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
   return d;
+}
+// v[i] for a lane-varying i in [0, 8), by selects (no local-memory indexing)
+__device__ __forceinline__ float pick8(const float *v, int i) {
+  const bool b0 = i & 1, b1 = i & 2, b2 = i & 4;
+  const float s0 = b0 ? v[1] : v[0], s1 = b0 ? v[3] : v[2];
+  const float s2 = b0 ? v[5] : v[4], s3 = b0 ? v[7] : v[6];
+  const float t0 = b1 ? s1 : s0, t1 = b1 ? s3 : s2;
+  return b2 ? t1 : t0;
 }
 // maximum of 8 accumulator values (FP32 bit patterns)
 __device__ __forceinline__ float max8u(const uint32_t *a) {
@@ -433,28 +442,18 @@ __global__ void __maxnreg__(96)
               fma2(__uint_as_float(acc[2]), __uint_as_float(acc[3]), cscale, n0.z, n0.w, v[2], v[3]);
               fma2(__uint_as_float(acc[4]), __uint_as_float(acc[5]), cscale, n1.x, n1.y, v[4], v[5]);
               fma2(__uint_as_float(acc[6]), __uint_as_float(acc[7]), cscale, n1.z, n1.w, v[6], v[7]);
-              if (gb[g] <= theta) {
-                // this lane's kept columns, appended with predicated stores
-                const uint32_t rg = row0 + hh * 32 + 8 * g;
-                if (cnt + 8 <= a.region) {
-                  uint2 *wp = region + cnt;
+              // this lane's kept columns as a bit mask; one append per set bit (usually
+              // none or one), the value picked from registers by a select chain
+              unsigned keep = 0;
 #pragma unroll
-                  for (int i = 0; i < 8; i++) {
-                    const bool keep = v[i] <= theta;
-                    if (keep) *wp = make_uint2(rg + i, __float_as_uint(v[i]));
-                    wp += keep ? 1 : 0;
-                  }
-                  cnt = (int)(wp - region);
-                } else {
-                  // near the end of the region: a full region keeps overwriting its last slot
-#pragma unroll
-                  for (int i = 0; i < 8; i++) {
-                    if (v[i] <= theta) {
-                      region[min(cnt, last)] = make_uint2(rg + i, __float_as_uint(v[i]));
-                      cnt++;
-                    }
-                  }
-                }
+              for (int i = 0; i < 8; i++) keep |= (v[i] <= theta ? 1u : 0u) << i;
+              const uint32_t rg = row0 + hh * 32 + 8 * g;
+              while (keep) {
+                const int i = __ffs(keep) - 1;
+                keep &= keep - 1;
+                // a full region keeps overwriting its last slot (the count tells)
+                region[min(cnt, last)] = make_uint2(rg + i, __float_as_uint(pick8(v, i)));
+                cnt++;
               }
             }
           }
