@@ -36,10 +36,12 @@ from gpu_algo_b200.sharded import shard_range  # noqa: E402
 
 FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0}
 DEFAULT_WORKLOAD = "unit-10m"
-# DRAM bytes per database row of one main-filter launch, keyed by (workload, queries, d, k):
-# ncu dram__bytes_read.sum + dram__bytes_write.sum of the launch over all rows of a
-# 3,000,000-row sample ((1.350 + 0.378) GB / 3M rows), single-CTA kernel
-TRAFFIC_PER_ROW = {("unit-10m", 10_000, 128, 100): 576}
+# DRAM bytes read per database row by one main-filter launch, keyed by (workload, queries,
+# d, k): ncu dram__bytes_read.sum of the launch over all rows of a 3,000,000-row sample
+# (1.242 GB / 3M rows), single-CTA kernel.  Its writes are the candidate appends, 8 bytes
+# each (0.386 GB for the sample's 41.3M candidates, 9.3 B each with write granularity).
+TRAFFIC_READ_PER_ROW = {("unit-10m", 10_000, 128, 100): 414}
+TRAFFIC_WRITE_PER_CANDIDATE = 9.3
 
 
 def parse_args(argv=None):
@@ -282,12 +284,12 @@ def main(argv=None) -> int:
     peaks = load_peaks()
     m_shard = r1 - r0
     # DRAM bytes of one main-filter launch, from an ncu capture of a smaller case of the
-    # same workload, scaled by rows (the traffic is the f16 rows fetched once per group of
-    # query tiles that share L2, plus the candidate appends: both grow with the rows)
+    # same workload: the reads scale with the rows (the f16 rows, fetched again by some of
+    # the query tiles), the writes with the candidates the launch appended
     traffic = None
-    per_row = TRAFFIC_PER_ROW.get((a.workload, Qn, d, k))
+    per_row = TRAFFIC_READ_PER_ROW.get((a.workload, Qn, d, k))
     if per_row is not None and stats["engine"] == "tc_f16":
-        traffic = per_row * m_shard
+        traffic = per_row * m_shard + TRAFFIC_WRITE_PER_CANDIDATE * stats["candidates"]
     flops = 2.0 * Qn * m_shard * d  # algorithmic, per launch of the main kernel on one GPU
     achieved = flops / (main_max / 1e3) / 1e12 if main_max > 0 else None
     roofline = {
@@ -298,8 +300,9 @@ def main(argv=None) -> int:
         "unit": "TFLOP/s",
         "frac": (achieved / peaks["bf16_tflops"]) if achieved else None,
         "traffic": traffic,
-        "traffic_source": (f"ncu dram__bytes_read+write of a smaller row sample, "
-                           f"{per_row} B per row x {m_shard} rows") if traffic else None,
+        "traffic_source": (f"ncu dram__bytes of a 3M-row sample: {per_row} B read per row x "
+                           f"{m_shard} rows + {TRAFFIC_WRITE_PER_CANDIDATE} B written per "
+                           f"candidate x {stats['candidates']}") if traffic else None,
         "peak_source": f"{peaks['source']} dense bf16 (burst)",
         "main_kernel_ms": main_max,
         "algorithmic": "2*Q*N_shard*d flops per launch",

@@ -53,6 +53,7 @@ constexpr int kMaxKch = 16;         // d <= 1024: query K chunks stream with the
 constexpr int kTcMaxK = 512;
 constexpr int kSelThreads = 256;
 constexpr int kSurvCap = 2048;      // exact re-rank capacity per query
+constexpr int kRankSortMax = 512;   // survivors ordered by rank counting up to this many
 constexpr int kDefaultPool = 16384;  // candidate entries per query (all regions of a level)
 constexpr int kLevelTarget = 3072;   // expected candidates per query of a filter level
 
@@ -1014,15 +1015,37 @@ __global__ void __launch_bounds__(kSelThreads) tc_final_select_kernel(const SelA
     }
   }
   __syncthreads();
-  int P = 2;
-  while (P < ns) P <<= 1;
-  for (int e = ns + threadIdx.x; e < P; e += blockDim.x) keys[e] = ~0ull;
-  bitonic_sort_u64(keys, P);
-  for (int j = threadIdx.x; j < a.k; j += blockDim.x) {
-    const uint64_t key = j < ns ? keys[j] : ~0ull;
-    const bool pad = key == ~0ull;
-    a.out_d[q * a.k + j] = pad ? BFK_PAD_DIST : ord2f((uint32_t)(key >> 32));
-    a.out_i[q * a.k + j] = pad ? -1 : (int32_t)(uint32_t)(key & 0xffffffffu);
+  if (ns <= kRankSortMax) {
+    // few survivors: each key's place is the number of keys before it (equal keys,
+    // the non-finite distances, order by slot), one pass and no block-wide sort
+    for (int e = threadIdx.x; e < ns; e += blockDim.x) {
+      const uint64_t key = keys[e];
+      int rank = 0;
+      for (int j = 0; j < ns; j++) {
+        const uint64_t kj = keys[j];
+        rank += (kj < key || (kj == key && j < e)) ? 1 : 0;
+      }
+      if (rank < a.k) {
+        const bool pad = key == ~0ull;
+        a.out_d[q * a.k + rank] = pad ? BFK_PAD_DIST : ord2f((uint32_t)(key >> 32));
+        a.out_i[q * a.k + rank] = pad ? -1 : (int32_t)(uint32_t)(key & 0xffffffffu);
+      }
+    }
+    for (int j = ns + threadIdx.x; j < a.k; j += blockDim.x) {
+      a.out_d[q * a.k + j] = BFK_PAD_DIST;
+      a.out_i[q * a.k + j] = -1;
+    }
+  } else {
+    int P = 2;
+    while (P < ns) P <<= 1;
+    for (int e = ns + threadIdx.x; e < P; e += blockDim.x) keys[e] = ~0ull;
+    bitonic_sort_u64(keys, P);
+    for (int j = threadIdx.x; j < a.k; j += blockDim.x) {
+      const uint64_t key = j < ns ? keys[j] : ~0ull;
+      const bool pad = key == ~0ull;
+      a.out_d[q * a.k + j] = pad ? BFK_PAD_DIST : ord2f((uint32_t)(key >> 32));
+      a.out_i[q * a.k + j] = pad ? -1 : (int32_t)(uint32_t)(key & 0xffffffffu);
+    }
   }
   if (threadIdx.x == 0) {
     atomicAdd(&a.hdr->survivors, (unsigned long long)ns);
