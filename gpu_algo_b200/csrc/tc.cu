@@ -734,8 +734,6 @@ __device__ QueryRegions load_regions(const uint2 *cand, const int *ccount, int64
 }
 
 constexpr int kSelStage = 6144;  // candidates staged in shared memory (more: read in place)
-// the final select reuses the staging area for its warps' 32 x 33 row chunks
-static_assert((kSelThreads / 32) * 32 * 33 * 4 <= kSelStage * 8, "row chunks exceed the staging area");
 constexpr int kSelBins = 1024;
 
 // Copy the candidates into shared memory and return the block-wide min and max
@@ -924,23 +922,50 @@ struct SelArgs {
   const float2 *qinfo;
   const uint2 *cand;
   const int *ccount;
-  const float *r_shared;  // bounds B shared by every shard of a sharded search, or null
-  bool two_bounds;        // r_shared holds (n) B and (n) -B2
+  const float *r_bound;   // bounds B of the last level (minimised over the shards of a
+                          // sharded search)
+  bool two_bounds;        // r_bound holds (n) B and (n) -B2
   int *fb_list;       // queries left to the SIMT engine
   WsHeader *hdr;
   float *out_d;
   int32_t *out_i;
 };
 
-// one block per query; dynamic smem: kSelStage * 8 (staged candidates) +
-// kSurvCap * 8 (survivor keys) + d * 4 (query)
+// Apply f(entry) to every candidate of R read from global memory: thread t takes
+// entries t, t + B, ... of the regions' concatenation, four loads in flight at a
+// time (the region of an entry: the last whose prefix offset is <= its position).
+template <class F>
+__device__ __forceinline__ void scan_candidates(const QueryRegions &R, const int *s_off, F f) {
+  for (int e0 = threadIdx.x; e0 < R.total; e0 += 4 * blockDim.x) {
+    uint2 ent[4];
+#pragma unroll
+    for (int u = 0; u < 4; u++) {
+      const int e = e0 + u * (int)blockDim.x;
+      ent[u] = make_uint2(0u, 0x7fc00000u);  // NaN: never a survivor
+      if (e < R.total) {
+        int lo = 0, hi = R.nreg - 1;
+        while (lo < hi) {
+          const int mid = (lo + hi + 1) >> 1;
+          if (s_off[mid] <= e) lo = mid; else hi = mid - 1;
+        }
+        ent[u] = R.base[(size_t)lo * R.region + (e - s_off[lo])];
+      }
+    }
+#pragma unroll
+    for (int u = 0; u < 4; u++) f(ent[u]);
+  }
+}
+
+constexpr int kRerankDims = 16;  // dimensions of a survivor row staged at a time
+
+// one block per query; dynamic smem: kSurvCap * 8 (survivor keys) +
+// warps * 32 * (kRerankDims + 1) * 4 (row chunks) + d * 4 (query)
 __global__ void __launch_bounds__(kSelThreads) tc_final_select_kernel(const SelArgs a) {
   extern __shared__ __align__(1024) unsigned char smem_raw[];
-  uint2 *cs = reinterpret_cast<uint2 *>(smem_raw);
-  uint64_t *keys = reinterpret_cast<uint64_t *>(cs + kSelStage);
-  float *qs = reinterpret_cast<float *>(keys + kSurvCap);
-  __shared__ int hist[kSelBins], s_cnt[256], s_off[256], s_misc[2], s_bin[2], s_nsurv;
-  __shared__ float s_red[128];
+  uint64_t *keys = reinterpret_cast<uint64_t *>(smem_raw);
+  float *rows = reinterpret_cast<float *>(keys + kSurvCap);
+  float *qs = rows + (kSelThreads / 32) * 32 * (kRerankDims + 1);
+  __shared__ int s_cnt[256], s_off[256], s_misc[2], s_nsurv;
   const int64_t q = blockIdx.x;
   const QueryRegions R = load_regions(a.cand, a.ccount, q, a.pool, a.region, a.nreg, a.stride,
                                       s_cnt, s_off, s_misc);
@@ -954,22 +979,15 @@ __global__ void __launch_bounds__(kSelThreads) tc_final_select_kernel(const SelA
   }
   for (int c = threadIdx.x; c < a.d; c += blockDim.x) qs[c] = a.Q[q * a.d + c];
   if (threadIdx.x == 0) s_nsurv = 0;
-  float vmin, vmax;
-  stage_candidates(R, s_cnt, s_off, cs, s_red, &vmin, &vmax);
-  float theta = INFINITY;  // fewer than k candidates: keep them all
-  if (a.r_shared) {
-    // B bounds the k-th reference distance over every shard (minus ||q||^2), so the
-    // rows of the global top-k in this shard all have v <= B + margin; this shard
-    // then returns fewer than k rows when the others hold the rest
-    theta = __fadd_ru(read_bound(a.r_shared, a.n, q, a.two_bounds), a.qinfo[q].y);
-  } else if (R.total >= a.k)
-    theta = __fadd_ru(__fadd_ru(block_kth_bounds(R, s_cnt, cs, a.k, a.k, vmin, vmax, hist, s_red,
-                                                 s_bin).x,
-                                a.qinfo[q].y),
-                      a.qinfo[q].y);
+  // B (from the level select of the last level, minimised over the shards of a
+  // sharded search) bounds the k-th reference distance minus ||q||^2, so the rows of
+  // the top k all have v <= B + margin.  B is +inf when there were fewer than k
+  // candidates: then every candidate survives.  A shard returns fewer than k rows
+  // when the other shards hold the rest.
+  const float theta = __fadd_ru(read_bound(a.r_bound, a.n, q, a.two_bounds), a.qinfo[q].y);
   __syncthreads();
   // survivors: the rows with v <= theta, listed in `keys`
-  for_each_candidate(R, s_cnt, cs, [&](uint2 ent) {
+  scan_candidates(R, s_off, [&](uint2 ent) {
     if (__uint_as_float(ent.y) <= theta) {
       const int slot = atomicAdd(&s_nsurv, 1);
       if (slot < kSurvCap) keys[slot] = ent.x;
@@ -985,30 +1003,33 @@ __global__ void __launch_bounds__(kSelThreads) tc_final_select_kernel(const SelA
     return;
   }
   // Exact distances with the reference arithmetic.  A warp takes 32 survivors
-  // at a time, one per lane; their rows pass through shared memory (the staged
-  // candidates are no longer needed) in chunks of 32 dimensions, loaded with
-  // coalesced reads, and each lane accumulates its own row in dimension order.
+  // at a time, one per lane; their rows pass through shared memory in chunks of
+  // kRerankDims dimensions: lanes (j, c) load element c of survivor j's chunk with
+  // coalesced reads, and each lane then accumulates its own row in dimension order.
   {
+    constexpr int W = kRerankDims, P = kRerankDims + 1;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nw = blockDim.x >> 5;
-    float *tile = reinterpret_cast<float *>(cs) + warp * (32 * 33);
+    float *tile = rows + warp * (32 * P);
     for (int b0 = warp * 32; b0 < ns; b0 += nw * 32) {
       const int nb = min(32, ns - b0);
       const uint32_t myrow = lane < nb ? (uint32_t)keys[b0 + lane] : 0u;
       float acc = 0.f;
-      for (int c0 = 0; c0 < a.d; c0 += 32) {
-        const int cw = min(32, a.d - c0);
-        float t[32];
+      const int c = lane % W, j0 = lane / W;  // this lane loads column c of survivors j0, j0+2, ...
+      for (int c0 = 0; c0 < a.d; c0 += W) {
+        const int cw = min(W, a.d - c0);
+        float t[32 / (32 / W)];
 #pragma unroll
-        for (int j = 0; j < 32; j++) {
+        for (int u = 0; u < 32 / (32 / W); u++) {
+          const int j = j0 + u * (32 / W);
           const uint32_t rj = __shfl_sync(0xffffffffu, myrow, j);
-          t[j] = (j < nb && lane < cw) ? __ldg(a.X + (size_t)rj * a.d + c0 + lane) : 0.f;
+          t[u] = (j < nb && c < cw) ? __ldg(a.X + (size_t)rj * a.d + c0 + c) : 0.f;
         }
         __syncwarp();
 #pragma unroll
-        for (int j = 0; j < 32; j++) tile[j * 33 + lane] = t[j];
+        for (int u = 0; u < 32 / (32 / W); u++) tile[(j0 + u * (32 / W)) * P + c] = t[u];
         __syncwarp();
         if (lane < nb)
-          for (int c = 0; c < cw; c++) acc = dist_step(qs[c0 + c], tile[lane * 33 + c], acc);
+          for (int cc = 0; cc < cw; cc++) acc = dist_step(qs[c0 + cc], tile[lane * P + cc], acc);
       }
       if (lane < nb)
         keys[b0 + lane] = acc == acc ? pair_key(acc, (int32_t)(a.id_offset + myrow)) : ~0ull;
@@ -1337,9 +1358,9 @@ int tc_run(const float *Q, const float *X, int64_t id_offset, float *out_d, int3
     if (last && t1) cudaEventRecord(t1, stream);
     nl++;
     BFK_TRY(cudaGetLastError());
-    // after the last level too when the shards share bounds: the final select then
-    // keeps only rows that can be in the global top-k
-    if (!last || hook) {
+    // after the last level too: the final select keeps the rows below its bound (on a
+    // sharded search, the bound shared by all shards: rows that can be in the global top-k)
+    {
       LevelSelArgs S{};
       S.cand = cand;
       S.ccount = ccount;
@@ -1377,13 +1398,14 @@ int tc_run(const float *Q, const float *X, int64_t id_offset, float *out_d, int3
   S.qinfo = qinfo;
   S.cand = cand;
   S.ccount = ccount;
-  S.r_shared = hook ? rlev : nullptr;
+  S.r_bound = rlev;
   S.two_bounds = two;
   S.fb_list = fb_list;
   S.hdr = hdr;
   S.out_d = out_d;
   S.out_i = out_i;
-  const size_t ssmem = (size_t)kSelStage * 8 + (size_t)kSurvCap * 8 + (size_t)p.d * 4;
+  const size_t ssmem = (size_t)kSurvCap * 8 +
+                       (size_t)(kSelThreads / 32) * 32 * (kRerankDims + 1) * 4 + (size_t)p.d * 4;
   BFK_TRY(cudaFuncSetAttribute((const void *)tc_final_select_kernel,
                                cudaFuncAttributeMaxDynamicSharedMemorySize, (int)ssmem));
   tc_final_select_kernel<<<(unsigned)p.n, kSelThreads, ssmem, stream>>>(S);
