@@ -353,6 +353,7 @@ __global__ void __maxnreg__(96)
     const float margin = a.qinfo[(size_t)qt * kBM + r].y;
     // theta = B + margin, B = (k-th smallest v of the previous level) + margin, rounded up.
     // Rows past m carry ||x||^2 = +inf, so theta stays finite: FLT_MAX when there is no bound.
+    const bool all_pass = a.r_in == nullptr;  // the first level: no bound yet
     float theta = -INFINITY;
     if (valid)
       theta = a.r_in ? fminf(__fadd_ru(read_bound(a.r_in, a.n, q, a.two_bounds), margin), FLT_MAX)
@@ -424,6 +425,29 @@ __global__ void __maxnreg__(96)
         // v = cscale * acc + ||x||^2 of the group of 8 columns, exactly and after
         // rounding (round-to-nearest is monotonic).  Only groups whose bound is <= theta
         // can hold a candidate; their exact v are computed for the appends.
+        if (all_pass) {
+          // a level without a bound (theta = FLT_MAX) keeps every finite v: no group
+          // bounds or votes, one predicated append per column
+          const float4 *nx4 = reinterpret_cast<const float4 *>(nxt + hh * 32);
+#pragma unroll
+          for (int g = 0; g < 4; g++) {
+            const uint32_t *acc = va + 8 * g;
+            const float4 n0 = nx4[2 * g], n1 = nx4[2 * g + 1];
+            float v[8];
+            fma2(__uint_as_float(acc[0]), __uint_as_float(acc[1]), cscale, n0.x, n0.y, v[0], v[1]);
+            fma2(__uint_as_float(acc[2]), __uint_as_float(acc[3]), cscale, n0.z, n0.w, v[2], v[3]);
+            fma2(__uint_as_float(acc[4]), __uint_as_float(acc[5]), cscale, n1.x, n1.y, v[4], v[5]);
+            fma2(__uint_as_float(acc[6]), __uint_as_float(acc[7]), cscale, n1.z, n1.w, v[6], v[7]);
+            const uint32_t rg = row0 + hh * 32 + 8 * g;
+#pragma unroll
+            for (int i = 0; i < 8; i++) {
+              const bool keep = v[i] <= theta;
+              if (keep) region[min(cnt, last)] = make_uint2(rg + i, __float_as_uint(v[i]));
+              cnt += keep ? 1 : 0;
+            }
+          }
+          continue;
+        }
         const float4 gn = reinterpret_cast<const float4 *>(nxt + kGroupN)[hh];
         float gb[4];
         gb[0] = __fmaf_rn(cscale, max8u(va), gn.x);
