@@ -404,41 +404,28 @@ __global__ void __maxnreg__(96)
       }
       tc_fence_after();
       const uint32_t row0 = (uint32_t)(tile * kBN + cg * kGroupN);
-#pragma unroll 1
-      for (int hh = 0; hh < 2; hh++) {
-        // 32 columns at a time keeps the register footprint small (18 warps share the file)
-        uint32_t va[32];
-        tmem_ld_32x32b_x32(taddr0 + (uint32_t)(b * kBN + hh * 32), va);
-        tmem_ld_wait();
-        if (hh == 1) {
-          // this warp's columns are in registers: release them to the MMA warp
-          tc_fence_before();
-          __syncwarp();
-          if (lane == 0) {
-        if (PAIR) mbar_arrive_cluster(acc_empty + b, 0);
-        else mbar_arrive(acc_empty + b);
-      }
-        } else {
-          __syncwarp();  // the ||x||^2 staging written above is visible to every lane
-        }
-        // Group bound: cscale < 0, so cscale * max(acc) + min ||x||^2 <= every
-        // v = cscale * acc + ||x||^2 of the group of 8 columns, exactly and after
-        // rounding (round-to-nearest is monotonic).  Only groups whose bound is <= theta
-        // can hold a candidate; their exact v are computed for the appends.
-        if (all_pass) {
-          // a level without a bound (theta = FLT_MAX) keeps every finite v: no group
-          // bounds or votes, one predicated append per column
-          const float4 *nx4 = reinterpret_cast<const float4 *>(nxt + hh * 32);
+      // 16 columns at a time; the load of the next 16 is in flight while these are checked
+      uint32_t ra[16], rb[16];
+      tmem_ld_32x32b_x16(taddr0 + (uint32_t)(b * kBN), ra);
+      tmem_ld_wait(ra);
+      __syncwarp();  // the ||x||^2 staging written above is visible to every lane
 #pragma unroll
-          for (int g = 0; g < 4; g++) {
-            const uint32_t *acc = va + 8 * g;
+      for (int qq = 0; qq < 4; qq++) {
+        uint32_t (&cur)[16] = (qq & 1) ? rb : ra;
+        uint32_t (&nxb)[16] = (qq & 1) ? ra : rb;
+        if (qq < 3) tmem_ld_32x32b_x16(taddr0 + (uint32_t)(b * kBN + (qq + 1) * 16), nxb);
+        if (all_pass) {
+          const float4 *nx4 = reinterpret_cast<const float4 *>(nxt + qq * 16);
+#pragma unroll
+          for (int g = 0; g < 2; g++) {
+            const uint32_t *acc = cur + 8 * g;
             const float4 n0 = nx4[2 * g], n1 = nx4[2 * g + 1];
             float v[8];
             fma2(__uint_as_float(acc[0]), __uint_as_float(acc[1]), cscale, n0.x, n0.y, v[0], v[1]);
             fma2(__uint_as_float(acc[2]), __uint_as_float(acc[3]), cscale, n0.z, n0.w, v[2], v[3]);
             fma2(__uint_as_float(acc[4]), __uint_as_float(acc[5]), cscale, n1.x, n1.y, v[4], v[5]);
             fma2(__uint_as_float(acc[6]), __uint_as_float(acc[7]), cscale, n1.z, n1.w, v[6], v[7]);
-            const uint32_t rg = row0 + hh * 32 + 8 * g;
+            const uint32_t rg = row0 + qq * 16 + 8 * g;
 #pragma unroll
             for (int i = 0; i < 8; i++) {
               const bool keep = v[i] <= theta;
@@ -446,41 +433,45 @@ __global__ void __maxnreg__(96)
               cnt += keep ? 1 : 0;
             }
           }
-          continue;
-        }
-        const float4 gn = reinterpret_cast<const float4 *>(nxt + kGroupN)[hh];
-        float gb[4];
-        gb[0] = __fmaf_rn(cscale, max8u(va), gn.x);
-        gb[1] = __fmaf_rn(cscale, max8u(va + 8), gn.y);
-        gb[2] = __fmaf_rn(cscale, max8u(va + 16), gn.z);
-        gb[3] = __fmaf_rn(cscale, max8u(va + 24), gn.w);
-        const float all = fminf(min3f(gb[0], gb[1], gb[2]), gb[3]);
-        if (__any_sync(0xffffffffu, all <= theta)) {
-          const float4 *nx4 = reinterpret_cast<const float4 *>(nxt + hh * 32);
+        } else {
+          const float2 gn = reinterpret_cast<const float2 *>(nxt + kGroupN)[qq];
+          float gb[2];
+          gb[0] = __fmaf_rn(cscale, max8u(cur), gn.x);
+          gb[1] = __fmaf_rn(cscale, max8u(cur + 8), gn.y);
+          if (__any_sync(0xffffffffu, fminf(gb[0], gb[1]) <= theta)) {
+            const float4 *nx4 = reinterpret_cast<const float4 *>(nxt + qq * 16);
 #pragma unroll
-          for (int g = 0; g < 4; g++) {
-            if (__any_sync(0xffffffffu, gb[g] <= theta)) {
-              const uint32_t *acc = va + 8 * g;
-              const float4 n0 = nx4[2 * g], n1 = nx4[2 * g + 1];
-              float v[8];
-              fma2(__uint_as_float(acc[0]), __uint_as_float(acc[1]), cscale, n0.x, n0.y, v[0], v[1]);
-              fma2(__uint_as_float(acc[2]), __uint_as_float(acc[3]), cscale, n0.z, n0.w, v[2], v[3]);
-              fma2(__uint_as_float(acc[4]), __uint_as_float(acc[5]), cscale, n1.x, n1.y, v[4], v[5]);
-              fma2(__uint_as_float(acc[6]), __uint_as_float(acc[7]), cscale, n1.z, n1.w, v[6], v[7]);
-              // this lane's kept columns as a bit mask; one append per set bit (usually
-              // none or one), the value picked from registers by a select chain
-              unsigned keep = 0;
+            for (int g = 0; g < 2; g++) {
+              if (__any_sync(0xffffffffu, gb[g] <= theta)) {
+                const uint32_t *acc = cur + 8 * g;
+                const float4 n0 = nx4[2 * g], n1 = nx4[2 * g + 1];
+                float v[8];
+                fma2(__uint_as_float(acc[0]), __uint_as_float(acc[1]), cscale, n0.x, n0.y, v[0], v[1]);
+                fma2(__uint_as_float(acc[2]), __uint_as_float(acc[3]), cscale, n0.z, n0.w, v[2], v[3]);
+                fma2(__uint_as_float(acc[4]), __uint_as_float(acc[5]), cscale, n1.x, n1.y, v[4], v[5]);
+                fma2(__uint_as_float(acc[6]), __uint_as_float(acc[7]), cscale, n1.z, n1.w, v[6], v[7]);
+                unsigned keep = 0;
 #pragma unroll
-              for (int i = 0; i < 8; i++) keep |= (v[i] <= theta ? 1u : 0u) << i;
-              const uint32_t rg = row0 + hh * 32 + 8 * g;
-              while (keep) {
-                const int i = __ffs(keep) - 1;
-                keep &= keep - 1;
-                // a full region keeps overwriting its last slot (the count tells)
-                region[min(cnt, last)] = make_uint2(rg + i, __float_as_uint(pick8(v, i)));
-                cnt++;
+                for (int i = 0; i < 8; i++) keep |= (v[i] <= theta ? 1u : 0u) << i;
+                const uint32_t rg = row0 + qq * 16 + 8 * g;
+                while (keep) {
+                  const int i = __ffs(keep) - 1;
+                  keep &= keep - 1;
+                  region[min(cnt, last)] = make_uint2(rg + i, __float_as_uint(pick8(v, i)));
+                  cnt++;
+                }
               }
             }
+          }
+        }
+        if (qq < 3) tmem_ld_wait(nxb);
+        if (qq == 2) {
+          // every column of this warp is in registers: release them to the MMA warp
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) {
+            if (PAIR) mbar_arrive_cluster(acc_empty + b, 0);
+            else mbar_arrive(acc_empty + b);
           }
         }
       }
