@@ -36,6 +36,10 @@ from gpu_algo_b200.sharded import shard_range  # noqa: E402
 
 FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0}
 DEFAULT_WORKLOAD = "unit-10m"
+# published queries/sec for a workload's exact shape (other hardware): the reference's best
+# run at 1M rows, d=8, k=1, 128k queries, on an RTX 5090 (the q16 query-group variant,
+# bf/5090_results/bf_fp32_variant_repeat_over_n_d8_k1_full.json:1772)
+PUBLISHED_QPS = {("published-d8", 1_000_000, 128_000, 8, 1): 607_025.0}
 # DRAM bytes read per database row by one main-filter launch, keyed by (workload, queries,
 # d, k): ncu dram__bytes_read.sum of the launch over all rows of a 3,000,000-row sample
 # (1.242 GB / 3M rows), single-CTA kernel.  Its writes are the candidate appends, 8 bytes
@@ -329,7 +333,8 @@ def main(argv=None) -> int:
             "ms_per_step": t_max,
             "higher_is_better": True,
             "scaling": "strong",
-            "vs_baseline": None,
+            "vs_baseline": (value / PUBLISHED_QPS[(a.workload, N, Qn, d, k)]
+                            if (a.workload, N, Qn, d, k) in PUBLISHED_QPS else None),
             "dtype": "f32",
             "data": "synthetic",
             "config": {"workload": a.workload, "N": N, "Q": Qn, "d": d, "k": k,

@@ -56,6 +56,7 @@ constexpr int kSurvCap = 2048;      // exact re-rank capacity per query
 constexpr int kRankSortMax = 512;   // survivors ordered by rank counting up to this many
 constexpr int kDefaultPool = 16384;  // candidate entries per query (all regions of a level)
 constexpr int kLevelTarget = 3072;   // expected candidates per query of a filter level
+constexpr int kMinLevelTarget = 256;
 
 struct FilterArgs {
   const float *xnorm;    // (x_tiles*256) ||x||^2, +inf past m
@@ -1171,7 +1172,9 @@ bool tc_make_plan(int64_t n, int64_t m, int d, int k, int slices, int pool, bool
   if (P.cand_cap < 2 * k) P.cand_cap = 2 * k;
 
   // level sizes: each level's expected candidates ~ target (the pool holds 5x that)
-  int64_t target = kLevelTarget;
+  // a level's expected candidates: 32 k, between kMinLevelTarget and kLevelTarget (each
+  // level keeps about target rows per query; the next level is target / k times larger)
+  int64_t target = std::min<int64_t>(kLevelTarget, std::max<int64_t>(kMinLevelTarget, 32 * (int64_t)k));
   if (target < 4 * (int64_t)k) target = 4 * (int64_t)k;
   if (target > P.cand_cap / 4) target = P.cand_cap / 4;
   int64_t ratio = target / k;

@@ -107,6 +107,9 @@ WORKLOADS = {
     "unit-10m": dict(kind="unit", db_seed=4, q_seed=5, N=10_000_000, Q=10_000, d=128, ks=(100,)),
     "highdim-960": dict(kind="normal", db_seed=6, q_seed=7, N=2_000_000, Q=1_000, d=960, ks=(100,)),
     "stream-100m": dict(kind="normal", db_seed=8, q_seed=9, N=100_000_000, Q=128, d=96, ks=(10,)),
+    # the shape of the reference's only published results (1M rows, d=8, k=1, up to 128k
+    # queries, Gaussian data); the seeds are this package's own
+    "published-d8": dict(kind="normal", db_seed=10, q_seed=11, N=1_000_000, Q=128_000, d=8, ks=(1,)),
 }
 
 

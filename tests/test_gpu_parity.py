@@ -102,7 +102,8 @@ def test_tc_nonfinite_rows_use_exact_engine():
                                         ("mixture-k-sweep", 257, 120_000, 100),
                                         ("unit-10m", 256, 300_000, 100),
                                         ("stream-100m", 130, 250_000, 10),
-                                        ("mixture-k-sweep", 200, 100_000, 1)])
+                                        ("mixture-k-sweep", 200, 100_000, 1),
+                                        ("published-d8", 300, 1_000_000, 1)])
 def test_tc_workload_samples(name, n, m, k):
     from gpu_algo_b200 import data
     X, Q = data.workload_arrays(name, n_rows=m, n_queries=n)
