@@ -704,6 +704,7 @@ struct QueryRegions {
   int nreg;            // regions of the level
   int total;
   bool over;
+  int stage_cap;       // candidates the caller's shared memory can stage
 };
 
 __device__ QueryRegions load_regions(const uint2 *cand, const int *ccount, int64_t q, int pool,
@@ -746,10 +747,15 @@ __device__ QueryRegions load_regions(const uint2 *cand, const int *ccount, int64
   R.nreg = nreg;
   R.total = s_misc[0];
   R.over = s_misc[1] != 0;
+  R.stage_cap = 0;
   return R;
 }
 
-constexpr int kSelStage = 6144;  // candidates staged in shared memory (more: read in place)
+// candidates a level select stages in shared memory (more: read in place): a search
+// alone, or shards that share bounds (each then holds a fraction of the candidates and
+// smaller staging admits twice the blocks per SM)
+constexpr int kSelStage = 6144;
+constexpr int kSelStageShared = 2048;
 constexpr int kSelBins = 1024;
 
 // Copy the candidates into shared memory and return the block-wide min and max
@@ -759,7 +765,7 @@ constexpr int kSelBins = 1024;
 __device__ void stage_candidates(const QueryRegions &R, const int *s_cnt, const int *s_off,
                                  uint2 *cs, float *s_red, float *vmin, float *vmax) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nw = blockDim.x >> 5;
-  const bool stage = R.total <= kSelStage;
+  const bool stage = R.total <= R.stage_cap;
   float lo = INFINITY, hi = -INFINITY;
   for (int e0 = threadIdx.x; e0 < R.total; e0 += 4 * blockDim.x) {
     uint2 ent[4];
@@ -806,7 +812,7 @@ __device__ void stage_candidates(const QueryRegions &R, const int *s_cnt, const 
 template <class F>
 __device__ __forceinline__ void for_each_candidate(const QueryRegions &R, const int *s_cnt,
                                                    const uint2 *cs, F f) {
-  if (R.total <= kSelStage) {
+  if (R.total <= R.stage_cap) {
     for (int e = threadIdx.x; e < R.total; e += blockDim.x) f(cs[e]);
   } else {
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nw = blockDim.x >> 5;
@@ -895,6 +901,7 @@ struct LevelSelArgs {
   int k, pool, region;
   int nreg, stride;  // regions of the level and the count-array stride
   int k2;            // shards > 1: ceil(k / shards), else 0
+  int stage_cap;     // candidates staged in shared memory (dynamic smem stage_cap * 8)
   float *r_out;      // (n) bound B = R + margin for the next level, +inf when fewer than k;
                      // k2 > 0: then (n) -(R2 + margin), R2 >= the k2-th smallest v
 };
@@ -906,8 +913,9 @@ __global__ void __launch_bounds__(kSelThreads) tc_level_select_kernel(const Leve
   __shared__ int hist[kSelBins], s_cnt[256], s_off[256], s_misc[2], s_bin[2];
   __shared__ float s_red[128];
   const int64_t q = blockIdx.x;
-  const QueryRegions R = load_regions(a.cand, a.ccount, q, a.pool, a.region, a.nreg, a.stride,
-                                      s_cnt, s_off, s_misc);
+  QueryRegions R = load_regions(a.cand, a.ccount, q, a.pool, a.region, a.nreg, a.stride, s_cnt,
+                                s_off, s_misc);
+  R.stage_cap = a.stage_cap;
   // entries lost to a full region only make R larger than it could be: still a
   // valid bound, since R is taken over real rows that were kept
   const int k2 = a.k2 > 0 ? a.k2 : a.k;
@@ -1327,7 +1335,8 @@ int tc_run(const float *Q, const float *X, int64_t id_offset, float *out_d, int3
   const void *filter = p.pair ? (const void *)knn_tc_filter_kernel<true>
                               : (const void *)knn_tc_filter_kernel<false>;
   BFK_TRY(cudaFuncSetAttribute(filter, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
-  const size_t lsmem = (size_t)kSelStage * 8;
+  const int stage_cap = (hook != nullptr && shards > 1) ? kSelStageShared : kSelStage;
+  const size_t lsmem = (size_t)stage_cap * 8;
   BFK_TRY(cudaFuncSetAttribute((const void *)tc_level_select_kernel,
                                cudaFuncAttributeMaxDynamicSharedMemorySize, (int)lsmem));
   FilterArgs A{};
@@ -1391,6 +1400,7 @@ int tc_run(const float *Q, const float *X, int64_t id_offset, float *out_d, int3
       S.stride = kColGroups * p.max_slices;
       S.r_out = rlev;
       S.k2 = two ? (p.k + shards - 1) / shards : 0;
+      S.stage_cap = stage_cap;
       tc_level_select_kernel<<<(unsigned)p.n, kSelThreads, lsmem, stream>>>(S);
       nl++;
       BFK_TRY(cudaGetLastError());
