@@ -751,11 +751,7 @@ __device__ QueryRegions load_regions(const uint2 *cand, const int *ccount, int64
   return R;
 }
 
-// candidates a level select stages in shared memory (more: read in place): a search
-// alone, or shards that share bounds (each then holds a fraction of the candidates and
-// smaller staging admits twice the blocks per SM)
-constexpr int kSelStage = 6144;
-constexpr int kSelStageShared = 2048;
+constexpr int kSelStage = 6144;  // candidates staged in shared memory (more: read in place)
 constexpr int kSelBins = 1024;
 
 // Copy the candidates into shared memory and return the block-wide min and max
@@ -937,6 +933,135 @@ __global__ void __launch_bounds__(kSelThreads) tc_level_select_kernel(const Leve
   }
 }
 
+// The kk-th smallest (1-based, kk <= count) of `count` ordered keys in shared
+// memory, by one warp: four passes of an 8-bit radix select, most significant digit
+// first; `hist` is the warp's own 256 counters.
+__device__ uint32_t warp_select_key(const uint32_t *keys, int count, int kk, int *hist) {
+  const int lane = threadIdx.x & 31;
+  uint32_t prefix = 0, mask = 0;
+  for (int shift = 24; shift >= 0; shift -= 8) {
+    for (int b = lane; b < 256; b += 32) hist[b] = 0;
+    __syncwarp();
+    for (int e = lane; e < count; e += 32) {
+      const uint32_t key = keys[e];
+      if ((key & mask) == prefix) atomicAdd(&hist[(key >> shift) & 255u], 1);
+    }
+    __syncwarp();
+    // the digit whose running count reaches kk (8 bins per lane)
+    int sum = 0;
+#pragma unroll
+    for (int j = 0; j < 8; j++) sum += hist[lane * 8 + j];
+    int incl = sum;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int t = __shfl_up_sync(0xffffffffu, incl, o);
+      if (lane >= o) incl += t;
+    }
+    const int excl = incl - sum;
+    const unsigned hit = __ballot_sync(0xffffffffu, excl < kk && incl >= kk);
+    const int src = __ffs(hit) - 1;
+    int dgt = 0, run = 0;
+    if (lane == src) {
+      run = excl;
+      dgt = lane * 8;
+      for (;; dgt++) {
+        if (run + hist[dgt] >= kk) break;
+        run += hist[dgt];
+      }
+    }
+    dgt = __shfl_sync(0xffffffffu, dgt, src);
+    run = __shfl_sync(0xffffffffu, run, src);
+    prefix |= (uint32_t)dgt << shift;
+    kk -= run;
+    mask |= 255u << shift;
+    __syncwarp();
+  }
+  return prefix;
+}
+
+constexpr int kWarpSelCap = 1024;   // candidates a warp-level select stages per query
+constexpr int kWarpSelQueries = 8;  // queries (warps) per block
+
+// Level select of shards that share bounds, one warp per query: each shard holds a
+// small share of a query's candidates, so a warp stages up to kWarpSelCap of them
+// (as ordered keys of v) and selects the exact k-th and k2-th smallest.  A query with
+// more candidates uses the first kWarpSelCap: the k-th smallest of any k real rows
+// is still a bound.  dynamic smem: 8 * (kWarpSelCap + 256 + 256) * 4
+__global__ void __launch_bounds__(kSelThreads) tc_level_select_warp_kernel(const LevelSelArgs a) {
+  extern __shared__ __align__(1024) unsigned char smem_raw[];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  uint32_t *keys = reinterpret_cast<uint32_t *>(smem_raw) + warp * kWarpSelCap;
+  int *hist = reinterpret_cast<int *>(smem_raw) + kWarpSelQueries * kWarpSelCap + warp * 256;
+  int *off = reinterpret_cast<int *>(smem_raw) + kWarpSelQueries * (kWarpSelCap + 256) + warp * 256;
+  const int64_t q = (int64_t)blockIdx.x * kWarpSelQueries + warp;
+  if (q >= a.n) return;
+  // regions' kept counts (clamped to the region size) and their prefix offsets
+  int loc[8], sum = 0;
+#pragma unroll
+  for (int j = 0; j < 8; j++) {
+    const int i = lane * 8 + j;
+    int c = i < a.nreg ? a.ccount[(size_t)q * a.stride + i] : 0;
+    c = min(c, a.region);
+    loc[j] = c;
+    sum += c;
+  }
+  int incl = sum;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const int t = __shfl_up_sync(0xffffffffu, incl, o);
+    if (lane >= o) incl += t;
+  }
+  int run = incl - sum;
+#pragma unroll
+  for (int j = 0; j < 8; j++) {
+    const int i = lane * 8 + j;
+    if (i < a.nreg) off[i] = run;
+    run += loc[j];
+  }
+  const int total = __shfl_sync(0xffffffffu, incl, 31);
+  const int staged = min(total, kWarpSelCap);
+  __syncwarp();
+  const uint2 *base = a.cand + (size_t)q * a.pool;
+  for (int e0 = lane; e0 < staged; e0 += 4 * 32) {
+    uint2 ent[4];
+#pragma unroll
+    for (int u = 0; u < 4; u++) {
+      const int e = e0 + u * 32;
+      ent[u] = make_uint2(0u, 0x7fc00000u);
+      if (e < staged) {
+        int lo = 0, hi = a.nreg - 1;
+        while (lo < hi) {
+          const int mid = (lo + hi + 1) >> 1;
+          if (off[mid] <= e) lo = mid; else hi = mid - 1;
+        }
+        ent[u] = base[(size_t)lo * a.region + (e - off[lo])];
+      }
+    }
+#pragma unroll
+    for (int u = 0; u < 4; u++) {
+      const int e = e0 + u * 32;
+      const float v = __uint_as_float(ent[u].y);
+      if (e < staged) keys[e] = v == v ? f2ord(v) : 0xffffffffu;
+    }
+  }
+  __syncwarp();
+  // R (R2): the k-th (k2-th) smallest v of real candidates; +inf when there are fewer
+  float r1 = INFINITY, r2 = INFINITY;
+  if (staged >= a.k) {
+    const uint32_t key = warp_select_key(keys, staged, a.k, hist);
+    if (key != 0xffffffffu) r1 = ord2f(key);
+  }
+  if (a.k2 > 0 && staged >= a.k2) {
+    const uint32_t key = warp_select_key(keys, staged, a.k2, hist);
+    if (key != 0xffffffffu) r2 = ord2f(key);
+  }
+  if (lane == 0) {
+    const float m = a.qinfo[q].y;
+    a.r_out[q] = __fadd_ru(r1, m);
+    if (a.k2 > 0) a.r_out[a.n + q] = -__fadd_ru(r2, m);
+  }
+}
+
 struct SelArgs {
   const float *Q;
   const float *X;
@@ -1096,6 +1221,146 @@ __global__ void __launch_bounds__(kSelThreads) tc_final_select_kernel(const SelA
     atomicAdd(&a.hdr->survivors, (unsigned long long)ns);
     atomicAdd(&a.hdr->candidates, (unsigned long long)R.total);
     atomicMax(&a.hdr->max_cand, R.total);
+  }
+}
+
+constexpr int kWarpFinalQueries = 4;   // queries (warps) per block of the warp-level final select
+constexpr int kWarpSurvCap = 512;      // survivors a warp re-ranks; more: the SIMT engine
+
+// Final select of shards that share bounds, one warp per query: a shard holds few of
+// a query's candidates and fewer survivors, so the block-wide phases of
+// tc_final_select_kernel would be mostly waiting.  Same steps, per warp: survivors
+// below the shared bound, exact re-rank in dimension order, rank-count ordering.
+// dynamic smem: 4 * warp_final_smem(d)
+__host__ __device__ inline size_t warp_final_smem(int d) {
+  // keys, row chunk, region offsets, query; a multiple of 16 bytes keeps every warp's
+  // 64-bit keys aligned
+  const size_t b = (size_t)kWarpSurvCap * 8 + 32 * (kRerankDims + 1) * 4 + 256 * 4 + (size_t)d * 4;
+  return (b + 15) & ~(size_t)15;
+}
+__global__ void __launch_bounds__(kWarpFinalQueries * 32) tc_final_select_warp_kernel(const SelArgs a) {
+  extern __shared__ __align__(1024) unsigned char smem_raw[];
+  constexpr int W = kRerankDims, P = kRerankDims + 1;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const size_t per_warp = warp_final_smem(a.d);
+  unsigned char *mine = smem_raw + warp * per_warp;
+  uint64_t *keys = reinterpret_cast<uint64_t *>(mine);
+  float *tile = reinterpret_cast<float *>(keys + kWarpSurvCap);
+  int *off = reinterpret_cast<int *>(tile + 32 * P);
+  float *qs = reinterpret_cast<float *>(off + 256);
+  const int64_t q = (int64_t)blockIdx.x * kWarpFinalQueries + warp;
+  if (q >= a.n) return;
+  int loc[8], sum = 0, over = 0;
+#pragma unroll
+  for (int j = 0; j < 8; j++) {
+    const int i = lane * 8 + j;
+    int c = i < a.nreg ? a.ccount[(size_t)q * a.stride + i] : 0;
+    if (c > a.region) { over = 1; c = a.region; }
+    loc[j] = c;
+    sum += c;
+  }
+  int incl = sum;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const int t = __shfl_up_sync(0xffffffffu, incl, o);
+    if (lane >= o) incl += t;
+  }
+  int run = incl - sum;
+#pragma unroll
+  for (int j = 0; j < 8; j++) {
+    const int i = lane * 8 + j;
+    if (i < a.nreg) off[i] = run;
+    run += loc[j];
+  }
+  const int total = __shfl_sync(0xffffffffu, incl, 31);
+  // a region that lost entries, or non-finite inputs (the margin needs finite norms)
+  if (__any_sync(0xffffffffu, over) || a.hdr->nonfinite) {
+    if (lane == 0) {
+      const int slot = atomicAdd(&a.hdr->fallback, 1);
+      a.fb_list[slot] = (int)q;
+    }
+    return;
+  }
+  for (int c = lane; c < a.d; c += 32) qs[c] = a.Q[q * a.d + c];
+  const float theta = __fadd_ru(read_bound(a.r_bound, a.n, q, a.two_bounds), a.qinfo[q].y);
+  __syncwarp();
+  // survivors, appended in warp order with a ballot per round of 32 entries
+  const uint2 *base = a.cand + (size_t)q * a.pool;
+  int ns = 0;
+  for (int e = lane; e - lane < total; e += 32) {
+    bool keep = false;
+    uint32_t row = 0;
+    if (e < total) {
+      int lo = 0, hi = a.nreg - 1;
+      while (lo < hi) {
+        const int mid = (lo + hi + 1) >> 1;
+        if (off[mid] <= e) lo = mid; else hi = mid - 1;
+      }
+      const uint2 ent = base[(size_t)lo * a.region + (e - off[lo])];
+      keep = __uint_as_float(ent.y) <= theta;
+      row = ent.x;
+    }
+    const unsigned m = __ballot_sync(0xffffffffu, keep);
+    const int slot = ns + __popc(m & ((1u << lane) - 1u));
+    if (keep && slot < kWarpSurvCap) keys[slot] = row;
+    ns += __popc(m);
+  }
+  if (ns > kWarpSurvCap) {
+    if (lane == 0) {
+      const int slot = atomicAdd(&a.hdr->fallback, 1);
+      a.fb_list[slot] = (int)q;
+    }
+    return;
+  }
+  __syncwarp();
+  // exact distances: 32 survivors at a time, rows staged in chunks of W dimensions
+  for (int b0 = 0; b0 < ns; b0 += 32) {
+    const int nb = min(32, ns - b0);
+    const uint32_t myrow = lane < nb ? (uint32_t)keys[b0 + lane] : 0u;
+    float acc = 0.f;
+    const int c = lane % W, j0 = lane / W;
+    for (int c0 = 0; c0 < a.d; c0 += W) {
+      const int cw = min(W, a.d - c0);
+      float t[32 / (32 / W)];
+#pragma unroll
+      for (int u = 0; u < 32 / (32 / W); u++) {
+        const int j = j0 + u * (32 / W);
+        const uint32_t rj = __shfl_sync(0xffffffffu, myrow, j);
+        t[u] = (j < nb && c < cw) ? __ldg(a.X + (size_t)rj * a.d + c0 + c) : 0.f;
+      }
+      __syncwarp();
+#pragma unroll
+      for (int u = 0; u < 32 / (32 / W); u++) tile[(j0 + u * (32 / W)) * P + c] = t[u];
+      __syncwarp();
+      if (lane < nb)
+        for (int cc = 0; cc < cw; cc++) acc = dist_step(qs[c0 + cc], tile[lane * P + cc], acc);
+    }
+    __syncwarp();
+    if (lane < nb) keys[b0 + lane] = acc == acc ? pair_key(acc, (int32_t)(a.id_offset + myrow)) : ~0ull;
+  }
+  __syncwarp();
+  // order by rank counting; equal keys (non-finite distances) order by slot
+  for (int e = lane; e < ns; e += 32) {
+    const uint64_t key = keys[e];
+    int rank = 0;
+    for (int j = 0; j < ns; j++) {
+      const uint64_t kj = keys[j];
+      rank += (kj < key || (kj == key && j < e)) ? 1 : 0;
+    }
+    if (rank < a.k) {
+      const bool pad = key == ~0ull;
+      a.out_d[q * a.k + rank] = pad ? BFK_PAD_DIST : ord2f((uint32_t)(key >> 32));
+      a.out_i[q * a.k + rank] = pad ? -1 : (int32_t)(uint32_t)(key & 0xffffffffu);
+    }
+  }
+  for (int j = ns + lane; j < a.k; j += 32) {
+    a.out_d[q * a.k + j] = BFK_PAD_DIST;
+    a.out_i[q * a.k + j] = -1;
+  }
+  if (lane == 0) {
+    atomicAdd(&a.hdr->survivors, (unsigned long long)ns);
+    atomicAdd(&a.hdr->candidates, (unsigned long long)total);
+    atomicMax(&a.hdr->max_cand, total);
   }
 }
 
@@ -1335,10 +1600,13 @@ int tc_run(const float *Q, const float *X, int64_t id_offset, float *out_d, int3
   const void *filter = p.pair ? (const void *)knn_tc_filter_kernel<true>
                               : (const void *)knn_tc_filter_kernel<false>;
   BFK_TRY(cudaFuncSetAttribute(filter, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
-  const int stage_cap = (hook != nullptr && shards > 1) ? kSelStageShared : kSelStage;
+  const int stage_cap = kSelStage;
   const size_t lsmem = (size_t)stage_cap * 8;
   BFK_TRY(cudaFuncSetAttribute((const void *)tc_level_select_kernel,
                                cudaFuncAttributeMaxDynamicSharedMemorySize, (int)lsmem));
+  const size_t wsmem = (size_t)kWarpSelQueries * (kWarpSelCap + 512) * 4;
+  BFK_TRY(cudaFuncSetAttribute((const void *)tc_level_select_warp_kernel,
+                               cudaFuncAttributeMaxDynamicSharedMemorySize, (int)wsmem));
   FilterArgs A{};
   A.xnorm = xnorm;
   A.xinv = xinv;
@@ -1401,7 +1669,11 @@ int tc_run(const float *Q, const float *X, int64_t id_offset, float *out_d, int3
       S.r_out = rlev;
       S.k2 = two ? (p.k + shards - 1) / shards : 0;
       S.stage_cap = stage_cap;
-      tc_level_select_kernel<<<(unsigned)p.n, kSelThreads, lsmem, stream>>>(S);
+      if (two)
+        tc_level_select_warp_kernel<<<(unsigned)((p.n + kWarpSelQueries - 1) / kWarpSelQueries),
+                                      kSelThreads, wsmem, stream>>>(S);
+      else
+        tc_level_select_kernel<<<(unsigned)p.n, kSelThreads, lsmem, stream>>>(S);
       nl++;
       BFK_TRY(cudaGetLastError());
       // a sharded search replaces each query's bound by the minimum over all shards
@@ -1436,7 +1708,15 @@ int tc_run(const float *Q, const float *X, int64_t id_offset, float *out_d, int3
                        (size_t)(kSelThreads / 32) * 32 * (kRerankDims + 1) * 4 + (size_t)p.d * 4;
   BFK_TRY(cudaFuncSetAttribute((const void *)tc_final_select_kernel,
                                cudaFuncAttributeMaxDynamicSharedMemorySize, (int)ssmem));
-  tc_final_select_kernel<<<(unsigned)p.n, kSelThreads, ssmem, stream>>>(S);
+  if (two) {
+    const size_t wfsmem = (size_t)kWarpFinalQueries * warp_final_smem(p.d);
+    BFK_TRY(cudaFuncSetAttribute((const void *)tc_final_select_warp_kernel,
+                                 cudaFuncAttributeMaxDynamicSharedMemorySize, (int)wfsmem));
+    tc_final_select_warp_kernel<<<(unsigned)((p.n + kWarpFinalQueries - 1) / kWarpFinalQueries),
+                                  kWarpFinalQueries * 32, wfsmem, stream>>>(S);
+  } else {
+    tc_final_select_kernel<<<(unsigned)p.n, kSelThreads, ssmem, stream>>>(S);
+  }
   nl++;
   BFK_TRY(cudaGetLastError());
 
