@@ -61,6 +61,9 @@ def parse_args(argv=None):
     ap.add_argument("--engine", default="auto", choices=["auto", "direct", "tc_f16"])
     ap.add_argument("--cta-pair", action="store_true",
                     help="TC engine: CTA pairs (tcgen05.mma.cta_group::2)")
+    ap.add_argument("--prepared", action="store_true",
+                    help="index use: the rows' TC form is prepared once, outside the timed "
+                         "steps (bfk_prepare); the default step converts them every time")
     ap.add_argument("--cpu-sample", type=int, default=32,
                     help="queries in the bounded CPU-baseline sample")
     ap.add_argument("--no-cpu-baseline", action="store_true")
@@ -214,9 +217,12 @@ def main(argv=None) -> int:
     # every rank plans its sampling levels for the largest shard
     plan_rows = shard_range(N, 0, world)[1] - shard_range(N, 0, world)[0]
 
+    prepared = engine.PreparedRows.prepare(Xd) if a.prepared else None
+
     def step(time_main=False, Q_=None):
         return sharded_search(Qd if Q_ is None else Q_, Xd, k, r0, plan_rows=plan_rows,
-                              engine=a.engine, time_main=time_main, cta_pair=a.cta_pair)
+                              engine=a.engine, time_main=time_main, cta_pair=a.cta_pair,
+                              prepared=prepared)
 
     def barrier():
         if world > 1:
@@ -227,7 +233,7 @@ def main(argv=None) -> int:
     torch.cuda.synchronize()
     # the stats calls pass the search's own plan options (same workspace size)
     stat_opts = dict(engine=a.engine, plan_rows=plan_rows if world > 1 else 0,
-                     shards=world if world > 1 else 0)
+                     shards=world if world > 1 else 0, prepared=a.prepared)
     engine.last_stats(Qd, Xd, k, **stat_opts)  # clear timing records
     barrier()
     torch.cuda.synchronize()
@@ -339,6 +345,7 @@ def main(argv=None) -> int:
             "data": "synthetic",
             "config": {"workload": a.workload, "N": N, "Q": Qn, "d": d, "k": k,
                        "engine": stats["engine"], "parallelism": f"rowshard{world}",
+                       "rows_prepared_once": bool(a.prepared),
                        "l2": "inputs larger than L2 (database "
                              f"{N * d * 4 / 1e9:.2f} GB), no flush"},
             "roofline": roofline,

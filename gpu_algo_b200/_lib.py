@@ -39,6 +39,9 @@ EXPORTS = (
     "bfk_kernel_attrs",
     "bfk_search_stats",
     "bfk_search_noalloc",
+    "bfk_prepared_size",
+    "bfk_prepare",
+    "bfk_search_prepared",
 )
 
 
@@ -115,6 +118,13 @@ def load() -> ctypes.CDLL:
         lib.bfk_merge.argtypes = [vp, vp, i64, i32, i32, vp, vp, vp]
         lib.bfk_kernel_attrs.restype = i32
         lib.bfk_kernel_attrs.argtypes = [i32, i32, i32, ctypes.POINTER(Attrs)]
+        lib.bfk_prepared_size.restype = i32
+        lib.bfk_prepared_size.argtypes = [i64, i32, ctypes.POINTER(u64)]
+        lib.bfk_prepare.restype = i32
+        lib.bfk_prepare.argtypes = [vp, i64, i32, vp, u64, vp]
+        lib.bfk_search_prepared.restype = i32
+        lib.bfk_search_prepared.argtypes = [vp, i64, vp, vp, i64, i32, i32, i64, vp, vp, vp, u64,
+                                            ctypes.POINTER(Opts), vp]
         lib.bfk_search_noalloc.restype = i32
         lib.bfk_search_noalloc.argtypes = [vp, i64, vp, i64, i32, i32, i64, vp, vp, vp]
         lib.bfk_search_stats.restype = i32
@@ -138,6 +148,7 @@ def check(status: int, what: str) -> None:
 
 FLAG_TIME_MAIN = 1
 FLAG_CTA_PAIR = 2
+FLAG_PREPARED = 4
 
 
 def make_opts(engine: str | int = "auto", slices: int = 0, max_candidates: int = 0,

@@ -59,13 +59,20 @@ DirectPlan direct_plan(int64_t n, int64_t m, int d, int k, int slices_req) {
   return p;
 }
 
+// the TC engine's plan under these options (BFK_FLAG_PREPARED: rows from a prepared buffer)
+bool make_plan(int64_t n, int64_t m, int32_t d, int32_t k, const bfk_opts_t *opts, TcPlan *p) {
+  return tc_make_plan(n, m, d, k, opts ? opts->slices : 0, opts ? opts->max_candidates : 0,
+                      opts && (opts->flags & BFK_FLAG_CTA_PAIR), opts ? opts->plan_rows : 0,
+                      opts && (opts->flags & BFK_FLAG_PREPARED), p);
+}
+
 bool opts_ok(const bfk_opts_t *o) {
   if (!o) return true;
   for (int i = 0; i < 3; i++)
     if (o->reserved[i] != 0) return false;
   return o->engine >= BFK_ENGINE_AUTO && o->engine <= BFK_ENGINE_TC_F16 && o->slices >= 0 &&
          o->max_candidates >= 0 && o->plan_rows >= 0 && o->shards >= 0 &&
-         (o->flags & ~(BFK_FLAG_TIME_MAIN | BFK_FLAG_CTA_PAIR)) == 0;
+         (o->flags & ~(BFK_FLAG_TIME_MAIN | BFK_FLAG_CTA_PAIR | BFK_FLAG_PREPARED)) == 0;
 }
 
 int choose_engine(int64_t n, int64_t m, int d, int k, const bfk_opts_t *o) {
@@ -171,8 +178,7 @@ bfk_status_t bfk_workspace_size(int64_t n, int64_t m, int32_t d, int32_t k,
   if (eng == BFK_ENGINE_TC_F16) {
     if (!tc_supported(d, k)) return BFK_ERR_UNSUPPORTED;
     TcPlan p;
-    if (!tc_make_plan(n, m, d, k, opts ? opts->slices : 0, opts ? opts->max_candidates : 0, opts && (opts->flags & BFK_FLAG_CTA_PAIR),
-                      opts ? opts->plan_rows : 0, &p))
+    if (!make_plan(n, m, d, k, opts, &p))
       return BFK_ERR_UNSUPPORTED;
     *bytes = p.total;
   } else {
@@ -181,11 +187,14 @@ bfk_status_t bfk_workspace_size(int64_t n, int64_t m, int32_t d, int32_t k,
   return BFK_OK;
 }
 
-bfk_status_t bfk_search(const float *Q, int64_t n, const float *X, int64_t m, int32_t d,
-                        int32_t k, int64_t id_offset, float *out_dists, int32_t *out_ids,
-                        void *workspace, uint64_t workspace_bytes, const bfk_opts_t *opts,
-                        void *stream_) {
+static bfk_status_t search_impl(const float *Q, int64_t n, const float *X, const void *prepared,
+                                int64_t m, int32_t d, int32_t k, int64_t id_offset,
+                                float *out_dists, int32_t *out_ids, void *workspace,
+                                uint64_t workspace_bytes, const bfk_opts_t *opts, void *stream_) {
   if (!opts_ok(opts)) return BFK_ERR_INVALID_ARGUMENT;
+  // a prepared buffer comes with BFK_FLAG_PREPARED (which sizes the workspace without rows)
+  if ((prepared != nullptr) != (opts && (opts->flags & BFK_FLAG_PREPARED)))
+    return BFK_ERR_INVALID_ARGUMENT;
   bfk_status_t s = validate(n, m, d, k, id_offset);
   if (s != BFK_OK) return s;
   if (n == 0) return BFK_OK;
@@ -205,13 +214,17 @@ bfk_status_t bfk_search(const float *Q, int64_t n, const float *X, int64_t m, in
   if (eng == BFK_ENGINE_TC_F16) {
     if (!tc_supported(d, k)) return BFK_ERR_UNSUPPORTED;
     TcPlan p;
-    if (!tc_make_plan(n, m, d, k, opts ? opts->slices : 0, opts ? opts->max_candidates : 0, opts && (opts->flags & BFK_FLAG_CTA_PAIR),
-                      opts ? opts->plan_rows : 0, &p))
+    if (!make_plan(n, m, d, k, opts, &p))
       return BFK_ERR_UNSUPPORTED;
     if (workspace_bytes < p.total) return BFK_ERR_WORKSPACE;
+    if (prepared) {
+      const int pc = tc_check_prepared(prepared, m, d);
+      if (pc == 1) return BFK_ERR_CUDA;
+      if (pc == 3) return BFK_ERR_INVALID_ARGUMENT;  // made for other rows
+    }
     int rc = tc_run(Q, X, id_offset, out_dists, out_ids, ws, p, stream, t0, t1, &g_calls.launches,
                     opts ? opts->level_hook : nullptr, opts ? opts->hook_user : nullptr,
-                    opts ? opts->shards : 0);
+                    opts ? opts->shards : 0, prepared);
     if (rc == 1) return BFK_ERR_CUDA;
     if (rc == 2) return BFK_ERR_DEVICE_TIMEOUT;
     return BFK_OK;
@@ -242,6 +255,43 @@ bfk_status_t bfk_search(const float *Q, int64_t n, const float *X, int64_t m, in
   if (e != cudaSuccess) return cuda_status(e);
   g_calls.launches = 2;
   return cuda_status(launch_merge(pd, pi, n, p.slices, k, out_dists, out_ids, stream));
+}
+
+bfk_status_t bfk_search(const float *Q, int64_t n, const float *X, int64_t m, int32_t d,
+                        int32_t k, int64_t id_offset, float *out_dists, int32_t *out_ids,
+                        void *workspace, uint64_t workspace_bytes, const bfk_opts_t *opts,
+                        void *stream) {
+  return search_impl(Q, n, X, nullptr, m, d, k, id_offset, out_dists, out_ids, workspace,
+                     workspace_bytes, opts, stream);
+}
+
+bfk_status_t bfk_search_prepared(const float *Q, int64_t n, const float *X, const void *prepared,
+                                 int64_t m, int32_t d, int32_t k, int64_t id_offset,
+                                 float *out_dists, int32_t *out_ids, void *workspace,
+                                 uint64_t workspace_bytes, const bfk_opts_t *opts, void *stream) {
+  if (!prepared || (reinterpret_cast<uintptr_t>(prepared) & 255u)) return BFK_ERR_INVALID_ARGUMENT;
+  return search_impl(Q, n, X, prepared, m, d, k, id_offset, out_dists, out_ids, workspace,
+                     workspace_bytes, opts, stream);
+}
+
+bfk_status_t bfk_prepared_size(int64_t m, int32_t d, uint64_t *bytes) {
+  if (!bytes || m < 0 || m > INT32_MAX || d <= 0) return BFK_ERR_INVALID_ARGUMENT;
+  if (!tc_supported(d, 1)) return BFK_ERR_UNSUPPORTED;
+  *bytes = tc_prepared_layout(m, d).total;
+  return BFK_OK;
+}
+
+bfk_status_t bfk_prepare(const float *X, int64_t m, int32_t d, void *prepared, uint64_t bytes,
+                         void *stream) {
+  if (!prepared || (m > 0 && !X) || m < 0 || m > INT32_MAX || d <= 0) return BFK_ERR_INVALID_ARGUMENT;
+  if ((reinterpret_cast<uintptr_t>(prepared) & 255u) || (reinterpret_cast<uintptr_t>(X) & 3u))
+    return BFK_ERR_INVALID_ARGUMENT;
+  if (!tc_supported(d, 1)) return BFK_ERR_UNSUPPORTED;
+  if (bytes < tc_prepared_layout(m, d).total) return BFK_ERR_WORKSPACE;
+  bfk_status_t s = check_device();
+  if (s != BFK_OK) return s;
+  return tc_prepare(X, m, d, prepared, reinterpret_cast<cudaStream_t>(stream)) == 0 ? BFK_OK
+                                                                                    : BFK_ERR_CUDA;
 }
 
 bfk_status_t bfk_merge(const float *cand_dists, const int32_t *cand_ids, int64_t n,
@@ -324,8 +374,7 @@ bfk_status_t bfk_search_stats(const void *workspace, int64_t n, int64_t m, int32
   out->main_kernel_ms = total;
   if (eng == BFK_ENGINE_TC_F16) {
     TcPlan p;
-    if (tc_make_plan(n, m, d, k, opts ? opts->slices : 0, opts ? opts->max_candidates : 0, opts && (opts->flags & BFK_FLAG_CTA_PAIR),
-                      opts ? opts->plan_rows : 0, &p))
+    if (make_plan(n, m, d, k, opts, &p))
       out->slices = p.slices;
   } else {
     out->slices = direct_plan(n, m, d, k, opts ? opts->slices : 0).slices;

@@ -46,12 +46,38 @@ struct TcPlan {
   int cand_cap;     // candidate entries per query
   // workspace offsets (bytes from the workspace base)
   size_t off_xh, off_xnorm, off_xscale, off_qh, off_qinfo, off_rlev, off_cand, off_ccount,
-      off_flags, off_fbq, off_fbd, off_fbi, off_fbpart_d, off_fbpart_i, total;
+      off_flags, off_fbq, off_fbd, off_fbi, off_fbpart_d, off_fbpart_i, off_invsq, total;
   int fb_slices;
+  bool prepared;    // the rows' f16 form, norms and scales come from a prepared buffer
 };
+
+// A prepared database (bfk_prepare): the TC engine's row arrays for one X, made once.
+// Layout, every part 256-byte aligned: a 256-byte status block (the rows' norm bound and
+// non-finite flag, as the workspace header holds them), a 256-byte description
+// (PreparedInfo), the f16 rows (m, d_pad), ||x||^2 (x_tiles * 256) and the inverse scale
+// of every 64-row group (x_tiles * 4).
+struct PreparedInfo {
+  char magic[8];     // "BFKPREP1"
+  int32_t version;   // 1
+  int32_t d;
+  int64_t m;
+  int32_t d_pad;
+  int32_t reserved0;
+  int64_t x_tiles;
+  uint64_t total;    // bytes of the whole buffer
+};
+struct PreparedLayout {
+  size_t off_status, off_info, off_xh, off_xnorm, off_xinv, total;
+};
+PreparedLayout tc_prepared_layout(int64_t m, int d);
+// Fills `prep` from X on `stream` and waits for it; 0 ok, 1 CUDA error.
+int tc_prepare(const float *X, int64_t m, int d, void *prep, cudaStream_t stream);
+// Reads the description of `prep` back and checks it against (m, d); 0 ok, 1 CUDA
+// error, 3 mismatch.
+int tc_check_prepared(const void *prep, int64_t m, int d);
 bool tc_supported(int d, int k);
 bool tc_make_plan(int64_t n, int64_t m, int d, int k, int slices, int cand_cap, bool pair,
-                  int64_t plan_rows, TcPlan *p);
+                  int64_t plan_rows, bool prepared, TcPlan *p);
 // Returns 0 ok, 1 CUDA error, 2 device timeout.  t0/t1 (may be null) are
 // recorded around the main kernel; *launches counts the kernels launched.
 // `hook` (may be null) is called after every level with the level's bounds;
@@ -59,7 +85,8 @@ bool tc_make_plan(int64_t n, int64_t m, int d, int k, int slices, int cand_cap, 
 typedef void (*LevelHook)(float *bound, int64_t count, void *user, void *stream);
 int tc_run(const float *Q, const float *X, int64_t id_offset, float *out_d, int32_t *out_i,
            void *ws, const TcPlan &p, cudaStream_t stream, cudaEvent_t t0, cudaEvent_t t1,
-           int *launches, LevelHook hook, void *hook_user, int shards);
+           int *launches, LevelHook hook, void *hook_user, int shards,
+           const void *prepared = nullptr);
 const void *tc_kernel_ptr(int d, int k);
 size_t tc_smem_bytes(int d, int k);
 int tc_threads();

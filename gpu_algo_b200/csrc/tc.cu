@@ -31,6 +31,7 @@
 
 #include <algorithm>
 #include <cfloat>
+#include <cstring>
 #include <cmath>
 
 #include "common.cuh"
@@ -605,6 +606,14 @@ __global__ void __launch_bounds__(256) tc_prep_x_kernel(const float *__restrict_
       const float *x = X + row * d;
       for (int c = lane; c < d_pad; c += 32) xh[c] = __float2half_rn(c < d ? x[c] * sc : 0.f);
     }
+  }
+}
+
+// A prepared database's row status (norm bound, non-finite rows) into this search's header.
+__global__ void tc_take_row_status(const WsHeader *src, WsHeader *dst) {
+  if (threadIdx.x == 0) {
+    dst->rx_bits = src->rx_bits;
+    dst->nonfinite = src->nonfinite;
   }
 }
 
@@ -1428,7 +1437,7 @@ static int choose_slices(int q_tiles, int64_t tiles, int sms, int max_s) {
 }
 
 bool tc_make_plan(int64_t n, int64_t m, int d, int k, int slices, int pool, bool pair,
-                  int64_t plan_rows, TcPlan *p) {
+                  int64_t plan_rows, bool prepared, TcPlan *p) {
   if (!tc_supported(d, k) || n <= 0 || m <= 0) return false;
   TcPlan P{};
   P.n = n;
@@ -1498,9 +1507,13 @@ bool tc_make_plan(int64_t n, int64_t m, int d, int k, int slices, int pool, bool
   if (P.fb_slices < 1) P.fb_slices = 1;
   const int64_t q_rows = (int64_t)P.q_tiles * kBM;
   size_t off = sizeof(WsHeader);
-  P.off_xh = off;       off = al256(off + (size_t)m * P.d_pad * 2);
-  P.off_xnorm = off;    off = al256(off + (size_t)P.x_tiles * kBN * 4);
-  P.off_xscale = off;   off = al256(off + (size_t)P.x_tiles * kColGroups * 4 + 16);
+  // the row arrays live in the workspace unless a prepared buffer holds them
+  P.prepared = prepared;
+  const size_t rows_f = prepared ? 0 : 1;
+  P.off_xh = off;       off = al256(off + rows_f * (size_t)m * P.d_pad * 2);
+  P.off_xnorm = off;    off = al256(off + rows_f * (size_t)P.x_tiles * kBN * 4);
+  P.off_xscale = off;   off = al256(off + rows_f * (size_t)P.x_tiles * kColGroups * 4);
+  P.off_invsq = off;    off = al256(off + 16);
   P.off_qh = off;       off = al256(off + (size_t)q_rows * P.d_pad * 2);
   P.off_qinfo = off;    off = al256(off + (size_t)q_rows * 8);
   P.off_rlev = off;     off = al256(off + (size_t)n * 8);  // two bounds per query
@@ -1545,15 +1558,99 @@ static bool make_tmap(CUtensorMap *map, const void *base, int64_t rows, int cols
   return r == CUDA_SUCCESS;
 }
 
+// rows -> f16 in 64-row scale groups, ||x||^2, inverse scales; norm bound and
+// non-finite flag into hdr
+static void launch_prep_rows(const float *X, int64_t m, int d, int d_pad, int64_t x_tiles,
+                             __half *Xh, float *xnorm, float *xinv, WsHeader *hdr,
+                             cudaStream_t stream) {
+  const unsigned groups = (unsigned)(x_tiles * kColGroups);  // 64-row scale groups
+  const bool vec = (d & 3) == 0 && (reinterpret_cast<uintptr_t>(X) & 15) == 0;
+  if (vec && d_pad <= 128)
+    tc_prep_x_kernel<true, 1><<<groups, 256, 0, stream>>>(X, m, d, d_pad, Xh, xnorm, xinv, hdr);
+  else if (vec && d_pad <= 256)
+    tc_prep_x_kernel<true, 2><<<groups, 256, 0, stream>>>(X, m, d, d_pad, Xh, xnorm, xinv, hdr);
+  else
+    tc_prep_x_kernel<false, 1><<<groups, 256, 0, stream>>>(X, m, d, d_pad, Xh, xnorm, xinv, hdr);
+}
+
+PreparedLayout tc_prepared_layout(int64_t m, int d) {
+  PreparedLayout L{};
+  const int d_pad = kch_for(d) * kBK;
+  const int64_t x_tiles = (m + kBN - 1) / kBN;
+  size_t off = 0;
+  L.off_status = off; off = al256(off + sizeof(WsHeader));
+  L.off_info = off;   off = al256(off + sizeof(PreparedInfo));
+  L.off_xh = off;     off = al256(off + (size_t)m * d_pad * 2);
+  L.off_xnorm = off;  off = al256(off + (size_t)x_tiles * kBN * 4);
+  L.off_xinv = off;   off = al256(off + (size_t)x_tiles * kColGroups * 4);
+  L.total = off;
+  return L;
+}
+
+static PreparedInfo prepared_info(int64_t m, int d) {
+  PreparedInfo I{};
+  memcpy(I.magic, "BFKPREP1", 8);
+  I.version = 1;
+  I.d = d;
+  I.m = m;
+  I.d_pad = kch_for(d) * kBK;
+  I.x_tiles = (m + kBN - 1) / kBN;
+  I.total = tc_prepared_layout(m, d).total;
+  return I;
+}
+
+int tc_prepare(const float *X, int64_t m, int d, void *prep, cudaStream_t stream) {
+  const PreparedLayout L = tc_prepared_layout(m, d);
+  unsigned char *pb = static_cast<unsigned char *>(prep);
+  WsHeader *status = reinterpret_cast<WsHeader *>(pb + L.off_status);
+  const PreparedInfo I = prepared_info(m, d);
+  cudaError_t e = cudaMemsetAsync(status, 0, sizeof(WsHeader), stream);
+  if (e == cudaSuccess)
+    e = cudaMemcpyAsync(pb + L.off_info, &I, sizeof(I), cudaMemcpyHostToDevice, stream);
+  if (e == cudaSuccess) {
+    launch_prep_rows(X, m, d, I.d_pad, I.x_tiles, reinterpret_cast<__half *>(pb + L.off_xh),
+                     reinterpret_cast<float *>(pb + L.off_xnorm),
+                     reinterpret_cast<float *>(pb + L.off_xinv), status, stream);
+    e = cudaGetLastError();
+  }
+  // the description is copied from this stack frame: wait before returning
+  if (e == cudaSuccess) e = cudaStreamSynchronize(stream);
+  if (e != cudaSuccess) {
+    BFK_NOTE(e, "bfk_prepare");
+    return 1;
+  }
+  return 0;
+}
+
+int tc_check_prepared(const void *prep, int64_t m, int d) {
+  const PreparedLayout L = tc_prepared_layout(m, d);
+  PreparedInfo got{};
+  const cudaError_t e = cudaMemcpy(&got, static_cast<const unsigned char *>(prep) + L.off_info,
+                                   sizeof(got), cudaMemcpyDeviceToHost);
+  if (e != cudaSuccess) {
+    BFK_NOTE(e, "bfk_search_prepared: reading the description");
+    return 1;
+  }
+  const PreparedInfo want = prepared_info(m, d);
+  return memcmp(&got, &want, sizeof(got)) == 0 ? 0 : 3;
+}
+
 int tc_run(const float *Q, const float *X, int64_t id_offset, float *out_d, int32_t *out_i,
            void *ws_, const TcPlan &p, cudaStream_t stream, cudaEvent_t t0, cudaEvent_t t1,
-           int *launches, LevelHook hook, void *hook_user, int shards) {
+           int *launches, LevelHook hook, void *hook_user, int shards, const void *prepared) {
   unsigned char *ws = static_cast<unsigned char *>(ws_);
   WsHeader *hdr = reinterpret_cast<WsHeader *>(ws);
   __half *Xh = reinterpret_cast<__half *>(ws + p.off_xh);
   float *xnorm = reinterpret_cast<float *>(ws + p.off_xnorm);
   float *xinv = reinterpret_cast<float *>(ws + p.off_xscale);
-  float *inv_sq = xinv + p.x_tiles * kColGroups;  // one float after the group scales
+  float *inv_sq = reinterpret_cast<float *>(ws + p.off_invsq);
+  const unsigned char *pb = static_cast<const unsigned char *>(prepared);
+  if (prepared) {
+    const PreparedLayout PL = tc_prepared_layout(p.m, p.d);
+    Xh = reinterpret_cast<__half *>(const_cast<unsigned char *>(pb) + PL.off_xh);
+    xnorm = reinterpret_cast<float *>(const_cast<unsigned char *>(pb) + PL.off_xnorm);
+    xinv = reinterpret_cast<float *>(const_cast<unsigned char *>(pb) + PL.off_xinv);
+  }
   __half *Qh = reinterpret_cast<__half *>(ws + p.off_qh);
   float2 *qinfo = reinterpret_cast<float2 *>(ws + p.off_qinfo);
   float *rlev = reinterpret_cast<float *>(ws + p.off_rlev);
@@ -1575,14 +1672,14 @@ int tc_run(const float *Q, const float *X, int64_t id_offset, float *out_d, int3
   BFK_TRY(cudaMemsetAsync(hdr, 0, sizeof(WsHeader), stream));
   // pass 0: prep
   tc_qmax_kernel<<<592, 256, 0, stream>>>(Q, p.n * p.d, hdr);
-  const unsigned groups = (unsigned)(p.x_tiles * kColGroups);  // 64-row scale groups
-  const bool vec = (p.d & 3) == 0 && (reinterpret_cast<uintptr_t>(X) & 15) == 0;
-  if (vec && p.d_pad <= 128)
-    tc_prep_x_kernel<true, 1><<<groups, 256, 0, stream>>>(X, p.m, p.d, p.d_pad, Xh, xnorm, xinv, hdr);
-  else if (vec && p.d_pad <= 256)
-    tc_prep_x_kernel<true, 2><<<groups, 256, 0, stream>>>(X, p.m, p.d, p.d_pad, Xh, xnorm, xinv, hdr);
-  else
-    tc_prep_x_kernel<false, 1><<<groups, 256, 0, stream>>>(X, p.m, p.d, p.d_pad, Xh, xnorm, xinv, hdr);
+  if (prepared) {
+    // the rows' norm bound and non-finite flag, as their preparation found them
+    const PreparedLayout PL = tc_prepared_layout(p.m, p.d);
+    tc_take_row_status<<<1, 32, 0, stream>>>(
+        reinterpret_cast<const WsHeader *>(pb + PL.off_status), hdr);
+  } else {
+    launch_prep_rows(X, p.m, p.d, p.d_pad, p.x_tiles, Xh, xnorm, xinv, hdr, stream);
+  }
   tc_prep_q_kernel<<<(unsigned)(q_rows / 8), 256, 0, stream>>>(Q, p.n, p.d, p.d_pad, q_rows, Qh,
                                                                 qinfo, inv_sq, hdr);
   nl += 3;

@@ -10,6 +10,7 @@ from __future__ import annotations
 import ctypes
 import threading
 
+import numpy as np
 import torch
 
 from . import _lib
@@ -66,7 +67,7 @@ class _DeviceArray:
 def search(Q, X, k: int, *, engine: str = "auto", slices: int = 0, max_candidates: int = 0,
            id_offset: int = 0, out: tuple[torch.Tensor, torch.Tensor] | None = None,
            ws: torch.Tensor | None = None, time_main: bool = False, cta_pair: bool = False,
-           bound_hook=None, plan_rows: int = 0, shards: int = 0):
+           bound_hook=None, plan_rows: int = 0, shards: int = 0, prepared=None):
     """Exact k-NN on the GPU.  Returns (dists, ids) device tensors.
 
     ``bound_hook(t)``, if given, is called by the tensor-core engine after each
@@ -74,7 +75,8 @@ def search(Q, X, k: int, *, engine: str = "auto", slices: int = 0, max_candidate
     may lower in place (a sharded search takes the minimum over shards): (n,)
     values, or (2n,) when ``shards`` > 1 (the number of shards in that minimum;
     see ``bfk_level_hook_t``).  ``plan_rows`` makes shards of one search plan
-    the same levels.
+    the same levels.  ``prepared`` (a ``PreparedRows`` of this X) skips the
+    conversion of the rows.
     """
     Q = as_device_f32(Q, "Q")
     X = as_device_f32(X, "X")
@@ -93,6 +95,11 @@ def search(Q, X, k: int, *, engine: str = "auto", slices: int = 0, max_candidate
                           (_lib.FLAG_CTA_PAIR if cta_pair else 0))
     opts.plan_rows = int(plan_rows)
     opts.shards = int(shards)
+    if prepared is not None:
+        if prepared.shape != (m, d) or prepared.buffer.device != X.device:
+            raise ValueError(f"prepared rows are {prepared.shape} on {prepared.buffer.device}, "
+                             f"X is {(m, d)} on {X.device}")
+        opts.flags |= _lib.FLAG_PREPARED
     hook_error = []
     if bound_hook is not None:
         def _hook(ptr, count, user, stream_ptr):
@@ -114,17 +121,80 @@ def search(Q, X, k: int, *, engine: str = "auto", slices: int = 0, max_candidate
             ws = workspace(nbytes, Q.device, stream)
         elif ws.numel() < nbytes:
             raise ValueError(f"workspace needs {nbytes} bytes, got {ws.numel()}")
-        st = lib.bfk_search(Q.data_ptr(), n, X.data_ptr() if m else None, m, d, k, int(id_offset),
-                            dists.data_ptr(), ids.data_ptr(), ws.data_ptr(), ws.numel(),
-                            ctypes.byref(opts), ctypes.c_void_p(stream.cuda_stream))
+        if prepared is None:
+            st = lib.bfk_search(Q.data_ptr(), n, X.data_ptr() if m else None, m, d, k,
+                                int(id_offset), dists.data_ptr(), ids.data_ptr(), ws.data_ptr(),
+                                ws.numel(), ctypes.byref(opts),
+                                ctypes.c_void_p(stream.cuda_stream))
+        else:
+            st = lib.bfk_search_prepared(Q.data_ptr(), n, X.data_ptr() if m else None,
+                                         prepared.buffer.data_ptr(), m, d, k, int(id_offset),
+                                         dists.data_ptr(), ids.data_ptr(), ws.data_ptr(),
+                                         ws.numel(), ctypes.byref(opts),
+                                         ctypes.c_void_p(stream.cuda_stream))
         if hook_error:
             raise hook_error[0]
         _lib.check(st, "bfk_search")
     return dists, ids
 
 
+class PreparedRows:
+    """The tensor-core engine's form of one database X (``bfk_prepare``): f16 rows in
+    64-row groups scaled by powers of two, ||x||^2 and the group scales.  A search with
+    ``prepared=`` skips that conversion; it still reads X for the exact re-rank.
+
+    ``save(path)`` writes the buffer's bytes (a 512-byte header that records m and d,
+    then the arrays); ``load(path, device)`` reads them back.  The library rejects a
+    buffer made for another (m, d).
+    """
+
+    def __init__(self, buffer: torch.Tensor, shape: tuple[int, int]):
+        self.buffer = buffer
+        self.shape = (int(shape[0]), int(shape[1]))
+
+    @staticmethod
+    def nbytes(m: int, d: int) -> int:
+        nb = ctypes.c_uint64()
+        _lib.check(_lib.load().bfk_prepared_size(int(m), int(d), ctypes.byref(nb)),
+                   "bfk_prepared_size")
+        return int(nb.value)
+
+    @classmethod
+    def prepare(cls, X) -> "PreparedRows":
+        X = as_device_f32(X, "X")
+        m, d = X.shape
+        with torch.cuda.device(X.device):
+            stream = torch.cuda.current_stream()
+            nb = cls.nbytes(m, d)
+            buf = torch.empty(nb, dtype=torch.uint8, device=X.device)
+            _lib.check(_lib.load().bfk_prepare(X.data_ptr() if m else None, m, d,
+                                               buf.data_ptr(), nb,
+                                               ctypes.c_void_p(stream.cuda_stream)),
+                       "bfk_prepare")
+        return cls(buf, (m, d))
+
+    def save(self, path) -> None:
+        header = np.array([self.shape[0], self.shape[1]], dtype=np.int64)
+        with open(path, "wb") as f:
+            f.write(b"BFKROWS1")
+            f.write(header.tobytes())
+            f.write(self.buffer.cpu().numpy().tobytes())
+
+    @classmethod
+    def load(cls, path, device) -> "PreparedRows":
+        with open(path, "rb") as f:
+            if f.read(8) != b"BFKROWS1":
+                raise ValueError(f"{path} is not a prepared-rows file")
+            m, d = (int(v) for v in np.frombuffer(f.read(16), dtype=np.int64))
+            data = np.frombuffer(f.read(), dtype=np.uint8)
+        if data.size != cls.nbytes(m, d):
+            raise ValueError(f"{path}: {data.size} bytes, expected {cls.nbytes(m, d)}")
+        return cls(torch.from_numpy(data.copy()).to(device), (m, d))
+
+
 def last_stats(Q, X, k: int, *, engine: str = "auto", slices: int = 0,
-               max_candidates: int = 0, plan_rows: int = 0, shards: int = 0) -> dict:
+               max_candidates: int = 0, plan_rows: int = 0, shards: int = 0,
+               prepared: bool = False) -> dict:
     """Statistics of the last search of this shape on the current stream's workspace
     (pass the search's own engine options)."""
     Q = as_device_f32(Q, "Q")
@@ -134,6 +204,8 @@ def last_stats(Q, X, k: int, *, engine: str = "auto", slices: int = 0,
     opts = _lib.make_opts(engine, slices, max_candidates)
     opts.plan_rows = int(plan_rows)
     opts.shards = int(shards)
+    if prepared:
+        opts.flags |= _lib.FLAG_PREPARED
     with torch.cuda.device(Q.device):
         stream = torch.cuda.current_stream()
         ws = workspace(workspace_size(n, m, d, k, opts), Q.device, stream)

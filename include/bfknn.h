@@ -50,6 +50,8 @@ typedef enum {
 
 #define BFK_FLAG_TIME_MAIN 1 /* time the main kernel of every call with CUDA events      */
 #define BFK_FLAG_CTA_PAIR 2  /* TC engine: CTA pairs (tcgen05.mma.cta_group::2, M = 256)  */
+#define BFK_FLAG_PREPARED 4  /* the search reads its rows' TC form from a prepared buffer
+                                (bfk_search_prepared); the workspace then holds no rows */
 
 /*
  * Called by the TC engine after each filter level with `bound` (device, `count`
@@ -139,6 +141,28 @@ BFK_API bfk_status_t bfk_search(const float *Q, int64_t n, const float *X, int64
                         int32_t k, int64_t id_offset, float *out_dists, int32_t *out_ids,
                         void *workspace, uint64_t workspace_bytes, const bfk_opts_t *opts,
                         void *stream);
+
+/*
+ * Prepared database.  No reference counterpart (the reference re-reads X in FP32 on every
+ * call).  bfk_prepare converts X (m, d) once into the TC engine's row form: f16 rows in
+ * 64-row groups scaled by powers of two, ||x||^2 and the group scales, with a header that
+ * records m and d.  bfk_search_prepared then skips that pass; it still reads X for the
+ * exact FP32 re-rank, so X must be the array the buffer was prepared from.  The buffer's
+ * bytes are position-independent: copied to a file and back, they stay valid for the same
+ * X and library version.  `prepared` is device memory, 256-byte aligned.
+ */
+BFK_API bfk_status_t bfk_prepared_size(int64_t m, int32_t d, uint64_t *bytes);
+BFK_API bfk_status_t bfk_prepare(const float *X, int64_t m, int32_t d, void *prepared,
+                                 uint64_t bytes, void *stream);
+/* bfk_search with the rows' TC form from `prepared`; `opts` must carry BFK_FLAG_PREPARED
+ * (bfk_workspace_size with that flag sizes the smaller workspace).  A buffer made for other
+ * (m, d) is rejected with BFK_ERR_INVALID_ARGUMENT.  Shapes that the SIMT engine takes
+ * ignore the buffer. */
+BFK_API bfk_status_t bfk_search_prepared(const float *Q, int64_t n, const float *X,
+                                         const void *prepared, int64_t m, int32_t d, int32_t k,
+                                         int64_t id_offset, float *out_dists, int32_t *out_ids,
+                                         void *workspace, uint64_t workspace_bytes,
+                                         const bfk_opts_t *opts, void *stream);
 
 /*
  * Merge `lists` sorted candidate lists per query, laid out (lists, n, k), into
