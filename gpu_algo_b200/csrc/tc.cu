@@ -945,14 +945,18 @@ __global__ void __launch_bounds__(kSelThreads) tc_level_select_kernel(const Leve
 // The kk-th smallest (1-based, kk <= count) of `count` ordered keys in shared
 // memory, by one warp: four passes of an 8-bit radix select, most significant digit
 // first; `hist` is the warp's own 256 counters.
-__device__ uint32_t warp_select_key(const uint32_t *keys, int count, int kk, int *hist) {
+// Keys at positions >= `staged` are not in shared memory: `more(e)` loads them (each
+// pass reads them again).
+template <class More>
+__device__ uint32_t warp_select_key(const uint32_t *keys, int staged, int count, int kk, int *hist,
+                                    More more) {
   const int lane = threadIdx.x & 31;
   uint32_t prefix = 0, mask = 0;
   for (int shift = 24; shift >= 0; shift -= 8) {
     for (int b = lane; b < 256; b += 32) hist[b] = 0;
     __syncwarp();
     for (int e = lane; e < count; e += 32) {
-      const uint32_t key = keys[e];
+      const uint32_t key = e < staged ? keys[e] : more(e);
       if ((key & mask) == prefix) atomicAdd(&hist[(key >> shift) & 255u], 1);
     }
     __syncwarp();
@@ -993,9 +997,8 @@ constexpr int kWarpSelQueries = 8;  // queries (warps) per block
 
 // Level select of shards that share bounds, one warp per query: each shard holds a
 // small share of a query's candidates, so a warp stages up to kWarpSelCap of them
-// (as ordered keys of v) and selects the exact k-th and k2-th smallest.  A query with
-// more candidates uses the first kWarpSelCap: the k-th smallest of any k real rows
-// is still a bound.  dynamic smem: 8 * (kWarpSelCap + 256 + 256) * 4
+// (as ordered keys of v) and selects the exact k-th and k2-th smallest.  The
+// candidates of a query with more are read again from global memory by every pass.  dynamic smem: 8 * (kWarpSelCap + 256 + 256) * 4
 __global__ void __launch_bounds__(kSelThreads) tc_level_select_warp_kernel(const LevelSelArgs a) {
   extern __shared__ __align__(1024) unsigned char smem_raw[];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -1054,14 +1057,23 @@ __global__ void __launch_bounds__(kSelThreads) tc_level_select_warp_kernel(const
     }
   }
   __syncwarp();
+  auto more = [&](int e) {
+    int lo = 0, hi = a.nreg - 1;
+    while (lo < hi) {
+      const int mid = (lo + hi + 1) >> 1;
+      if (off[mid] <= e) lo = mid; else hi = mid - 1;
+    }
+    const float v = __uint_as_float(base[(size_t)lo * a.region + (e - off[lo])].y);
+    return v == v ? f2ord(v) : 0xffffffffu;
+  };
   // R (R2): the k-th (k2-th) smallest v of real candidates; +inf when there are fewer
   float r1 = INFINITY, r2 = INFINITY;
-  if (staged >= a.k) {
-    const uint32_t key = warp_select_key(keys, staged, a.k, hist);
+  if (total >= a.k) {
+    const uint32_t key = warp_select_key(keys, staged, total, a.k, hist, more);
     if (key != 0xffffffffu) r1 = ord2f(key);
   }
-  if (a.k2 > 0 && staged >= a.k2) {
-    const uint32_t key = warp_select_key(keys, staged, a.k2, hist);
+  if (a.k2 > 0 && total >= a.k2) {
+    const uint32_t key = warp_select_key(keys, staged, total, a.k2, hist, more);
     if (key != 0xffffffffu) r2 = ord2f(key);
   }
   if (lane == 0) {
