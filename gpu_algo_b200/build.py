@@ -20,7 +20,7 @@ CSRC = os.path.join(PKG, "csrc")
 INCLUDE = os.path.join(os.path.dirname(PKG), "include")
 BUILD = os.path.join(PKG, "_build")
 LIB = os.path.join(PKG, "libbfknn.so")
-SOURCES = ["bfknn.cu", "direct.cu", "merge.cu", "tc.cu", "noalloc.cu"]
+SOURCES = ["bfknn.cu", "direct.cu", "merge.cu", "tc.cu", "noalloc.cu", "scan.cu"]
 HEADERS = ["common.cuh", "internal.h"]
 
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]

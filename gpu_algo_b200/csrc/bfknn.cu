@@ -19,6 +19,7 @@ size_t align256(size_t x) { return (x + 255) & ~(size_t)255; }
 
 struct DirectPlan {
   int tq, slices;
+  bool scan;  // small batch: the streaming scan kernel, `slices` blocks of rows
   size_t off_part_d, off_part_i, total;
 };
 
@@ -30,6 +31,18 @@ int sm_count() {
 
 DirectPlan direct_plan(int64_t n, int64_t m, int d, int k, int slices_req) {
   DirectPlan p{};
+  if (slices_req <= 0 && m >= 8192 && scan_supported(n, d, k)) {
+    // a handful of queries: one streaming pass over the rows, many warps in flight
+    p.scan = true;
+    p.slices = scan_blocks(m, k);
+    size_t off = sizeof(WsHeader);
+    p.off_part_d = off;
+    off = align256(off + (size_t)p.slices * n * k * sizeof(float));
+    p.off_part_i = off;
+    off = align256(off + (size_t)p.slices * n * k * sizeof(int32_t));
+    p.total = align256(off);
+    return p;
+  }
   p.tq = (n >= 64 && k <= 512) ? 4 : 1;
   const int qb = 8 * p.tq;
   const int64_t qblocks = (n + qb - 1) / qb;
@@ -242,6 +255,19 @@ static bfk_status_t search_impl(const float *Q, int64_t n, const float *X, const
     return cuda_status(launch_fill_pad(out_dists, out_ids, n * k, stream));
   }
   if (t0) cudaEventRecord(t0, stream);
+  if (p.scan) {
+    const bool one = p.slices == 1;
+    float *pd = one ? out_dists : reinterpret_cast<float *>(ws + p.off_part_d);
+    int32_t *pi = one ? out_ids : reinterpret_cast<int32_t *>(ws + p.off_part_i);
+    e = launch_scan(Q, n, X, m, d, k, id_offset, p.slices, pd, pi, stream);
+    if (t1) cudaEventRecord(t1, stream);
+    if (e != cudaSuccess || one) {
+      g_calls.launches = 1;
+      return cuda_status(e);
+    }
+    g_calls.launches = 2;
+    return cuda_status(launch_merge(pd, pi, n, p.slices, k, out_dists, out_ids, stream));
+  }
   if (p.slices == 1) {
     e = launch_direct(Q, n, X, m, d, k, id_offset, 1, p.tq, out_dists, out_ids, stream);
     if (t1) cudaEventRecord(t1, stream);

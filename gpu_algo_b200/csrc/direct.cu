@@ -18,31 +18,6 @@ namespace bfk {
 constexpr int kDirRT = 128;  // database rows per tile
 constexpr int kDirDC = 32;   // dimensions per chunk
 
-// Insert (d, gid) into the sorted list (ld, li) of length cnt <= k; warp-collective.
-__device__ __forceinline__ void warp_insert(float *ld, int32_t *li, int &cnt, int k, float d,
-                                            int32_t gid, int lane) {
-  int p = 0;
-  for (int b = 0; b < cnt; b += 32) {
-    int e = b + lane;
-    bool lt = e < cnt && pair_lt(ld[e], li[e], d, gid);
-    p += __popc(__ballot_sync(0xffffffffu, lt));
-  }
-  const int newcnt = cnt + 1 < k ? cnt + 1 : k;
-  for (int top = newcnt - 1; top > p; top -= 32) {
-    int e = top - lane;
-    bool act = e > p;
-    float td = 0.f;
-    int32_t ti = 0;
-    if (act) { td = ld[e - 1]; ti = li[e - 1]; }
-    __syncwarp();
-    if (act) { ld[e] = td; li[e] = ti; }
-    __syncwarp();
-  }
-  if (lane == 0) { ld[p] = d; li[p] = gid; }
-  __syncwarp();
-  cnt = newcnt;
-}
-
 // grid (ceil(n / QB), slices); block 256 threads.
 // Slice s covers rows [s*slice_len, min((s+1)*slice_len, m)).  With one slice
 // the sorted top-k goes to (out_d, out_i) (n, k); with more, slice s writes

@@ -18,6 +18,13 @@ cudaError_t launch_direct(const float *Q, int64_t n, const float *X, int64_t m, 
                           cudaStream_t stream);
 
 // merge.cu -- sorted-list merge
+// streaming scan for n <= 16 queries (scan.cu): `blocks` row ranges, each writing its
+// sorted top-k per query to out + b*n*k
+bool scan_supported(int64_t n, int d, int k);
+int scan_blocks(int64_t m, int k);
+cudaError_t launch_scan(const float *Q, int64_t n, const float *X, int64_t m, int d, int k,
+                        int64_t id_offset, int blocks, float *out_d, int32_t *out_i,
+                        cudaStream_t stream);
 cudaError_t launch_merge(const float *cand_d, const int32_t *cand_i, int64_t n, int lists, int k,
                          float *out_d, int32_t *out_i, cudaStream_t stream);
 int merge_max_k();

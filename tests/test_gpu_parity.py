@@ -162,6 +162,23 @@ def test_merge_rank_and_grouped_paths(lists, k):
     assert_exact(md.cpu().numpy(), mi.cpu().numpy(), ed, ei, f"merge {lists}x{k}")
 
 
+@pytest.mark.parametrize("n,m,d,k", [(1, 100_000, 96, 10), (3, 50_000, 33, 1), (16, 70_001, 96, 64),
+                                     (9, 40_000, 300, 17), (16, 8192, 128, 10)])
+def test_small_batch_scan_is_exact(n, m, d, k):
+    """n <= 16 queries take the streaming scan (one pass over the rows, warps with
+    their own lists, merged per block and then across blocks); with duplicate
+    rows (exact ties) and a NaN row."""
+    rng = np.random.Generator(np.random.PCG64(n * 7 + d))
+    X = rng.standard_normal((m, d), dtype=np.float32)
+    X[m // 2: m // 2 + 40] = X[7]       # ties at equal distance: lower index first
+    X[m // 3, 0] = np.nan
+    Q = rng.standard_normal((n, d), dtype=np.float32)
+    Q[0] = X[7] + np.float32(0.001)
+    ed, ei = oracle_knn(Q, X, k)
+    d_, i_ = run(Q, X, k)
+    assert_exact(d_, i_, ed, ei, f"scan n={n} m={m} d={d} k={k}")
+
+
 def test_large_k_and_high_d():
     rng = np.random.Generator(np.random.PCG64(11))
     X = rng.standard_normal((20_000, 960), dtype=np.float32)
