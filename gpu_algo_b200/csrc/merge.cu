@@ -11,6 +11,7 @@ namespace bfk {
 
 constexpr int kMergeThreads = 256;
 constexpr int kMergeCap = 8192;  // keys sorted at once (64 KB of shared memory)
+constexpr int kRankMergeLists = 16;  // more lists: the bitonic path is cheaper
 
 __device__ void block_bitonic_sort(uint64_t *keys, int P) {
   for (int size = 2; size <= P; size <<= 1) {
@@ -62,7 +63,7 @@ __global__ void __launch_bounds__(kMergeThreads) knn_merge_kernel(
   }
 }
 
-// Merge by rank, for lists * k <= kMergeCap: every key's place in the merged order
+// Merge by rank, for up to kRankMergeLists lists and lists * k <= kMergeCap: every key's place in the merged order
 // is its index in its own list plus, in every other list, the number of keys
 // before it (binary searches; equal keys order by list), so one pass places
 // each of the first k keys without a sort.  grid (n), dynamic smem lists*k*8.
@@ -105,7 +106,8 @@ __global__ void __launch_bounds__(kMergeThreads) knn_merge_rank_kernel(
 cudaError_t launch_merge(const float *cand_d, const int32_t *cand_i, int64_t n, int lists, int k,
                          float *out_d, int32_t *out_i, cudaStream_t stream) {
   if (n == 0) return cudaSuccess;
-  if ((int64_t)lists * k <= kMergeCap) {
+  // by rank for a few lists (each key binary-searches every other list); sorting for many
+  if (lists <= kRankMergeLists && (int64_t)lists * k <= kMergeCap) {
     const size_t rsmem = (size_t)lists * k * sizeof(uint64_t);
     cudaError_t e = cudaFuncSetAttribute((const void *)knn_merge_rank_kernel,
                                          cudaFuncAttributeMaxDynamicSharedMemorySize,
