@@ -617,6 +617,101 @@ __global__ void tc_take_row_status(const WsHeader *src, WsHeader *dst) {
   }
 }
 
+// Database rows -> f16 for wide rows (d % 4 == 0, d > 256): the same 64-row scale
+// groups as tc_prep_x_kernel, in two passes over each row with float4 loads (four in
+// flight per lane): norms and the group maximum, then the conversion, whose re-read of
+// the group's rows mostly hits L2.  grid (ceil(m / 64)), block 256: eight warps of eight
+// rows each.
+__global__ void __launch_bounds__(256) tc_prep_x_wide_kernel(const float *__restrict__ X,
+                                                             int64_t m, int d, int d_pad,
+                                                             __half *__restrict__ Xh,
+                                                             float *__restrict__ xnorm,
+                                                             float *__restrict__ xinv,
+                                                             WsHeader *hdr) {
+  __shared__ float s_max[8], s_rn[8];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int64_t grp = blockIdx.x;
+  const int64_t row_base = grp * kScaleRows + warp * 8;
+  const int d4 = d >> 2, dp4 = d_pad >> 2;
+  float wmax = 0.f, wrn = 0.f;
+  bool bad = false;
+  for (int u = 0; u < 8; u++) {
+    const int64_t row = row_base + u;
+    float ss = 0.f, mx = 0.f;
+    if (row < m) {
+      const float4 *x4 = reinterpret_cast<const float4 *>(X + row * d);
+      for (int c0 = lane; c0 < d4; c0 += 4 * 32) {
+        float4 v[4];
+#pragma unroll
+        for (int h = 0; h < 4; h++) {
+          const int c = c0 + 32 * h;
+          v[h] = c < d4 ? __ldg(x4 + c) : make_float4(0.f, 0.f, 0.f, 0.f);
+        }
+#pragma unroll
+        for (int h = 0; h < 4; h++) {
+          ss = __fmaf_rn(v[h].x, v[h].x, ss);
+          ss = __fmaf_rn(v[h].y, v[h].y, ss);
+          ss = __fmaf_rn(v[h].z, v[h].z, ss);
+          ss = __fmaf_rn(v[h].w, v[h].w, ss);
+          mx = fmaxf(mx, fmaxf(fmaxf(fabsf(v[h].x), fabsf(v[h].y)), fmaxf(fabsf(v[h].z), fabsf(v[h].w))));
+        }
+      }
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      ss += __shfl_xor_sync(0xffffffffu, ss, o);
+      mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+    }
+    if (row < m) {
+      if (!isfinite(ss)) bad = true;
+      wmax = fmaxf(wmax, mx);
+      wrn = fmaxf(wrn, sqrtf(ss));
+    }
+    // rows past m: v = +inf never passes a finite threshold
+    if (lane == 0) xnorm[row] = row < m ? ss : INFINITY;
+  }
+  if (lane == 0) { s_max[warp] = wmax; s_rn[warp] = wrn; }
+  if (bad && lane == 0) atomicOr(&hdr->nonfinite, 1);
+  __syncthreads();
+  float gmax = 0.f, rn = 0.f;
+#pragma unroll
+  for (int w = 0; w < 8; w++) { gmax = fmaxf(gmax, s_max[w]); rn = fmaxf(rn, s_rn[w]); }
+  const float sc = pow2_scale_for(gmax);
+  if (threadIdx.x == 0) {
+    xinv[grp] = 1.f / sc;
+    // sqrt of an FP32 sum of d squares: (1 + 2^-10) covers its rounding for d <= 4096;
+    // the bound only grows, and non-negative floats order like their bit patterns
+    if (isfinite(rn)) atomicMax(&hdr->rx_bits, __float_as_uint(rn * (1.f + 0.0009765625f)));
+  }
+  for (int u = 0; u < 8; u++) {
+    const int64_t row = row_base + u;
+    if (row >= m) break;
+    const float4 *x4 = reinterpret_cast<const float4 *>(X + row * d);
+    uint2 *xh2 = reinterpret_cast<uint2 *>(Xh + row * d_pad);
+    for (int c0 = lane; c0 < dp4; c0 += 4 * 32) {
+      float4 v[4];
+#pragma unroll
+      for (int h = 0; h < 4; h++) {
+        const int c = c0 + 32 * h;
+        v[h] = c < d4 ? __ldg(x4 + c) : make_float4(0.f, 0.f, 0.f, 0.f);
+      }
+#pragma unroll
+      for (int h = 0; h < 4; h++) {
+        const int c = c0 + 32 * h;
+        if (c < dp4) {
+          // four halves (8 bytes) per lane and step; columns past d are zero
+          __half2 lo = __floats2half2_rn(v[h].x * sc, v[h].y * sc);
+          __half2 hi = __floats2half2_rn(v[h].z * sc, v[h].w * sc);
+          uint2 pk;
+          pk.x = *reinterpret_cast<uint32_t *>(&lo);
+          pk.y = *reinterpret_cast<uint32_t *>(&hi);
+          xh2[c] = pk;
+        }
+      }
+    }
+  }
+}
+
 // max |Q| -> hdr->qmax_bits
 __global__ void tc_qmax_kernel(const float *__restrict__ Q, int64_t count, WsHeader *hdr) {
   float mx = 0.f;
@@ -1581,6 +1676,8 @@ static void launch_prep_rows(const float *X, int64_t m, int d, int d_pad, int64_
     tc_prep_x_kernel<true, 1><<<groups, 256, 0, stream>>>(X, m, d, d_pad, Xh, xnorm, xinv, hdr);
   else if (vec && d_pad <= 256)
     tc_prep_x_kernel<true, 2><<<groups, 256, 0, stream>>>(X, m, d, d_pad, Xh, xnorm, xinv, hdr);
+  else if (vec)
+    tc_prep_x_wide_kernel<<<groups, 256, 0, stream>>>(X, m, d, d_pad, Xh, xnorm, xinv, hdr);
   else
     tc_prep_x_kernel<false, 1><<<groups, 256, 0, stream>>>(X, m, d, d_pad, Xh, xnorm, xinv, hdr);
 }
