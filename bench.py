@@ -45,7 +45,7 @@ PUBLISHED_QPS = {("published-d8", 1_000_000, 128_000, 8, 1): 607_025.0}
 # (1.242 GB / 3M rows), single-CTA kernel.  Its writes are the candidate appends, 8 bytes
 # each (0.386 GB for the sample's 41.3M candidates, 9.3 B each with write granularity).
 TRAFFIC_READ_PER_ROW = {("unit-10m", 10_000, 128, 100): 414}
-TRAFFIC_WRITE_PER_CANDIDATE = 9.3
+TRAFFIC_WRITE_PER_CANDIDATE = 9.3  # 0.385 GB for 41.3M candidates in the latest capture
 
 
 def parse_args(argv=None):
