@@ -20,16 +20,21 @@ constexpr int kScanWarps = 8;
 
 // dist_step for two queries against one row value in packed FP32 instructions:
 // (qa, qb) - (x, x) and fma(dif, dif, acc), each element rounded to nearest exactly
-// as the scalar __fsub_rn / __fmaf_rn of dist_step.
-__device__ __forceinline__ void dist_step2(float qa, float qb, float x, float &acc_a,
-                                           float &acc_b) {
-  unsigned long long q2, x2, a2, dif;
-  asm("mov.b64 %0, {%1, %2};" : "=l"(q2) : "f"(qa), "f"(qb));
-  asm("mov.b64 %0, {%1, %1};" : "=l"(x2) : "f"(x));
-  asm("mov.b64 %0, {%1, %2};" : "=l"(a2) : "f"(acc_a), "f"(acc_b));
+// as the scalar __fsub_rn / __fmaf_rn of dist_step.  q2 and acc2 hold the pairs
+// packed (low word: the first query), x2 the row value twice.
+__device__ __forceinline__ void dist_step2(unsigned long long q2, unsigned long long x2,
+                                           unsigned long long &acc2) {
+  unsigned long long dif;
   asm("sub.rn.f32x2 %0, %1, %2;" : "=l"(dif) : "l"(q2), "l"(x2));
-  asm("fma.rn.f32x2 %0, %1, %1, %2;" : "=l"(a2) : "l"(dif), "l"(a2));
-  asm("mov.b64 {%0, %1}, %2;" : "=f"(acc_a), "=f"(acc_b) : "l"(a2));
+  asm("fma.rn.f32x2 %0, %1, %1, %0;" : "+l"(acc2) : "l"(dif));
+}
+__device__ __forceinline__ unsigned long long pack2(float lo, float hi) {
+  unsigned long long r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(lo), "f"(hi));
+  return r;
+}
+__device__ __forceinline__ void unpack2(unsigned long long v, float &lo, float &hi) {
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(lo), "=f"(hi) : "l"(v));
 }
 constexpr int kScanPad = 33;  // transposed chunk row stride (conflict-free)
 
@@ -78,8 +83,11 @@ __global__ void __launch_bounds__(kScanWarps * 32) knn_scan_kernel(
 
   for (int64_t t = rbeg + (int64_t)warp * 32; t < rend; t += kScanWarps * 32) {
     float acc[NQ];
+    unsigned long long acc2[NQ / 2 > 0 ? NQ / 2 : 1];
 #pragma unroll
     for (int i = 0; i < NQ; i++) acc[i] = 0.f;
+#pragma unroll
+    for (int i = 0; i < NQ / 2; i++) acc2[i] = 0ull;  // two +0.0f
     const int64_t my_row = t + lane;
     for (int c0 = 0; c0 < d; c0 += 32) {
       // rows t .. t+31 of dimensions c0 .. c0+31, lane = dimension, all loads in flight
@@ -102,10 +110,16 @@ __global__ void __launch_bounds__(kScanWarps * 32) knn_scan_kernel(
           acc[0] = dist_step(qc[0], xv, acc[0]);
         } else {
           // two queries per packed step (round to nearest per element, as dist_step)
+          const unsigned long long x2 = pack2(xv, xv);
+          const unsigned long long *qc2 = reinterpret_cast<const unsigned long long *>(qc);
 #pragma unroll
-          for (int i = 0; i < NQ; i += 2) dist_step2(qc[i], qc[i + 1], xv, acc[i], acc[i + 1]);
+          for (int i = 0; i < NQ / 2; i++) dist_step2(qc2[i], x2, acc2[i]);
         }
       }
+    }
+    if (NQ > 1) {
+#pragma unroll
+      for (int i = 0; i < NQ / 2; i++) unpack2(acc2[i], acc[2 * i], acc[2 * i + 1]);
     }
     // this lane's row against each query's running k-th (the distances go through
     // shared memory so that the loop over queries is not unrolled)
