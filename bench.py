@@ -6,9 +6,10 @@
     python bench.py --impl reference      # the CPU baseline arm
 
 A step is one exact k-NN search of the whole query batch against the whole
-database: on N GPUs the database is row-sharded, each rank searches its shard,
-one NCCL all-gather moves the per-shard (n, k) lists and the merge kernel
-produces the result on every rank.  `value` is queries/sec of the whole job
+database: on N GPUs the database is row-sharded, each rank searches its shard
+(sharing per-query distance bounds with the other ranks after every filter level,
+one all-reduce of 2n floats), one NCCL all-gather moves the per-shard (n, k)
+lists and the merge kernel produces the result on every rank.  `value` is queries/sec of the whole job
 (the query batch / the max over ranks of the device-timed step).  Inputs are
 synthetic (seeded, the workload's shapes and distributions), resident in HBM
 when timing starts; the database is larger than L2, so no flush is needed.
