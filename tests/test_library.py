@@ -65,3 +65,30 @@ def test_workspace_has_room_for_partials(lib):
     nb = ctypes.c_uint64()
     assert lib.bfk_workspace_size(100, 10_000, 16, 10, ctypes.byref(o), ctypes.byref(nb)) == 0
     assert nb.value >= 8 * 100 * 10 * 8
+
+
+def test_header_is_plain_c_and_links(tmp_path):
+    """include/bfknn.h compiles as C99 and C++11, and a C caller links against the
+    library (the ABI a cgo / ctypes / JNI binding would use)."""
+    import shutil
+    import subprocess
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    inc = os.path.join(root, "include")
+    cc = shutil.which("gcc")
+    if cc is None:
+        pytest.skip("no C compiler")
+    src = tmp_path / "caller.c"
+    src.write_text(
+        '#include "bfknn.h"\n#include <stdio.h>\n'
+        'int main(void) { int32_t a, b; bfk_version(&a, &b);\n'
+        '  uint64_t nb = 0; bfk_opts_t o = {0};\n'
+        '  int s = bfk_workspace_size(10, 1000, 128, 5, &o, &nb);\n'
+        '  printf("%d %d %d %d\\n", a, b, s, nb > 0); return 0; }\n')
+    exe = tmp_path / "caller"
+    libdir = os.path.join(root, "gpu_algo_b200")
+    subprocess.run([cc, "-std=c99", "-Wall", "-Werror", "-I", inc, str(src), "-o", str(exe),
+                    "-L", libdir, "-lbfknn", f"-Wl,-rpath,{libdir}"], check=True)
+    subprocess.run(["g++", "-std=c++11", "-fsyntax-only", "-x", "c++",
+                    os.path.join(inc, "bfknn.h")], check=True)
+    out = subprocess.run([str(exe)], check=True, capture_output=True, text=True).stdout.split()
+    assert out[2] == "0" and out[3] == "1"
