@@ -92,3 +92,21 @@ def test_header_is_plain_c_and_links(tmp_path):
                     os.path.join(inc, "bfknn.h")], check=True)
     out = subprocess.run([str(exe)], check=True, capture_output=True, text=True).stdout.split()
     assert out[2] == "0" and out[3] == "1"
+
+
+def test_prepared_sizes_without_gpu(lib):
+    """A prepared search's workspace holds no rows; a prepared buffer holds them plus a
+    512-byte header, all parts 256-byte aligned."""
+    m, d = 40_000, 128
+    plain = _lib.make_opts("tc_f16")
+    prep = _lib.make_opts("tc_f16", flags=_lib.FLAG_PREPARED)
+    full, small, pb = ctypes.c_uint64(), ctypes.c_uint64(), ctypes.c_uint64()
+    assert lib.bfk_workspace_size(64, m, d, 10, ctypes.byref(plain), ctypes.byref(full)) == 0
+    assert lib.bfk_workspace_size(64, m, d, 10, ctypes.byref(prep), ctypes.byref(small)) == 0
+    assert full.value - small.value >= m * d * 2
+    assert lib.bfk_prepared_size(m, d, ctypes.byref(pb)) == 0
+    assert pb.value % 256 == 0 and pb.value >= 512 + m * d * 2 + m * 4
+    assert lib.bfk_prepared_size(m, 0, ctypes.byref(pb)) == 1
+    # a prepared search needs the flag and the buffer together
+    assert lib.bfk_search_prepared(None, 4, None, None, m, d, 10, 0, None, None, None, 0,
+                                   ctypes.byref(prep), None) == 1
