@@ -91,8 +91,11 @@ bool opts_ok(const bfk_opts_t *o) {
 int choose_engine(int64_t n, int64_t m, int d, int k, const bfk_opts_t *o) {
   const int req = o ? o->engine : BFK_ENGINE_AUTO;
   if (req != BFK_ENGINE_AUTO) return req;
+  // Shards of one search (plan_rows set) decide on the largest shard's rows, so that
+  // every shard picks the same engine and makes the same level-hook calls.
+  const int64_t rows = (o && o->plan_rows > m) ? o->plan_rows : m;
   // the filter engine needs whole 128-query tiles' worth of work to pay off
-  if (tc_supported(d, k) && n >= 64 && m >= 4096) return BFK_ENGINE_TC_F16;
+  if (tc_supported(d, k) && n >= 64 && rows >= 4096) return BFK_ENGINE_TC_F16;
   return BFK_ENGINE_DIRECT;
 }
 

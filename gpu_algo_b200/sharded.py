@@ -53,6 +53,9 @@ def make_local_search(group=None, plan_rows: int = 0, **search_kwargs) -> Callab
         dist.all_reduce(t, op=dist.ReduceOp.MIN, group=group)
 
     def local_search(Q_, X_, k_, id_offset):
+        if world > 1 and X_.shape[0] == 0:
+            # the other shards would wait in the bound all-reduce for this one
+            raise ValueError("every shard of a sharded search needs at least one row")
         if world > 1 and state["plan_rows"] <= 0:
             sizes = torch.tensor([X_.shape[0]], dtype=torch.int64, device=X_.device)
             dist.all_reduce(sizes, op=dist.ReduceOp.MAX, group=group)

@@ -110,3 +110,19 @@ def test_prepared_sizes_without_gpu(lib):
     # a prepared search needs the flag and the buffer together
     assert lib.bfk_search_prepared(None, 4, None, None, m, d, 10, 0, None, None, None, 0,
                                    ctypes.byref(prep), None) == 1
+
+
+def test_shards_pick_one_engine(lib):
+    """A shard just under the filter engine's row threshold still takes the engine
+    its larger sibling shards take (plan_rows), so all make the same hook calls."""
+    nb_auto, nb_tc, nb_alone = ctypes.c_uint64(), ctypes.c_uint64(), ctypes.c_uint64()
+    o = _lib.make_opts()
+    o.plan_rows = 4096
+    assert lib.bfk_workspace_size(64, 4095, 128, 10, ctypes.byref(o), ctypes.byref(nb_auto)) == 0
+    t = _lib.make_opts("tc_f16")
+    t.plan_rows = 4096
+    assert lib.bfk_workspace_size(64, 4095, 128, 10, ctypes.byref(t), ctypes.byref(nb_tc)) == 0
+    assert nb_auto.value == nb_tc.value
+    alone = _lib.make_opts()
+    assert lib.bfk_workspace_size(64, 4095, 128, 10, ctypes.byref(alone), ctypes.byref(nb_alone)) == 0
+    assert nb_alone.value != nb_tc.value  # on its own, the SIMT engine
