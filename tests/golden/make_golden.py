@@ -74,7 +74,7 @@ def main() -> int:
     np.savez_compressed(os.path.join(HERE, "plumbing_k10.npz"), dists=d_, ids=i_)
     shas = {"plumbing.X": data.sha256(X), "plumbing.Q": data.sha256(Q)}
     # small prefixes of the large workloads, to pin the generators
-    for name in ("mixture-k-sweep", "unit-10m", "highdim-960", "stream-100m"):
+    for name in ("mixture-k-sweep", "unit-10m", "highdim-960", "stream-100m", "published-d8"):
         Xs, Qs = data.workload_arrays(name, n_rows=2048, n_queries=64)
         shas[f"{name}.X[:2048]"] = data.sha256(Xs)
         shas[f"{name}.Q[:64]"] = data.sha256(Qs)

@@ -63,7 +63,7 @@ def test_inputs_match_pinned_hashes():
     X, Q = data.workload_arrays("plumbing")
     assert data.sha256(X) == shas["plumbing.X"]
     assert data.sha256(Q) == shas["plumbing.Q"]
-    for name in ("mixture-k-sweep", "unit-10m", "highdim-960", "stream-100m"):
+    for name in ("mixture-k-sweep", "unit-10m", "highdim-960", "stream-100m", "published-d8"):
         Xs, Qs = data.workload_arrays(name, n_rows=2048, n_queries=64)
         assert data.sha256(Xs) == shas[f"{name}.X[:2048]"]
         assert data.sha256(Qs) == shas[f"{name}.Q[:64]"]
