@@ -216,6 +216,27 @@ def test_errors_are_raised():
         engine.search(Q, torch.zeros((16, 9), device="cuda"), 3)
 
 
+def test_main_kernel_timing_after_rejected_and_padding_calls(plumbing):
+    """A timed call that is rejected before its kernels run leaves no unrecorded event
+    pair behind, and a timed call with no rows times its padding fill. Reading an
+    unrecorded pair would fail and leave that error for the next launch check."""
+    X, Q, gd, gi = plumbing
+    Qd, Xd = dev(Q[:64]), dev(X)
+    engine.last_stats(Qd, Xd, 10, engine="tc_f16")  # drain earlier timed calls
+    other = engine.PreparedRows.prepare(Xd[:30_000])
+    forged = engine.PreparedRows(other.buffer, tuple(Xd.shape))
+    with pytest.raises(_lib.BfkError) as e:
+        engine.search(Qd, Xd, 10, engine="tc_f16", prepared=forged, time_main=True)
+    assert e.value.status == 1
+    d_, i_ = engine.search(Qd, Xd[:0], 10, time_main=True)
+    assert (i_ == -1).all()
+    engine.search(Qd, Xd, 10, engine="tc_f16", time_main=True)
+    st = engine.last_stats(Qd, Xd, 10, engine="tc_f16")
+    assert st["timed_calls"] == 2 and st["main_kernel_ms"] > 0
+    d_, i_ = run(Q[:64], X, 10, engine="direct")
+    assert_exact(d_, i_, gd[:64], gi[:64], "after timed calls")
+
+
 def test_bf_dropin_runners(plumbing):
     from gpu_algo_b200.bf import fp32, fp32_heap, fp32_q2, fp32_qgroup, fp32_tiled
     X, Q, gd, gi = plumbing
