@@ -40,26 +40,33 @@ def make_local_search(group=None, plan_rows: int = 0, **search_kwargs) -> Callab
     """The per-shard search of `sharded_search` with the CUDA engine.
 
     Every rank must use the same `plan_rows` (the largest shard's row count);
-    0 looks it up with an all-reduce on the first call.  With more than one
-    rank, the engine's level hook all-reduces (MIN) each query's bounds over
-    `group` after every filter level; `search_kwargs` go to `engine.search`.
+    0 looks it up with an all-reduce on the first call, which also finds the
+    smallest shard, so that every rank raises if one shard is empty.  With more
+    than one rank, the engine's level hook all-reduces (MIN) each query's bounds
+    over `group` after every filter level; `search_kwargs` go to `engine.search`.
     """
     from .engine import search
     world = dist.get_world_size(group) if dist.is_initialized() else 1
     state = {"plan_rows": int(plan_rows)}
+    empty = "every shard of a sharded search needs at least one row"
 
     def share_bounds(t):
         # both halves of `t` are minimised: see bfk_level_hook_t
         dist.all_reduce(t, op=dist.ReduceOp.MIN, group=group)
 
     def local_search(Q_, X_, k_, id_offset):
-        if world > 1 and X_.shape[0] == 0:
-            # the other shards would wait in the bound all-reduce for this one
-            raise ValueError("every shard of a sharded search needs at least one row")
         if world > 1 and state["plan_rows"] <= 0:
-            sizes = torch.tensor([X_.shape[0]], dtype=torch.int64, device=X_.device)
+            # (largest rows, -smallest rows) over the shards
+            sizes = torch.tensor([X_.shape[0], -X_.shape[0]], dtype=torch.int64, device=X_.device)
             dist.all_reduce(sizes, op=dist.ReduceOp.MAX, group=group)
-            state["plan_rows"] = int(sizes.item())
+            largest, neg_smallest = (int(v) for v in sizes.tolist())
+            if neg_smallest == 0:
+                raise ValueError(empty)
+            state["plan_rows"] = largest
+        if world > 1 and X_.shape[0] == 0:
+            # with `plan_rows` given there is no size exchange: the other shards learn
+            # of this one when their bound all-reduce runs out of time
+            raise ValueError(empty)
         return search(Q_, X_, k_, id_offset=id_offset,
                       bound_hook=share_bounds if world > 1 else None,
                       plan_rows=state["plan_rows"] if world > 1 else 0,

@@ -1,9 +1,11 @@
-"""The row-sharded multi-GPU orchestration, run as 2 gloo ranks on CPU.
+"""The row-sharded multi-GPU orchestration, run as 2 or 3 gloo ranks on CPU.
 
 The per-shard search and the merge are CPU stand-ins from the oracle; what is
 under test is the host logic of gpu_algo_b200.sharded: shard ranges, the
-global row offsets, the all-gather layout and the merge call.
+global row offsets, the all-gather layout, the merge call, and the size
+exchange that rejects an empty shard on every rank.
 """
+import datetime
 import os
 import socket
 
@@ -67,6 +69,39 @@ def test_sharded_search_matches_single_shard(tmp_path, world):
         spans.append((int(z["r0"]), int(z["r1"])))
     assert spans[0][0] == 0 and spans[-1][1] == 20_011
     assert all(a[1] == b[0] for a, b in zip(spans, spans[1:]))
+
+
+def _empty_shard_main(rank, world, port, outdir):
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    # a rank left waiting in the size exchange ends with an error, not a hang
+    dist.init_process_group("gloo", rank=rank, world_size=world,
+                            timeout=datetime.timedelta(seconds=60))
+    try:
+        from gpu_algo_b200.sharded import make_local_search
+        rows = 0 if rank == world - 1 else 5000
+        X = torch.zeros((rows, 16), dtype=torch.float32)
+        Q = torch.zeros((3, 16), dtype=torch.float32)
+        local = make_local_search()  # plan_rows looked up from the shards
+        try:
+            local(Q, X, 4, 0)
+            outcome = "searched"
+        except ValueError as e:
+            outcome = str(e)
+        with open(os.path.join(outdir, f"r{rank}.txt"), "w") as f:
+            f.write(outcome)
+    finally:
+        dist.destroy_process_group()
+
+
+def test_empty_shard_is_rejected_on_every_rank(tmp_path):
+    """The size exchange that finds the largest shard finds the smallest too, so every
+    rank raises before any search (and its bound all-reduces) starts."""
+    world = 3
+    mp.start_processes(_empty_shard_main, args=(world, _free_port(), str(tmp_path)),
+                       nprocs=world, join=True, start_method="spawn")
+    for r in range(world):
+        assert "at least one row" in (tmp_path / f"r{r}.txt").read_text()
 
 
 def test_shard_range_balanced():
