@@ -4,8 +4,11 @@
  * Drop-in boundary for the reference's `bf/` kernels (hantaoyu-theory/gpu_algo).
  * Every entry point takes plain pointers and sizes; device pointers are
  * caller-owned CUDA device memory, `stream` is a cudaStream_t (NULL = the
- * legacy default stream).  Launches are asynchronous on that stream; no entry
- * point allocates device memory, calls exit(), or throws.  Results:
+ * legacy default stream).  Launches go on that stream; the SIMT engine and
+ * bfk_merge return without waiting for them, while a search on the tensor-core
+ * engine waits for its stream before it returns (it reads back how many queries
+ * need the exact fallback).  No entry point allocates device memory, calls
+ * exit(), or throws.  Results:
  *   out_dists (n, k) float32  squared L2 distances, ascending;
  *   out_ids   (n, k) int32    id_offset + database row, ties by lower index;
  *   missing slots (m < k, or rows whose distance is NaN) are padded with
