@@ -1,0 +1,38 @@
+"""bench.py's reference arm on CPU: one JSON line with the keys the driver reads, on
+rank 0 only; the other ranks exit 0 without work."""
+import json
+import os
+import subprocess
+import sys
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+ARGS = [sys.executable, os.path.join(ROOT, "bench.py"), "--impl", "reference",
+        "--workload", "plumbing", "--steps", "2", "--warmup", "1", "--cpu-sample", "8"]
+
+
+def _run(rank: str):
+    env = dict(os.environ, RANK=rank)
+    return subprocess.run(ARGS, env=env, capture_output=True, text=True, timeout=600)
+
+
+def test_reference_arm_prints_one_contract_line():
+    p = _run("0")
+    assert p.returncode == 0, p.stderr[-2000:]
+    lines = [ln for ln in p.stdout.splitlines() if ln.strip()]
+    assert len(lines) == 1
+    j = json.loads(lines[0])
+    assert j["impl"] == "reference"
+    assert j["metric"] == "queries/sec, exact FP32 k-NN" and j["unit"] == "queries/s"
+    assert j["value"] > 0 and j["ms_per_step"] > 0 and j["higher_is_better"] is True
+    assert (j["steps"], j["warmup"], j["n_gpus"]) == (2, 1, 1)
+    assert j["config"] == {"workload": "plumbing", "N": 65_536, "Q": 1_024, "d": 128, "k": 10}
+    cb = j["cpu_baseline"]
+    assert cb["kind"] == "port" and cb["cores"] >= 1 and cb["value"] == j["value"]
+    assert "8 queries" in cb["sample"]
+    assert j["e2e"] == {"value": j["value"], "unit": "queries/s", "h2d_bytes_per_step": 0,
+                        "d2h_bytes_per_step": 0}
+
+
+def test_reference_arm_other_ranks_do_no_work():
+    p = _run("1")
+    assert p.returncode == 0 and p.stdout.strip() == ""
