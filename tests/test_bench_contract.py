@@ -4,6 +4,7 @@ import json
 import os
 import subprocess
 import sys
+import time
 
 ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
 ARGS = [sys.executable, os.path.join(ROOT, "bench.py"), "--impl", "reference",
@@ -36,3 +37,23 @@ def test_reference_arm_prints_one_contract_line():
 def test_reference_arm_other_ranks_do_no_work():
     p = _run("1")
     assert p.returncode == 0 and p.stdout.strip() == ""
+
+
+def test_clock_sampler_reads_clocks_and_active_reasons(tmp_path, monkeypatch):
+    """The clock record comes from `nvidia-smi --query-gpu ... -lms`; a stand-in script
+    prints three samples, one with sw_power_cap active."""
+    fake = tmp_path / "nvidia-smi"
+    fake.write_text(
+        "#!/bin/sh\n"
+        "echo '0, 1800, 1965, 700.5, 0x4, Not Active, Not Active, Not Active, Active'\n"
+        "echo '0, 1900, 1965, 710.0, 0x0, Not Active, Not Active, Not Active, Not Active'\n"
+        "echo '0, 1850, 1965, 705.0, 0x0, Not Active, Not Active, Not Active, Not Active'\n"
+        "exec sleep 30\n")
+    fake.chmod(0o755)
+    monkeypatch.setenv("PATH", f"{tmp_path}{os.pathsep}{os.environ['PATH']}")
+    import bench  # the repository root is on sys.path (conftest)
+    s = bench.ClockSampler(0)
+    s.start()
+    time.sleep(0.5)
+    assert s.stop() == {"sm_mhz": 1850.0, "sm_max_mhz": 1965.0, "reasons": ["sw_power_cap"],
+                        "samples": 3}
