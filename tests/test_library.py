@@ -126,3 +126,35 @@ def test_shards_pick_one_engine(lib):
     alone = _lib.make_opts()
     assert lib.bfk_workspace_size(64, 4095, 128, 10, ctypes.byref(alone), ctypes.byref(nb_alone)) == 0
     assert nb_alone.value != nb_tc.value  # on its own, the SIMT engine
+
+
+def test_struct_layouts_match_the_header(tmp_path):
+    """The ctypes mirrors of bfk_opts_t, bfk_attrs_t and bfk_stats_t have the C
+    header's size and field offsets (a shifted field would pass options wrongly)."""
+    import shutil
+    import subprocess
+    cc = shutil.which("gcc")
+    if cc is None:
+        pytest.skip("no C compiler")
+    mirrors = {"bfk_opts_t": _lib.Opts, "bfk_attrs_t": _lib.Attrs, "bfk_stats_t": _lib.Stats}
+    lines = ['#include "bfknn.h"', "#include <stddef.h>", "#include <stdio.h>",
+             "int main(void) {"]
+    for cname, py in mirrors.items():
+        lines.append(f'  printf("{cname} sizeof %zu\\n", sizeof({cname}));')
+        for fname, _ in py._fields_:
+            lines.append(f'  printf("{cname} {fname} %zu\\n", offsetof({cname}, {fname}));')
+    lines += ["  return 0;", "}"]
+    src = tmp_path / "layout.c"
+    src.write_text("\n".join(lines) + "\n")
+    exe = tmp_path / "layout"
+    subprocess.run([cc, "-std=c99", "-Wall", "-Werror", "-I", os.path.join(ROOT, "include"),
+                    str(src), "-o", str(exe)], check=True)
+    got = {}
+    for ln in subprocess.run([str(exe)], check=True, capture_output=True,
+                             text=True).stdout.splitlines():
+        cname, field, value = ln.split()
+        got[(cname, field)] = int(value)
+    for cname, py in mirrors.items():
+        assert got[(cname, "sizeof")] == ctypes.sizeof(py), cname
+        for fname, _ in py._fields_:
+            assert got[(cname, fname)] == getattr(py, fname).offset, f"{cname}.{fname}"
