@@ -25,7 +25,9 @@
 //   (dif = q - x; acc = fma(dif, dif, acc), bf/fp32.py:80) and the k best by
 //   (distance, index) are written, so output distances are bit-identical to
 //   the reference kernels'.  A query whose final candidate region overflowed
-//   (degenerate data) is finished by the exact SIMT engine.
+//   (degenerate data) is finished by the exact SIMT engine, and so is every
+//   query when the inputs hold a non-finite norm or norms too small for the
+//   margin (qn + Rx < 2^-48, see tc_prep_q_kernel).
 #include <cuda.h>
 #include <cudaTypedefs.h>
 
@@ -570,7 +572,7 @@ __global__ void __launch_bounds__(256) tc_prep_x_kernel(const float *__restrict_
     if (lane == u) xnorm[row] = row < m ? ss[u] : INFINITY;
   }
   if (lane == 0) { s_max[warp] = wmax; s_rn[warp] = wrn; }
-  if (bad && lane == 0) atomicOr(&hdr->nonfinite, 1);
+  if (bad && lane == 0) atomicOr(&hdr->exact_only, 1);
   __syncthreads();
   float gmax = 0.f, rn = 0.f;
 #pragma unroll
@@ -613,7 +615,7 @@ __global__ void __launch_bounds__(256) tc_prep_x_kernel(const float *__restrict_
 __global__ void tc_take_row_status(const WsHeader *src, WsHeader *dst) {
   if (threadIdx.x == 0) {
     dst->rx_bits = src->rx_bits;
-    dst->nonfinite = src->nonfinite;
+    dst->exact_only = src->exact_only;
   }
 }
 
@@ -671,7 +673,7 @@ __global__ void __launch_bounds__(256) tc_prep_x_wide_kernel(const float *__rest
     if (lane == 0) xnorm[row] = row < m ? ss : INFINITY;
   }
   if (lane == 0) { s_max[warp] = wmax; s_rn[warp] = wrn; }
-  if (bad && lane == 0) atomicOr(&hdr->nonfinite, 1);
+  if (bad && lane == 0) atomicOr(&hdr->exact_only, 1);
   __syncthreads();
   float gmax = 0.f, rn = 0.f;
 #pragma unroll
@@ -722,7 +724,7 @@ __global__ void tc_qmax_kernel(const float *__restrict__ Q, int64_t count, WsHea
   for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
   if ((threadIdx.x & 31) == 0 && mx > 0.f) {
     if (isfinite(mx)) atomicMax(&hdr->qmax_bits, __float_as_uint(mx));
-    else atomicOr(&hdr->nonfinite, 1);
+    else atomicOr(&hdr->exact_only, 1);
   }
 }
 
@@ -756,7 +758,7 @@ __global__ void __launch_bounds__(256) tc_prep_q_kernel(const float *__restrict_
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
   if (lane == 0) {
-    if (!isfinite(ss)) atomicOr(&hdr->nonfinite, 1);
+    if (!isfinite(ss)) atomicOr(&hdr->exact_only, 1);
     // Error margin.  With u = 2^-11 the f16 unit roundoff, qn >= ||q||, Rx >= max ||x||:
     //   e_q = u qn + sqrt(d) 2^-25 / s_q        (f16 rounding of q, incl. subnormals)
     //   e_x = (u + sqrt(d) 2^-38) Rx             (row groups scaled to [2^13, 2^14))
@@ -777,6 +779,11 @@ __global__ void __launch_bounds__(256) tc_prep_q_kernel(const float *__restrict_
     const double acc = (double)(d_pad + 16) * ldexp(1.0, -22) * (qn + eq) * (rx + ex);
     const double f32 = 2.0 * (double)(d + 8) * ldexp(1.0, -24) * (qn + rx) * (qn + rx);
     const double margin = 2.0 * (dotr + acc) + f32;
+    // The bound needs qn + Rx >= 2^-48.  Below it the epilogue's factor -2/(s_q s_x)
+    // can underflow to zero (s_q s_x > 2^150) and FP32 rounding stops being relative
+    // (subnormals), so |(||q||^2 + v) - D| can exceed the margin.  Such data (every norm
+    // under about 3.6e-15) is searched by the exact SIMT engine instead.
+    if (qn + rx < ldexp(1.0, -48)) atomicOr(&hdr->exact_only, 1);
     qinfo[row] = make_float2(ss, __double2float_ru(margin * (1.0 + 1e-6)));
   }
 }
@@ -1234,8 +1241,8 @@ __global__ void __launch_bounds__(kSelThreads) tc_final_select_kernel(const SelA
   const int64_t q = blockIdx.x;
   const QueryRegions R = load_regions(a.cand, a.ccount, q, a.pool, a.region, a.nreg, a.stride,
                                       s_cnt, s_off, s_misc);
-  // a region that lost entries, or non-finite inputs (the margin needs finite norms)
-  if (R.over || a.hdr->nonfinite) {
+  // a region that lost entries, or inputs the margin does not cover (exact_only)
+  if (R.over || a.hdr->exact_only) {
     if (threadIdx.x == 0) {
       const int slot = atomicAdd(&a.hdr->fallback, 1);
       a.fb_list[slot] = (int)q;
@@ -1389,8 +1396,8 @@ __global__ void __launch_bounds__(kWarpFinalQueries * 32) tc_final_select_warp_k
     run += loc[j];
   }
   const int total = __shfl_sync(0xffffffffu, incl, 31);
-  // a region that lost entries, or non-finite inputs (the margin needs finite norms)
-  if (__any_sync(0xffffffffu, over) || a.hdr->nonfinite) {
+  // a region that lost entries, or inputs the margin does not cover (exact_only)
+  if (__any_sync(0xffffffffu, over) || a.hdr->exact_only) {
     if (lane == 0) {
       const int slot = atomicAdd(&a.hdr->fallback, 1);
       a.fb_list[slot] = (int)q;

@@ -98,6 +98,22 @@ def test_tc_nonfinite_rows_use_exact_engine():
     assert_exact(d_, i_, ed, ei, "nonfinite")
 
 
+@pytest.mark.parametrize("scale,exact_only", [(1e-20, True), (1e-13, False)])
+def test_tc_norms_below_the_margin_guard_use_exact_engine(scale, exact_only):
+    """Below ||q|| + max ||x|| = 2^-48 the filter's margin does not hold (its scale factor
+    underflows, FP32 rounding goes subnormal): every query then goes to the exact
+    engine.  Just above it the filter runs as usual.  Both stay bit-exact."""
+    rng = np.random.Generator(np.random.PCG64(8))
+    X = (rng.standard_normal((9000, 64)) * scale).astype(np.float32)
+    Q = (rng.standard_normal((130, 64)) * scale).astype(np.float32)
+    ed, ei = oracle_knn(Q, X, 16)
+    Qd, Xd = dev(Q), dev(X)
+    d_, i_ = engine.search(Qd, Xd, 16, engine="tc_f16")
+    st = engine.last_stats(Qd, Xd, 16, engine="tc_f16")
+    assert st["fallback_queries"] == (130 if exact_only else 0)
+    assert_exact(d_.cpu().numpy(), i_.cpu().numpy(), ed, ei, f"scale {scale}")
+
+
 @pytest.mark.parametrize("name,n,m,k", [("mixture-k-sweep", 300, 200_000, 32),
                                         ("mixture-k-sweep", 257, 120_000, 100),
                                         ("unit-10m", 256, 300_000, 100),

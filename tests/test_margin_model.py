@@ -1,0 +1,110 @@
+"""The tensor-core filter's error margin, checked on CPU against the oracle's reference
+distances (no GPU).
+
+The filter value of row j for query q is v = fma(c, acc, ||x_j||^2) in FP32, where acc
+is the dot product of the f16 forms of q and x_j (q scaled by one power of two per
+batch, rows by one per 64-row group, each max |value| into [2^13, 2^14)) and
+c = -2 / (s_q s_x).  tc_prep_q_kernel bounds |(||q||^2 + v) - D_j| by a per-query
+margin, D_j being the reference kernel's FP32 distance.  This restates that arithmetic
+in NumPy (the tensor core modelled as an exact sum rounded once to FP32; the margin's
+accumulation term covers the rest) and checks:
+* the bound holds, with room, from data scales of 1e6 down to norms near 2^-48;
+* below that it fails (c underflows to zero, FP32 rounding goes subnormal), which is
+  why queries with ||q|| + max ||x|| < 2^-48 go to the exact SIMT engine.
+"""
+import math
+
+import numpy as np
+import pytest
+
+from oracle import oracle_all_dists
+
+GUARD = 2.0 ** -48  # tc_prep_q_kernel: qn + Rx below this -> exact SIMT engine
+GROUP_ROWS = 64
+
+
+def _pow2_scale_for(maxabs) -> np.float32:
+    """2^p with maxabs * 2^p in [2^13, 2^14), p clamped to [-126, 126]."""
+    mx = float(maxabs)
+    if not mx > 0 or not math.isfinite(mx):
+        return np.float32(1.0)
+    _, e = math.frexp(mx)
+    return np.float32(2.0 ** min(126, max(-126, 14 - e)))
+
+
+def _f32_round_up(x: float) -> np.float32:
+    y = np.float32(x)
+    return np.nextafter(y, np.float32(np.inf)) if float(y) < x else y
+
+
+def filter_model(Q: np.ndarray, X: np.ndarray):
+    """(|(||q||^2 + v) - D| / margin, max over rows, per query; qn + Rx per query)."""
+    n, d = Q.shape
+    d_pad = -(-d // 64) * 64
+    sq = _pow2_scale_for(np.abs(Q).max())
+    qh = (Q * sq).astype(np.float16)
+    ssq = np.einsum("ij,ij->i", Q, Q, dtype=np.float32)
+    ssx = np.einsum("ij,ij->i", X, X, dtype=np.float32)
+    rx = float(np.max(np.sqrt(ssx) * np.float32(1.0 + 2.0 ** -10)))
+    xh = np.empty(X.shape, dtype=np.float16)
+    xinv = np.empty(X.shape[0], dtype=np.float32)
+    for g in range(0, X.shape[0], GROUP_ROWS):
+        sc = _pow2_scale_for(np.abs(X[g:g + GROUP_ROWS]).max())
+        xh[g:g + GROUP_ROWS] = (X[g:g + GROUP_ROWS] * sc).astype(np.float16)
+        xinv[g:g + GROUP_ROWS] = np.float32(1.0) / sc
+    acc = (qh.astype(np.float64) @ xh.astype(np.float64).T).astype(np.float32)
+    c = (np.float32(-2.0) * (np.float32(1.0) / sq)) * xinv  # FP32, may underflow to 0
+    v = (c.astype(np.float64)[None, :] * acc.astype(np.float64)
+         + ssx.astype(np.float64)[None, :]).astype(np.float32)
+    # the margin, as tc_prep_q_kernel forms it
+    u = 2.0 ** -11
+    qn = np.sqrt(ssq.astype(np.float64)) * (1.0 + 2.0 ** -10)
+    sd = math.sqrt(d)
+    eq = u * qn + sd * 2.0 ** -25 / float(sq)
+    ex = (u + sd * 2.0 ** -38) * rx
+    dotr = eq * rx + qn * ex + eq * ex
+    accr = (d_pad + 16) * 2.0 ** -22 * (qn + eq) * (rx + ex)
+    f32t = 2.0 * (d + 8) * 2.0 ** -24 * (qn + rx) ** 2
+    margin = np.array([_f32_round_up(t * (1 + 1e-6)) for t in 2.0 * (dotr + accr) + f32t],
+                      dtype=np.float64)
+    nq = (Q.astype(np.float64) ** 2).sum(1)  # any value common to a query's rows works
+    err = np.abs(nq[:, None] + v.astype(np.float64) - oracle_all_dists(Q, X).astype(np.float64))
+    with np.errstate(divide="ignore", invalid="ignore"):
+        ratio = np.where(err == 0, 0.0, err / margin[:, None]).max(axis=1)
+    return ratio, qn + rx
+
+
+def _data(seed, n, m, d, q_scale, x_scale):
+    rng = np.random.Generator(np.random.PCG64(seed))
+    return ((rng.standard_normal((n, d)) * q_scale).astype(np.float32),
+            (rng.standard_normal((m, d)) * x_scale).astype(np.float32))
+
+
+@pytest.mark.parametrize("q_scale,x_scale", [(1.0, 1.0), (1e6, 1e6), (1e-6, 1e-6),
+                                             (1e-13, 1e-13), (1e-15, 1e-15),
+                                             (1.0, 1e-30), (1e-30, 1.0), (1e-20, 1e-10)])
+@pytest.mark.parametrize("d", [8, 128, 300])
+def test_margin_bounds_the_filter_error(q_scale, x_scale, d):
+    Q, X = _data(d, 24, 640, d, q_scale, x_scale)
+    ratio, norms = filter_model(Q, X)
+    assert (norms >= GUARD).all()
+    assert ratio.max() <= 0.5, ratio.max()
+
+
+def test_rows_of_mixed_scale_in_one_group():
+    """Small rows share their group's scale with a large one: their f16 values lose
+    precision (down to subnormals), which the margin's Rx terms cover."""
+    Q, X = _data(3, 24, 640, 64, 1.0, 1.0)
+    X[::64] *= 1e4
+    X[1::64] *= 1e-8
+    ratio, _ = filter_model(Q, X)
+    assert ratio.max() <= 0.5, ratio.max()
+
+
+@pytest.mark.parametrize("scale", [1e-20, 1e-22])
+def test_margin_fails_below_the_guard(scale):
+    """Below the guard the bound does not hold, so those inputs must not be filtered."""
+    Q, X = _data(5, 24, 640, 64, scale, scale)
+    ratio, norms = filter_model(Q, X)
+    assert (norms < GUARD).all()
+    assert ratio.max() > 1.0
