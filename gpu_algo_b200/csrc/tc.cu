@@ -27,7 +27,8 @@
 //   the reference kernels'.  A query whose final candidate region overflowed
 //   (degenerate data) is finished by the exact SIMT engine, and so is every
 //   query when the inputs hold a non-finite norm or norms too small for the
-//   margin (qn + Rx < 2^-48, see tc_prep_q_kernel).
+//   margin or too large for FP32 (qn + Rx outside [2^-48, 2^63), see
+//   tc_prep_q_kernel).
 #include <cuda.h>
 #include <cudaTypedefs.h>
 
@@ -779,11 +780,16 @@ __global__ void __launch_bounds__(256) tc_prep_q_kernel(const float *__restrict_
     const double acc = (double)(d_pad + 16) * ldexp(1.0, -22) * (qn + eq) * (rx + ex);
     const double f32 = 2.0 * (double)(d + 8) * ldexp(1.0, -24) * (qn + rx) * (qn + rx);
     const double margin = 2.0 * (dotr + acc) + f32;
-    // The bound needs qn + Rx >= 2^-48.  Below it the epilogue's factor -2/(s_q s_x)
-    // can underflow to zero (s_q s_x > 2^150) and FP32 rounding stops being relative
-    // (subnormals), so |(||q||^2 + v) - D| can exceed the margin.  Such data (every norm
-    // under about 3.6e-15) is searched by the exact SIMT engine instead.
-    if (qn + rx < ldexp(1.0, -48)) atomicOr(&hdr->exact_only, 1);
+    // The filter needs 2^-48 <= qn + Rx < 2^63, and such data goes to the exact SIMT
+    // engine:
+    // * below it, the epilogue's factor -2/(s_q s_x) can underflow to zero
+    //   (s_q s_x > 2^150) and FP32 rounding stops being relative (subnormals), so
+    //   |(||q||^2 + v) - D| can exceed the margin (every norm under about 3.6e-15);
+    // * from 2^63 on, (||q|| + ||x||)^2 >= 2^126 and a distance or v can overflow to
+    //   +inf.  A row with v = +inf is never a candidate, but an infinite distance is
+    //   still returned when fewer than k rows have a finite one.
+    if (!(qn + rx >= ldexp(1.0, -48) && qn + rx < ldexp(1.0, 63)))
+      atomicOr(&hdr->exact_only, 1);
     qinfo[row] = make_float2(ss, __double2float_ru(margin * (1.0 + 1e-6)));
   }
 }

@@ -98,20 +98,31 @@ def test_tc_nonfinite_rows_use_exact_engine():
     assert_exact(d_, i_, ed, ei, "nonfinite")
 
 
-@pytest.mark.parametrize("scale,exact_only", [(1e-20, True), (1e-13, False)])
-def test_tc_norms_below_the_margin_guard_use_exact_engine(scale, exact_only):
-    """Below ||q|| + max ||x|| = 2^-48 the filter's margin does not hold (its scale factor
-    underflows, FP32 rounding goes subnormal): every query then goes to the exact
-    engine.  Just above it the filter runs as usual.  Both stay bit-exact."""
+@pytest.mark.parametrize("case", ["tiny", "small", "huge"])
+def test_tc_norms_outside_the_margin_guard_use_exact_engine(case):
+    """Outside 2^-48 <= ||q|| + max ||x|| < 2^63 the filter cannot be trusted: below,
+    its margin does not hold (the scale factor underflows, FP32 rounding goes
+    subnormal); above, v and distances overflow to +inf, and rows at +inf are still
+    returned when fewer than k rows are finite.  Every query then goes to the exact
+    engine.  Inside the range ("small") the filter runs as usual.  All stay bit-exact."""
     rng = np.random.Generator(np.random.PCG64(8))
-    X = (rng.standard_normal((9000, 64)) * scale).astype(np.float32)
-    Q = (rng.standard_normal((130, 64)) * scale).astype(np.float32)
-    ed, ei = oracle_knn(Q, X, 16)
+    m, n, k = (300, 130, 300) if case == "huge" else (9000, 130, 16)
+    X = rng.standard_normal((m, 64)).astype(np.float32)
+    Q = rng.standard_normal((n, 64)).astype(np.float32)
+    if case == "huge":  # norms 1.2e19: finite squared norms, infinite distances
+        X = (X / np.linalg.norm(X, axis=1, keepdims=True) * np.float32(1.2e19)).astype(np.float32)
+        Q = (Q / np.linalg.norm(Q, axis=1, keepdims=True) * np.float32(1.2e19)).astype(np.float32)
+    else:
+        scale = np.float32(1e-20 if case == "tiny" else 1e-13)
+        X, Q = X * scale, Q * scale
+    ed, ei = oracle_knn(Q, X, k)
+    if case == "huge":
+        assert np.isinf(ed).any() and (ei >= 0).all()
     Qd, Xd = dev(Q), dev(X)
-    d_, i_ = engine.search(Qd, Xd, 16, engine="tc_f16")
-    st = engine.last_stats(Qd, Xd, 16, engine="tc_f16")
-    assert st["fallback_queries"] == (130 if exact_only else 0)
-    assert_exact(d_.cpu().numpy(), i_.cpu().numpy(), ed, ei, f"scale {scale}")
+    d_, i_ = engine.search(Qd, Xd, k, engine="tc_f16")
+    st = engine.last_stats(Qd, Xd, k, engine="tc_f16")
+    assert st["fallback_queries"] == (0 if case == "small" else n)
+    assert_exact(d_.cpu().numpy(), i_.cpu().numpy(), ed, ei, case)
 
 
 @pytest.mark.parametrize("name,n,m,k", [("mixture-k-sweep", 300, 200_000, 32),

@@ -9,8 +9,10 @@ margin, D_j being the reference kernel's FP32 distance.  This restates that arit
 in NumPy (the tensor core modelled as an exact sum rounded once to FP32; the margin's
 accumulation term covers the rest) and checks:
 * the bound holds, with room, from data scales of 1e6 down to norms near 2^-48;
-* below that it fails (c underflows to zero, FP32 rounding goes subnormal), which is
-  why queries with ||q|| + max ||x|| < 2^-48 go to the exact SIMT engine.
+* below that it fails (c underflows to zero, FP32 rounding goes subnormal), and from
+  ||q|| + max ||x|| = 2^63 on v can overflow to +inf, so that the filter never keeps a
+  row that the exact search returns with an infinite distance.  Outside
+  [2^-48, 2^63) every query goes to the exact SIMT engine.
 """
 import math
 
@@ -19,7 +21,8 @@ import pytest
 
 from oracle import oracle_all_dists
 
-GUARD = 2.0 ** -48  # tc_prep_q_kernel: qn + Rx below this -> exact SIMT engine
+# tc_prep_q_kernel: qn + Rx outside [LOW, HIGH) -> exact SIMT engine
+LOW, HIGH = 2.0 ** -48, 2.0 ** 63
 GROUP_ROWS = 64
 
 
@@ -37,8 +40,9 @@ def _f32_round_up(x: float) -> np.float32:
     return np.nextafter(y, np.float32(np.inf)) if float(y) < x else y
 
 
-def filter_model(Q: np.ndarray, X: np.ndarray):
-    """(|(||q||^2 + v) - D| / margin, max over rows, per query; qn + Rx per query)."""
+def filter_model(Q: np.ndarray, X: np.ndarray) -> dict:
+    """ratio: |(||q||^2 + v) - D| / margin, max over the rows where v and D are finite,
+    per query; norms: qn + Rx per query; v and D: (n, m)."""
     n, d = Q.shape
     d_pad = -(-d // 64) * 64
     sq = _pow2_scale_for(np.abs(Q).max())
@@ -54,8 +58,9 @@ def filter_model(Q: np.ndarray, X: np.ndarray):
         xinv[g:g + GROUP_ROWS] = np.float32(1.0) / sc
     acc = (qh.astype(np.float64) @ xh.astype(np.float64).T).astype(np.float32)
     c = (np.float32(-2.0) * (np.float32(1.0) / sq)) * xinv  # FP32, may underflow to 0
-    v = (c.astype(np.float64)[None, :] * acc.astype(np.float64)
-         + ssx.astype(np.float64)[None, :]).astype(np.float32)
+    with np.errstate(over="ignore"):  # v may overflow to +inf, as in FP32 on the GPU
+        v = (c.astype(np.float64)[None, :] * acc.astype(np.float64)
+             + ssx.astype(np.float64)[None, :]).astype(np.float32)
     # the margin, as tc_prep_q_kernel forms it
     u = 2.0 ** -11
     qn = np.sqrt(ssq.astype(np.float64)) * (1.0 + 2.0 ** -10)
@@ -68,10 +73,11 @@ def filter_model(Q: np.ndarray, X: np.ndarray):
     margin = np.array([_f32_round_up(t * (1 + 1e-6)) for t in 2.0 * (dotr + accr) + f32t],
                       dtype=np.float64)
     nq = (Q.astype(np.float64) ** 2).sum(1)  # any value common to a query's rows works
-    err = np.abs(nq[:, None] + v.astype(np.float64) - oracle_all_dists(Q, X).astype(np.float64))
-    with np.errstate(divide="ignore", invalid="ignore"):
-        ratio = np.where(err == 0, 0.0, err / margin[:, None]).max(axis=1)
-    return ratio, qn + rx
+    D = oracle_all_dists(Q, X)
+    with np.errstate(over="ignore", invalid="ignore", divide="ignore"):
+        err = np.abs(nq[:, None] + v.astype(np.float64) - D.astype(np.float64))
+        ratio = np.where(np.isfinite(err) & (err > 0), err / margin[:, None], 0.0).max(axis=1)
+    return {"ratio": ratio, "norms": qn + rx, "v": v, "D": D}
 
 
 def _data(seed, n, m, d, q_scale, x_scale):
@@ -86,9 +92,10 @@ def _data(seed, n, m, d, q_scale, x_scale):
 @pytest.mark.parametrize("d", [8, 128, 300])
 def test_margin_bounds_the_filter_error(q_scale, x_scale, d):
     Q, X = _data(d, 24, 640, d, q_scale, x_scale)
-    ratio, norms = filter_model(Q, X)
-    assert (norms >= GUARD).all()
-    assert ratio.max() <= 0.5, ratio.max()
+    f = filter_model(Q, X)
+    assert ((f["norms"] >= LOW) & (f["norms"] < HIGH)).all()
+    assert np.isfinite(f["v"]).all() and np.isfinite(f["D"]).all()
+    assert f["ratio"].max() <= 0.5, f["ratio"].max()
 
 
 def test_rows_of_mixed_scale_in_one_group():
@@ -97,14 +104,32 @@ def test_rows_of_mixed_scale_in_one_group():
     Q, X = _data(3, 24, 640, 64, 1.0, 1.0)
     X[::64] *= 1e4
     X[1::64] *= 1e-8
-    ratio, _ = filter_model(Q, X)
-    assert ratio.max() <= 0.5, ratio.max()
+    f = filter_model(Q, X)
+    assert f["ratio"].max() <= 0.5, f["ratio"].max()
 
 
 @pytest.mark.parametrize("scale", [1e-20, 1e-22])
 def test_margin_fails_below_the_guard(scale):
     """Below the guard the bound does not hold, so those inputs must not be filtered."""
     Q, X = _data(5, 24, 640, 64, scale, scale)
-    ratio, norms = filter_model(Q, X)
-    assert (norms < GUARD).all()
-    assert ratio.max() > 1.0
+    f = filter_model(Q, X)
+    assert (f["norms"] < LOW).all()
+    assert f["ratio"].max() > 1.0
+
+
+def test_filter_drops_infinite_distances_above_the_guard():
+    """From the upper guard on, v overflows to +inf for rows that the exact search returns
+    (with an infinite distance, when fewer than k rows have a finite one)."""
+    Q, X = _data(6, 24, 640, 8, 1.0, 1.0)
+    # every norm 1.2e19: the squared norms stay finite in FP32, their sums do not
+    Q = (Q / np.linalg.norm(Q, axis=1, keepdims=True) * np.float32(1.2e19)).astype(np.float32)
+    X = (X / np.linalg.norm(X, axis=1, keepdims=True) * np.float32(1.2e19)).astype(np.float32)
+    assert np.isfinite(np.einsum("ij,ij->i", X, X, dtype=np.float32)).all()
+    f = filter_model(Q, X)
+    assert (f["norms"] >= HIGH).all()
+    lost = np.isinf(f["v"])
+    assert lost.any() and np.isinf(f["D"][lost]).all()
+    from oracle import oracle_knn
+    _, ids = oracle_knn(Q, X, X.shape[0])
+    q = int(np.argmax(lost.any(axis=1)))
+    assert np.isin(np.flatnonzero(lost[q]), ids[q]).all()  # returned by the exact search
