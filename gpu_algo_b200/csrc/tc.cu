@@ -780,17 +780,19 @@ __global__ void __launch_bounds__(256) tc_prep_q_kernel(const float *__restrict_
     const double acc = (double)(d_pad + 16) * ldexp(1.0, -22) * (qn + eq) * (rx + ex);
     const double f32 = 2.0 * (double)(d + 8) * ldexp(1.0, -24) * (qn + rx) * (qn + rx);
     const double margin = 2.0 * (dotr + acc) + f32;
-    // The filter needs 2^-48 <= qn + Rx < 2^63, and such data goes to the exact SIMT
-    // engine:
-    // * below it, the epilogue's factor -2/(s_q s_x) can underflow to zero
+    // The filter needs 2^-48 <= qn + Rx < 2^63; outside it the search goes to the exact
+    // SIMT engine:
+    // * below, the epilogue's factor -2/(s_q s_x) can underflow to zero
     //   (s_q s_x > 2^150) and FP32 rounding stops being relative (subnormals), so
     //   |(||q||^2 + v) - D| can exceed the margin (every norm under about 3.6e-15);
     // * from 2^63 on, (||q|| + ||x||)^2 >= 2^126 and a distance or v can overflow to
     //   +inf.  A row with v = +inf is never a candidate, but an infinite distance is
     //   still returned when fewer than k rows have a finite one.
-    if (!(qn + rx >= ldexp(1.0, -48) && qn + rx < ldexp(1.0, 63)))
-      atomicOr(&hdr->exact_only, 1);
-    qinfo[row] = make_float2(ss, __double2float_ru(margin * (1.0 + 1e-6)));
+    // The margin is then +inf, so that the level bounds this search hands to the other
+    // shards of a sharded search (whose rows may be in range) bound nothing.
+    const bool in_range = qn + rx >= ldexp(1.0, -48) && qn + rx < ldexp(1.0, 63);
+    if (!in_range) atomicOr(&hdr->exact_only, 1);
+    qinfo[row] = make_float2(ss, in_range ? __double2float_ru(margin * (1.0 + 1e-6)) : INFINITY);
   }
 }
 
