@@ -8,7 +8,8 @@ Writes:
   edges.npz          expected outputs of small edge cases (m < k, exact ties
                      from duplicate rows, a query equal to a row, ragged d,
                      k in {1,2,31,32,33,100,256}, a NaN row, a single query,
-                     integer-valued data); their inputs come from
+                     integer-valued data, distances that overflow to +inf,
+                     subnormal distances); their inputs come from
                      ``edge_cases()`` (seeded) and are pinned by SHA-256;
   inputs.json        SHA-256 of the generated inputs, to catch generator drift.
 
@@ -65,6 +66,15 @@ def edge_cases() -> dict[str, tuple[np.ndarray, np.ndarray, int]]:
     # integer-valued data: many exact distance ties across different rows
     cases["int_grid"] = (rng.integers(-2, 3, size=(50, 8)).astype(np.float32),
                          rng.integers(-2, 3, size=(4000, 8)).astype(np.float32), 20)
+    # norms of 1.2e19: finite squared norms, distances that overflow to +inf; with k = m
+    # the rows at +inf come last, ordered by index
+    def at_norm(a, norm):
+        return (a / np.linalg.norm(a, axis=1, keepdims=True) * np.float32(norm)).astype(np.float32)
+    cases["inf_dists"] = (at_norm(rng.standard_normal((11, 16), dtype=np.float32), 1.2e19),
+                          at_norm(rng.standard_normal((300, 16), dtype=np.float32), 1.2e19), 300)
+    # norms near 1e-19: subnormal distances
+    cases["tiny_norms"] = ((rng.standard_normal((37, 32)) * 1e-20).astype(np.float32),
+                           (rng.standard_normal((3000, 32)) * 1e-20).astype(np.float32), 10)
     return cases
 
 

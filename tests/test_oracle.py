@@ -104,6 +104,17 @@ def test_edge_semantics(edges):
     for qi in range(Q.shape[0]):  # equal distances are ordered by index
         for a in range(k - 1):
             assert (gd[qi, a], gi[qi, a]) < (gd[qi, a + 1], gi[qi, a + 1])
+    # rows at +inf are returned (k = m), last, by index
+    Q, X, k, gd, gi = edges["inf_dists"]
+    assert np.isinf(gd).any() and (gi >= 0).all()
+    for qi in range(Q.shape[0]):
+        inf = np.isinf(gd[qi])
+        assert (np.diff(inf.astype(int)) >= 0).all()  # after every finite distance
+        assert (np.diff(gi[qi][inf]) > 0).all()
+    # subnormal distances keep their order
+    Q, X, k, gd, gi = edges["tiny_norms"]
+    assert (gd < np.finfo(np.float32).tiny).all() and (gd > 0).all()
+    assert (np.diff(gd, axis=1) >= 0).all()
 
 
 def test_merge_of_shards_equals_whole(plumbing):
