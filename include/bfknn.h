@@ -13,7 +13,8 @@
  *   out_ids   (n, k) int32    id_offset + database row, ties by lower index;
  *   missing slots (m < k, or rows whose distance is NaN) are padded with
  *   (3.402823e38f, -1); a distance that overflows to +inf is a value like any
- *   other (such rows come last, as the reference's heap_push keeps them).
+ *   other: such rows come last, as the reference's general kernel keeps them
+ *   (heap_push, bf/fp32.py:8-27; its small-k kernel drops them instead).
  * Distances are bit-identical to the reference kernels' direct-difference
  * arithmetic (bf/fp32.py:74-82: dif = q - x; dist = fma(dif, dif, dist),
  * in dimension order).
