@@ -21,6 +21,10 @@
  *   - rows whose distance is NaN are never returned (the reference's strict
  *     `dist < lmax` test rejects them once a list is full; the oracle rejects
  *     them always, which is the defined behaviour of this engine).
+ *   - a distance that overflowed to +inf is a value: such rows come last and
+ *     are returned when fewer than k rows are finite, as the general kernel's
+ *     heap_push (bf/fp32.py:8-27) keeps any distance while its list is not
+ *     full (the small-k kernel, bf/fp32.py:100-112, drops them instead).
  *   - merge of sorted per-shard lists: bf/fp32_tiled.py:118-178 (the
  *     reference's merge re-inserts every partial with heap_push; here the
  *     lists are merged under the same (distance, index) order).
