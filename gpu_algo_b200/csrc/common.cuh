@@ -15,8 +15,8 @@ struct WsHeader {
   int32_t error;          // device status word: 0 ok, else an ErrCode below
   uint32_t rx_bits;       // max row norm of X (float bits, positive => ordered as uint)
   uint32_t qmax_bits;     // max |Q| (float bits)
-  int32_t exact_only;     // the filter margin does not hold (a non-finite norm, or norms
-                          // too small for it): every query goes to the exact SIMT engine
+  int32_t exact_only;     // the filter cannot be trusted (a non-finite norm, or norms
+                          // outside its range): every query goes to the exact SIMT engine
   int32_t fallback;       // queries routed to the exact SIMT engine
   int32_t max_cand;       // max candidates of one query
   unsigned long long candidates;  // total candidates appended by the filter
