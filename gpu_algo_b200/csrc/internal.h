@@ -60,7 +60,7 @@ struct TcPlan {
 
 // A prepared database (bfk_prepare): the TC engine's row arrays for one X, made once.
 // Layout, every part 256-byte aligned: a 256-byte status block (the rows' norm bound and
-// non-finite flag, as the workspace header holds them), a 256-byte description
+// exact-only flag, set for a non-finite row, as the workspace header holds them), a 256-byte description
 // (PreparedInfo), the f16 rows (m, d_pad), ||x||^2 (x_tiles * 256) and the inverse scale
 // of every 64-row group (x_tiles * 4).
 struct PreparedInfo {

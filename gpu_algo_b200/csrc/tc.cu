@@ -1681,7 +1681,7 @@ static bool make_tmap(CUtensorMap *map, const void *base, int64_t rows, int cols
 }
 
 // rows -> f16 in 64-row scale groups, ||x||^2, inverse scales; norm bound and
-// non-finite flag into hdr
+// exact-only flag (set for a non-finite row) into hdr
 static void launch_prep_rows(const float *X, int64_t m, int d, int d_pad, int64_t x_tiles,
                              __half *Xh, float *xnorm, float *xinv, WsHeader *hdr,
                              cudaStream_t stream) {
@@ -1797,7 +1797,7 @@ int tc_run(const float *Q, const float *X, int64_t id_offset, float *out_d, int3
   // pass 0: prep
   tc_qmax_kernel<<<592, 256, 0, stream>>>(Q, p.n * p.d, hdr);
   if (prepared) {
-    // the rows' norm bound and non-finite flag, as their preparation found them
+    // the rows' norm bound and exact-only flag, as their preparation found them
     const PreparedLayout PL = tc_prepared_layout(p.m, p.d);
     tc_take_row_status<<<1, 32, 0, stream>>>(
         reinterpret_cast<const WsHeader *>(pb + PL.off_status), hdr);
