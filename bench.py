@@ -145,16 +145,32 @@ def gen_workload(name, rank, world, rows, queries):
 
 
 def cpu_baseline(X, Q, k, sample, steps=1):
-    """The NumPy/OpenBLAS restatement timed on this host (the CPU baseline)."""
+    """The NumPy/OpenBLAS restatement timed on this host (the CPU baseline).
+
+    BLAS runs on every core this process may use, whatever OMP_NUM_THREADS the
+    launcher set (torch.distributed.run sets it to 1); returns the per-step times
+    and the BLAS thread count in effect."""
+    from threadpoolctl import threadpool_info, threadpool_limits
+
     from oracle import numpy_knn
     cores = len(os.sched_getaffinity(0)) if hasattr(os, "sched_getaffinity") else os.cpu_count()
     times = []
-    for s in range(steps):
-        q0 = (s * sample) % max(1, Q.shape[0] - sample + 1)
-        t = time.perf_counter()
-        numpy_knn(Q[q0:q0 + sample], X, k)
-        times.append(time.perf_counter() - t)
-    return times, cores
+    with threadpool_limits(limits=cores, user_api="blas"):
+        blas = [p["num_threads"] for p in threadpool_info() if p.get("user_api") == "blas"]
+        threads = max(blas) if blas else 1
+        for s in range(steps):
+            q0 = (s * sample) % max(1, Q.shape[0] - sample + 1)
+            t = time.perf_counter()
+            numpy_knn(Q[q0:q0 + sample], X, k)
+            times.append(time.perf_counter() - t)
+    return times, threads
+
+
+def bench_config(a, N, Qn, d, k):
+    """The workload description both arms print (the same dict for the same run)."""
+    return {"workload": a.workload, "N": N, "Q": Qn, "d": d, "k": k,
+            "parallelism": f"rowshard{a.gpus}", "rows_prepared_once": bool(a.prepared),
+            "l2": f"inputs larger than L2 (database {N * d * 4 / 1e9:.2f} GB), no flush"}
 
 
 def run_reference(a):
@@ -176,7 +192,7 @@ def run_reference(a):
         "value": qps, "unit": "queries/s", "n_gpus": a.gpus, "steps": a.steps,
         "warmup": a.warmup, "ms_per_step": ms, "higher_is_better": True,
         "scaling": "strong", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-        "config": {"workload": a.workload, "N": N, "Q": Qn, "d": w["d"], "k": k},
+        "config": bench_config(a, N, Qn, w["d"], k),
         "cpu_baseline": {"value": qps, "unit": "queries/s", "cores": cores, "kind": "port",
                          "sample": f"{sample} queries per step against the full {N}-row database "
                                    "(NumPy/OpenBLAS blocked GEMM + argpartition)"},
@@ -344,11 +360,8 @@ def main(argv=None) -> int:
                             if (a.workload, N, Qn, d, k) in PUBLISHED_QPS else None),
             "dtype": "f32",
             "data": "synthetic",
-            "config": {"workload": a.workload, "N": N, "Q": Qn, "d": d, "k": k,
-                       "engine": stats["engine"], "parallelism": f"rowshard{world}",
-                       "rows_prepared_once": bool(a.prepared),
-                       "l2": "inputs larger than L2 (database "
-                             f"{N * d * 4 / 1e9:.2f} GB), no flush"},
+            "config": bench_config(a, N, Qn, d, k),
+            "engine": stats["engine"],
             "roofline": roofline,
             "cpu_baseline": cpu,
             "e2e": e2e,

@@ -37,6 +37,7 @@ EXPORTS = (
     "bfk_search",
     "bfk_merge",
     "bfk_kernel_attrs",
+    "bfk_merge_attrs",
     "bfk_search_stats",
     "bfk_search_noalloc",
     "bfk_prepared_size",
@@ -118,6 +119,8 @@ def load() -> ctypes.CDLL:
         lib.bfk_merge.argtypes = [vp, vp, i64, i32, i32, vp, vp, vp]
         lib.bfk_kernel_attrs.restype = i32
         lib.bfk_kernel_attrs.argtypes = [i32, i32, i32, ctypes.POINTER(Attrs)]
+        lib.bfk_merge_attrs.restype = i32
+        lib.bfk_merge_attrs.argtypes = [i32, i32, ctypes.POINTER(Attrs)]
         lib.bfk_prepared_size.restype = i32
         lib.bfk_prepared_size.argtypes = [i64, i32, ctypes.POINTER(u64)]
         lib.bfk_prepare.restype = i32

@@ -1,196 +1,194 @@
 #!/usr/bin/env python3
-"""Drop-in for bf/bench_fp32_variant_repeat_over_n.py: the repeated variant study
-over n at fixed k, writing the same JSON payload (``meta`` / ``results`` /
-``failures``, bf/bench_fp32_variant_repeat_over_n.py:165-184), so the reference's
-plot scripts read its output unchanged.
+"""Variant study over the query count n, writing the reference's result payload.
+
+The reference publishes its only numbers as JSON files written by
+bf/bench_fp32_variant_repeat_over_n.py, and its plot script
+bf/plot_fp32_variant_repeat_over_n.py reads them (``meta`` m/d/k/trials; per row
+variant, n, mean_queries_per_second, std_queries_per_second).  This study takes
+the same command-line flags with the same defaults and writes a payload with the
+same keys (``meta``, ``results``, ``failures``), so that plot script reads its
+output unchanged:
 
     python -m gpu_algo_b200.bf.bench_over_n --m 1000000 --d 8 --k 1 \\
         --n-values 1000,16000,128000 --out-json over_n.json
 
-The arguments and their defaults are the reference's.  Two differences:
-* the data comes from NumPy's PCG64 seeded with ``--seed`` (the reference draws
-  from CuPy's generator, which is not available here), Gaussian rows and queries
-  as in the reference, or clustered queries built the same way;
-* every variant runs this package's runner of the same name; they return the
-  same exact sorted results (the engine is chosen per shape).
+Everything else is this package's own:
+* data: NumPy PCG64 seeded with ``--seed``, rows then queries from one stream
+  (the reference draws from CuPy's generator, which is not installed here);
+  ``clustered`` queries are noisy copies of shared centres;
+* every variant name runs this package's runner of that name, and all of them
+  return the same exact, sorted top-k;
+* throughput per (variant, n) is n over the mean trial time; its spread is the
+  mean time's spread carried through q = n / t to first order, which is the
+  quantity the published files report.
 """
 from __future__ import annotations
 
 import argparse
+import itertools
 import json
-import math
+import statistics
+import sys
+from dataclasses import dataclass, field
 from pathlib import Path
 
 import numpy as np
 
 VARIANT_NAMES = ("baseline", "heap", "q2", "q4", "q8", "q16", "q32", "q64", "q128")
+QGROUP_SIZES = {f"q{g}": g for g in (4, 8, 16, 32, 64, 128)}
 
-
-def variants_table():
-    """Variant name -> runner(Q, X, k, reps), as in the reference's VARIANTS."""
-    from .fp32 import run_bf_fp32
-    from .fp32_heap import run_bf_fp32_heap
-    from .fp32_q2 import run_bf_fp32_q2
-    from .fp32_qgroup import run_bf_fp32_qgroup
-    table = {
-        "baseline": lambda Q, X, k, reps: run_bf_fp32(Q, X, k, reps=reps),
-        "heap": lambda Q, X, k, reps: run_bf_fp32_heap(Q, X, k, reps=reps),
-        "q2": lambda Q, X, k, reps: run_bf_fp32_q2(Q, X, k, reps=reps),
-    }
-    for g in (4, 8, 16, 32, 64, 128):
-        table[f"q{g}"] = (lambda qpb: lambda Q, X, k, reps: run_bf_fp32_qgroup(Q, X, k, qpb=qpb,
-                                                                               reps=reps))(g)
-    return table
-
-
-def parse_csv_ints(raw: str) -> list[int]:
-    values = [int(part.strip()) for part in raw.split(",") if part.strip()]
-    if not values:
-        raise ValueError("Need at least one integer value")
-    return values
-
-
-def parse_variants(raw: str) -> list[str]:
-    values = [part.strip() for part in raw.split(",") if part.strip()]
-    if not values:
-        raise ValueError("Need at least one variant")
-    bad = [v for v in values if v not in VARIANT_NAMES]
-    if bad:
-        raise ValueError(f"Unknown variants: {bad}")
-    return values
-
-
-def mean_std(values: list[float]) -> tuple[float, float]:
-    mean = sum(values) / len(values)
-    var = sum((v - mean) ** 2 for v in values) / len(values)
-    return mean, math.sqrt(var)
-
-
-def make_data(seed: int, m: int, d: int, max_n: int, mode: str, cluster_size: int,
-              cluster_noise: float) -> tuple[np.ndarray, np.ndarray]:
-    """Rows, then queries, from one PCG64 stream (the reference's order)."""
-    rng = np.random.Generator(np.random.PCG64(seed))
-    X = rng.standard_normal((m, d), dtype=np.float32)
-    if mode == "gaussian":
-        Q = rng.standard_normal((max_n, d), dtype=np.float32)
-    elif mode == "clustered":
-        if cluster_size <= 0:
-            raise ValueError("cluster_size must be positive")
-        groups = (max_n + cluster_size - 1) // cluster_size
-        centers = rng.standard_normal((groups, d), dtype=np.float32)
-        noise = rng.standard_normal((max_n, d), dtype=np.float32) * np.float32(cluster_noise)
-        Q = centers[np.arange(max_n) // cluster_size] + noise
-    else:
-        raise ValueError(f"Unknown query mode: {mode}")
-    return X, Q
-
-
-def result_row(variant: str, args, n: int, trial_ms: list[float], block: int) -> dict:
-    """One ``results`` entry, with the reference's keys and formulas."""
-    mean_ms, std_ms = mean_std(trial_ms)
-    mean_qps = n / (mean_ms * 1e-3)
-    std_qps = 0.0 if mean_ms == 0 else (n * std_ms) / ((mean_ms ** 2) * 1e-3)
-    return {
-        "variant": variant,
-        "distribution": args.query_mode,
-        "m": args.m,
-        "d": args.d,
-        "n": n,
-        "k": args.k,
-        "trials": args.trials,
-        "reps": args.reps,
-        "trial_query_ms": trial_ms,
-        "mean_query_ms": mean_ms,
-        "std_query_ms": std_ms,
-        "mean_queries_per_second": mean_qps,
-        "std_queries_per_second": std_qps,
-        "block": int(block),
-    }
-
-
-def make_payload(args, n_values: list[int], variants: list[str], rows: list[dict],
-                 failures: list[dict]) -> dict:
-    return {
-        "meta": {
-            "m": args.m,
-            "d": args.d,
-            "k": args.k,
-            "seed": args.seed,
-            "trials": args.trials,
-            "reps": args.reps,
-            "skip_failures": bool(args.skip_failures),
-            "query_mode": args.query_mode,
-            "cluster_size": args.cluster_size,
-            "cluster_noise": args.cluster_noise,
-            "n_values": n_values,
-            "variants": variants,
-        },
-        "results": rows,
-        "failures": failures,
-    }
+# (flag, type, default, help): the reference study's flags and defaults
+_FLAGS = (
+    ("--m", int, 1_000_000, "database rows"),
+    ("--d", int, 8, "dimensions"),
+    ("--n-values", str, "1000,2000,4000,8000,16000", "query counts, comma separated"),
+    ("--k", int, 1, "neighbours per query"),
+    ("--variants", str, ",".join(VARIANT_NAMES), "runner names, comma separated"),
+    ("--trials", int, 20, "timed trials per (variant, n)"),
+    ("--reps", int, 5, "searches per trial (the runner's reps)"),
+    ("--seed", int, 42, "PCG64 seed of the data"),
+    ("--cluster-size", int, 16, "clustered queries: queries per centre"),
+    ("--cluster-noise", float, 0.05, "clustered queries: noise scale around a centre"),
+    ("--out-json", str, "bf_fp32_variant_repeat_over_n_d8_k1.json", "where to write the payload"),
+)
 
 
 def build_parser() -> argparse.ArgumentParser:
-    ap = argparse.ArgumentParser(description="Repeated BF-FP32 variant study over n at fixed k.")
-    ap.add_argument("--m", type=int, default=1_000_000)
-    ap.add_argument("--d", type=int, default=8)
-    ap.add_argument("--n-values", type=str, default="1000,2000,4000,8000,16000")
-    ap.add_argument("--k", type=int, default=1)
-    ap.add_argument("--variants", type=str, default=",".join(VARIANT_NAMES))
-    ap.add_argument("--trials", type=int, default=20)
-    ap.add_argument("--reps", type=int, default=5)
-    ap.add_argument("--seed", type=int, default=42)
-    ap.add_argument("--query-mode", type=str, default="gaussian", choices=["gaussian", "clustered"])
-    ap.add_argument("--cluster-size", type=int, default=16)
-    ap.add_argument("--cluster-noise", type=float, default=0.05)
-    ap.add_argument("--skip-failures", action="store_true")
-    ap.add_argument("--out-json", type=str, default="bf_fp32_variant_repeat_over_n_d8_k1.json")
+    ap = argparse.ArgumentParser(
+        description="Exact k-NN runner variants timed over a range of query counts; writes the "
+                    "reference's over-n JSON payload.")
+    for flag, typ, default, text in _FLAGS:
+        ap.add_argument(flag, type=typ, default=default, help=f"{text} (default {default})")
+    ap.add_argument("--query-mode", default="gaussian", choices=("gaussian", "clustered"),
+                    help="query distribution (default gaussian)")
+    ap.add_argument("--skip-failures", action="store_true",
+                    help="record a failing (variant, n) in 'failures' and go on")
     return ap
 
 
-def main(argv=None) -> None:
+def _split(raw: str, what: str, convert) -> list:
+    items = [convert(tok) for tok in (t.strip() for t in raw.split(",")) if tok]
+    if not items:
+        raise ValueError(f"{what}: the list is empty")
+    return items
+
+
+def n_values_of(raw: str) -> list[int]:
+    return _split(raw, "--n-values", int)
+
+
+def variants_of(raw: str) -> list[str]:
+    names = _split(raw, "--variants", str)
+    unknown = sorted(set(names) - set(VARIANT_NAMES))
+    if unknown:
+        raise ValueError(f"--variants: no runner named {', '.join(unknown)} "
+                         f"(choose from {', '.join(VARIANT_NAMES)})")
+    return names
+
+
+def runner_for(variant: str):
+    """The package runner behind a variant name: f(Q, X, k, reps) -> result dict."""
+    from . import fp32, fp32_heap, fp32_q2, fp32_qgroup
+    if variant == "baseline":
+        return lambda Q, X, k, reps: fp32.run_bf_fp32(Q, X, k, reps=reps)
+    if variant == "heap":
+        return lambda Q, X, k, reps: fp32_heap.run_bf_fp32_heap(Q, X, k, reps=reps)
+    if variant == "q2":
+        return lambda Q, X, k, reps: fp32_q2.run_bf_fp32_q2(Q, X, k, reps=reps)
+    g = QGROUP_SIZES[variant]
+    return lambda Q, X, k, reps: fp32_qgroup.run_bf_fp32_qgroup(Q, X, k, qpb=g, reps=reps)
+
+
+def synthetic_data(seed: int, m: int, d: int, n_max: int, query_mode: str = "gaussian",
+                   cluster_size: int = 16, cluster_noise: float = 0.05):
+    """(X (m, d), Q (n_max, d)) float32: standard normal rows, then the queries."""
+    gen = np.random.default_rng(np.random.PCG64(seed))
+    X = gen.standard_normal((m, d), dtype=np.float32)
+    if query_mode == "gaussian":
+        return X, gen.standard_normal((n_max, d), dtype=np.float32)
+    if query_mode != "clustered":
+        raise ValueError(f"query mode {query_mode!r} is neither gaussian nor clustered")
+    if cluster_size <= 0:
+        raise ValueError("cluster size must be at least 1")
+    centres = gen.standard_normal((-(-n_max // cluster_size), d), dtype=np.float32)
+    owner = np.repeat(np.arange(centres.shape[0]), cluster_size)[:n_max]
+    jitter = gen.standard_normal((n_max, d), dtype=np.float32) * np.float32(cluster_noise)
+    return X, np.ascontiguousarray(centres[owner] + jitter)
+
+
+@dataclass
+class Cell:
+    """The timed trials of one (variant, n)."""
+    variant: str
+    n: int
+    trial_ms: list[float] = field(default_factory=list)
+    block: int = 0
+
+    def summary(self, args) -> dict:
+        """The payload row (the reference's keys)."""
+        mean_ms = statistics.fmean(self.trial_ms)
+        sd_ms = statistics.pstdev(self.trial_ms)
+        qps = self.n / (mean_ms / 1e3)
+        # q = n / t, so dq = q * dt / t to first order
+        sd_qps = qps * sd_ms / mean_ms if mean_ms > 0 else 0.0
+        return dict(variant=self.variant, distribution=args.query_mode, m=args.m, d=args.d,
+                    n=self.n, k=args.k, trials=args.trials, reps=args.reps,
+                    trial_query_ms=list(self.trial_ms), mean_query_ms=mean_ms,
+                    std_query_ms=sd_ms, mean_queries_per_second=qps,
+                    std_queries_per_second=sd_qps, block=int(self.block))
+
+
+def payload(args, n_values: list[int], variants: list[str], rows: list[dict],
+            failures: list[dict]) -> dict:
+    meta = {key: getattr(args, key) for key in
+            ("m", "d", "k", "seed", "trials", "reps", "query_mode", "cluster_size",
+             "cluster_noise")}
+    meta.update(skip_failures=bool(args.skip_failures), n_values=list(n_values),
+                variants=list(variants))
+    return {"meta": meta, "results": rows, "failures": failures}
+
+
+def run_study(args, log=print) -> dict:
     import torch
+    n_values = n_values_of(args.n_values)
+    variants = variants_of(args.variants)
+    X, Q = synthetic_data(args.seed, args.m, args.d, max(n_values), args.query_mode,
+                          args.cluster_size, args.cluster_noise)
+    Xd = torch.from_numpy(X).cuda()
+    Qd = torch.from_numpy(Q).cuda()
+    rows, failures = [], []
+    log(f"# over-n study: m={args.m} d={args.d} k={args.k} trials={args.trials} "
+        f"reps={args.reps} queries={args.query_mode}")
+    log(f"# {'variant':>8} {'n':>8} {'ms':>10} {'+-':>8} {'queries/s':>12} {'+-':>10}")
+    for variant, n in itertools.product(variants, n_values):
+        run = runner_for(variant)
+        cell = Cell(variant, n)
+        try:
+            for _ in range(args.trials):
+                res = run(Qd[:n], Xd, args.k, args.reps)
+                cell.trial_ms.append(float(res["ms"]))
+                cell.block = int(res["block"])
+        except Exception as exc:  # noqa: BLE001 -- recorded, or re-raised below
+            if not args.skip_failures:
+                raise
+            failures.append({"variant": variant, "n": n, "k": args.k,
+                             "error": f"{type(exc).__name__}: {exc}"})
+            log(f"  {variant:>8} {n:>8} failed: {exc}")
+            continue
+        row = cell.summary(args)
+        rows.append(row)
+        log(f"  {variant:>8} {n:>8} {row['mean_query_ms']:10.4f} {row['std_query_ms']:8.4f} "
+            f"{row['mean_queries_per_second']:12.0f} {row['std_queries_per_second']:10.0f}")
+    return payload(args, n_values, variants, rows, failures)
+
+
+def main(argv=None) -> int:
     args = build_parser().parse_args(argv)
-    n_values = parse_csv_ints(args.n_values)
-    variants = parse_variants(args.variants)
-    table = variants_table()
-    X, Q = make_data(args.seed, args.m, args.d, max(n_values), args.query_mode,
-                     args.cluster_size, args.cluster_noise)
-    X_gpu = torch.from_numpy(X).cuda()
-    Q_full = torch.from_numpy(np.ascontiguousarray(Q)).cuda()
-    rows: list[dict] = []
-    failures: list[dict] = []
-    print(f"BF-FP32 repeated variant study over n | m={args.m:,} d={args.d} k={args.k} "
-          f"n_values={n_values} variants={variants} trials={args.trials}")
-    for variant in variants:
-        print(f"\n[{variant}]")
-        runner = table[variant]
-        for n in n_values:
-            Q_gpu = Q_full[:n]
-            trial_ms = []
-            last = None
-            try:
-                for _ in range(args.trials):
-                    last = runner(Q_gpu, X_gpu, args.k, args.reps)
-                    trial_ms.append(float(last["ms"]))
-            except Exception as exc:  # recorded like the reference's --skip-failures
-                msg = f"{type(exc).__name__}: {exc}"
-                if not args.skip_failures:
-                    raise
-                failures.append({"variant": variant, "n": n, "k": args.k, "error": msg})
-                print(f"  n={n:>6}  FAILED  {msg}")
-                continue
-            row = result_row(variant, args, n, trial_ms, last["block"])
-            rows.append(row)
-            print(f"  n={n:>6}  mean={row['mean_query_ms']:9.3f} ms  "
-                  f"std={row['std_query_ms']:7.3f} ms  "
-                  f"qps={row['mean_queries_per_second']:9.0f} +/- "
-                  f"{row['std_queries_per_second']:7.0f}  block={row['block']}")
-    out_path = Path(args.out_json)
-    out_path.write_text(json.dumps(make_payload(args, n_values, variants, rows, failures),
-                                   indent=2) + "\n", encoding="ascii")
-    print(f"\nWrote {out_path}")
+    out = run_study(args)
+    Path(args.out_json).write_text(json.dumps(out, indent=2) + "\n", encoding="ascii")
+    print(f"# payload: {args.out_json}")
+    return 0
 
 
 if __name__ == "__main__":
-    main()
+    sys.exit(main())

@@ -132,6 +132,26 @@ def _engine_attrs(Q, X, k, engine: str, slices: int, label: str) -> tuple[int, i
     return block, smem, attrs
 
 
+def _merge_report(Q, X, k, engine: str, slices: int, label: str) -> tuple[int, dict]:
+    """(merge_shared_mem_bytes, merge_kernel_attrs) of the merge the search really ran.
+
+    The SIMT engine merges its database slices with the kernel of ``bfk_merge``; the
+    tensor-core engine and a one-slice search run no merge, which is reported as 0
+    bytes and an attribute dict that says so."""
+    stats = _engine.last_stats(Q, X, k, engine=engine, slices=slices)
+    lists = int(stats["slices"])
+    if stats["engine"] != "direct" or lists <= 1:
+        return 0, {"kernel_variant": "none", "reference_variant": label,
+                   "note": f"the {stats['engine']} engine ran no merge for this search"}
+    attrs = _engine.merge_attrs(lists, k)
+    smem = int(attrs.pop("dynamic_smem_bytes"))
+    attrs.pop("block_threads")
+    attrs = {key: int(v) for key, v in attrs.items()}
+    attrs["kernel_variant"] = f"merge of {lists} lists"
+    attrs["reference_variant"] = label
+    return smem, attrs
+
+
 def build_bf_fp32_runner(Q_gpu, X_gpu, k: int):
     """(fn, out_ids, out_dists, block, shared_mem, attrs) as bf/fp32.py:252-275."""
     Q, X, fn, out_ids, out_dists = _make_runner(Q_gpu, X_gpu, k)

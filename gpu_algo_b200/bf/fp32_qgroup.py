@@ -7,7 +7,7 @@ tile), so ``qpb`` is accepted and reported but does not change the launch.
 """
 from __future__ import annotations
 
-from .fp32 import _engine_attrs, _finish, _make_runner
+from .fp32 import _engine_attrs, _finish, _make_runner, _merge_report
 
 
 def choose_qgroup_block(k: int, d: int, qpb: int) -> int:
@@ -31,19 +31,20 @@ def run_bf_fp32_qgroup(Q_gpu, X_gpu, k: int, qpb: int, reps: int = 8) -> dict:
     Q, X, fn, out_ids, out_dists = _make_runner(Q_gpu, X_gpu, k)
     fn()
     block, smem, attrs = _engine_attrs(Q, X, k, "auto", 0, f"q{qpb}")
+    merge_smem, merge_attrs = _merge_report(Q, X, k, "auto", 0, "qgroup_merge")
     ms, ids, dists = _finish(fn, out_ids, out_dists, reps)
-    merge_attrs = dict(attrs)
-    merge_attrs["reference_variant"] = "qgroup_merge"
     return {
         "ids": ids,
         "dists": dists,
         "ms": ms,
         "block": block,
         "qpb": qpb,
+        "qpb_note": "qpb is reported only: the engine's own query tiles (32 or 128 queries) "
+                    "set the launch, so it does not change the work or the results",
         "tile_size": tile_size,
         "n_tiles": n_tiles,
         "partial_shared_mem_bytes": smem,
-        "merge_shared_mem_bytes": 8192 * 8,
+        "merge_shared_mem_bytes": merge_smem,
         "partial_kernel_attrs": attrs,
         "merge_kernel_attrs": merge_attrs,
     }

@@ -9,7 +9,7 @@ bf/fp32_tiled.py:172-177; the set of results is the same).
 """
 from __future__ import annotations
 
-from .fp32 import _engine_attrs, _finish, _make_runner
+from .fp32 import _engine_attrs, _finish, _make_runner, _merge_report
 
 
 def run_bf_fp32_tiled(Q_gpu, X_gpu, k: int, tile_size: int = 125_000, reps: int = 10) -> dict:
@@ -21,9 +21,8 @@ def run_bf_fp32_tiled(Q_gpu, X_gpu, k: int, tile_size: int = 125_000, reps: int 
     Q, X, fn, out_ids, out_dists = _make_runner(Q_gpu, X_gpu, k, engine="direct", slices=slices)
     fn()
     block, smem, attrs = _engine_attrs(Q, X, k, "direct", slices, "tiled_partial")
+    merge_smem, merge_attrs = _merge_report(Q, X, k, "direct", slices, "tiled_merge")
     ms, ids, dists = _finish(fn, out_ids, out_dists, reps)
-    merge_attrs = dict(attrs)
-    merge_attrs["reference_variant"] = "tiled_merge"
     return {
         "ids": ids,
         "dists": dists,
@@ -32,7 +31,7 @@ def run_bf_fp32_tiled(Q_gpu, X_gpu, k: int, tile_size: int = 125_000, reps: int 
         "tile_size": tile_size,
         "n_tiles": n_tiles,
         "partial_shared_mem_bytes": smem,
-        "merge_shared_mem_bytes": 8192 * 8,
+        "merge_shared_mem_bytes": merge_smem,
         "partial_kernel_attrs": attrs,
         "merge_kernel_attrs": merge_attrs,
     }

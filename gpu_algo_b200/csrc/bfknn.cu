@@ -366,6 +366,19 @@ bfk_status_t bfk_merge(const float *cand_dists, const int32_t *cand_ids, int64_t
                                   reinterpret_cast<cudaStream_t>(stream)));
 }
 
+static void fill_attrs(const cudaFuncAttributes &a, size_t dyn, int threads, bfk_attrs_t *out) {
+  std::memset(out, 0, sizeof(*out));
+  out->num_regs = a.numRegs;
+  out->shared_size_bytes = (int32_t)a.sharedSizeBytes;
+  out->dynamic_smem_bytes = (int32_t)dyn;
+  out->local_size_bytes = (int32_t)a.localSizeBytes;
+  out->const_size_bytes = (int32_t)a.constSizeBytes;
+  out->max_threads_per_block = a.maxThreadsPerBlock;
+  out->binary_version = a.binaryVersion;
+  out->ptx_version = a.ptxVersion;
+  out->block_threads = threads;
+}
+
 bfk_status_t bfk_kernel_attrs(int32_t engine, int32_t d, int32_t k, bfk_attrs_t *out) {
   if (!out || d <= 0 || k <= 0) return BFK_ERR_INVALID_ARGUMENT;
   if (d > kMaxD || k > kMaxK) return BFK_ERR_UNSUPPORTED;
@@ -386,16 +399,18 @@ bfk_status_t bfk_kernel_attrs(int32_t engine, int32_t d, int32_t k, bfk_attrs_t 
   }
   cudaFuncAttributes a;
   if (cudaFuncGetAttributes(&a, fn) != cudaSuccess) return BFK_ERR_CUDA;
-  std::memset(out, 0, sizeof(*out));
-  out->num_regs = a.numRegs;
-  out->shared_size_bytes = (int32_t)a.sharedSizeBytes;
-  out->dynamic_smem_bytes = (int32_t)dyn;
-  out->local_size_bytes = (int32_t)a.localSizeBytes;
-  out->const_size_bytes = (int32_t)a.constSizeBytes;
-  out->max_threads_per_block = a.maxThreadsPerBlock;
-  out->binary_version = a.binaryVersion;
-  out->ptx_version = a.ptxVersion;
-  out->block_threads = threads;
+  fill_attrs(a, dyn, threads, out);
+  return BFK_OK;
+}
+
+bfk_status_t bfk_merge_attrs(int32_t lists, int32_t k, bfk_attrs_t *out) {
+  if (!out || lists <= 0 || k <= 0) return BFK_ERR_INVALID_ARGUMENT;
+  if (k > merge_max_k()) return BFK_ERR_UNSUPPORTED;
+  size_t dyn = 0;
+  const void *fn = merge_kernel_for(lists, k, &dyn);
+  cudaFuncAttributes a;
+  if (cudaFuncGetAttributes(&a, fn) != cudaSuccess) return BFK_ERR_CUDA;
+  fill_attrs(a, dyn, merge_threads(), out);
   return BFK_OK;
 }
 

@@ -28,6 +28,9 @@ cudaError_t launch_scan(const float *Q, int64_t n, const float *X, int64_t m, in
 cudaError_t launch_merge(const float *cand_d, const int32_t *cand_i, int64_t n, int lists, int k,
                          float *out_d, int32_t *out_i, cudaStream_t stream);
 int merge_max_k();
+// the kernel launch_merge runs for `lists` lists of k, and its dynamic shared memory
+const void *merge_kernel_for(int lists, int k, size_t *smem);
+int merge_threads();
 cudaError_t launch_fill_pad(float *out_d, int32_t *out_i, int64_t count, cudaStream_t stream);
 
 // tc.cu -- tcgen05 filter engine

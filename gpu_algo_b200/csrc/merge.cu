@@ -128,6 +128,17 @@ cudaError_t launch_merge(const float *cand_d, const int32_t *cand_i, int64_t n, 
 
 int merge_max_k() { return kMergeCap / 2; }
 
+const void *merge_kernel_for(int lists, int k, size_t *smem) {
+  if (lists <= kRankMergeLists && (int64_t)lists * k <= kMergeCap) {
+    *smem = (size_t)lists * k * sizeof(uint64_t);
+    return (const void *)knn_merge_rank_kernel;
+  }
+  *smem = (size_t)kMergeCap * sizeof(uint64_t);
+  return (const void *)knn_merge_kernel;
+}
+
+int merge_threads() { return kMergeThreads; }
+
 __global__ void fill_pad_kernel(float *out_d, int32_t *out_i, int64_t count) {
   for (int64_t e = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; e < count;
        e += (int64_t)gridDim.x * blockDim.x) {

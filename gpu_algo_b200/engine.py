@@ -248,10 +248,7 @@ def merge(cand_d: torch.Tensor, cand_i: torch.Tensor, k: int):
     return out_d, out_i
 
 
-def kernel_attrs(engine: str, d: int, k: int) -> dict:
-    a = _lib.Attrs()
-    _lib.check(_lib.load().bfk_kernel_attrs(_lib.ENGINES[engine], d, k, ctypes.byref(a)),
-               "bfk_kernel_attrs")
+def _attrs_dict(a: "_lib.Attrs") -> dict:
     return {
         "num_regs": a.num_regs,
         "shared_size_bytes": a.shared_size_bytes + a.dynamic_smem_bytes,
@@ -263,3 +260,19 @@ def kernel_attrs(engine: str, d: int, k: int) -> dict:
         "block_threads": a.block_threads,
         "dynamic_smem_bytes": a.dynamic_smem_bytes,
     }
+
+
+def kernel_attrs(engine: str, d: int, k: int) -> dict:
+    """Attributes of the main kernel an engine launches for (d, k)."""
+    a = _lib.Attrs()
+    _lib.check(_lib.load().bfk_kernel_attrs(_lib.ENGINES[engine], d, k, ctypes.byref(a)),
+               "bfk_kernel_attrs")
+    return _attrs_dict(a)
+
+
+def merge_attrs(lists: int, k: int) -> dict:
+    """Attributes of the kernel ``merge`` launches for ``lists`` lists of k."""
+    a = _lib.Attrs()
+    _lib.check(_lib.load().bfk_merge_attrs(int(lists), int(k), ctypes.byref(a)),
+               "bfk_merge_attrs")
+    return _attrs_dict(a)

@@ -187,6 +187,14 @@ BFK_API bfk_status_t bfk_merge(const float *cand_dists, const int32_t *cand_ids,
 BFK_API bfk_status_t bfk_kernel_attrs(int32_t engine, int32_t d, int32_t k, bfk_attrs_t *out);
 
 /*
+ * Attributes of the kernel bfk_merge launches for `lists` sorted lists of k per
+ * query (the rank merge for a few lists, the sorting network for many).  Replaces
+ * kernel_attrs of bf_fp32_tiled_merge / bf_fp32_qgroup_merge, which the reference
+ * runners report (bf/fp32_tiled.py:229-239, bf/fp32_qgroup.py:279-291).
+ */
+BFK_API bfk_status_t bfk_merge_attrs(int32_t lists, int32_t k, bfk_attrs_t *out);
+
+/*
  * Statistics of the last bfk_search that used this workspace (synchronises
  * `stream`); also returns and resets the main-kernel times this thread
  * recorded with BFK_FLAG_TIME_MAIN.  No reference counterpart.
@@ -202,12 +210,13 @@ BFK_API bfk_status_t bfk_search_stats(const void *workspace, int64_t n, int64_t 
  *
  * It takes no workspace: its scratch is a 16 MiB array inside the library that
  * every GPU loading the library holds until exit.  Requires
- * 16 * n * k <= 16 MiB - 256 bytes (n * k <= 1,048,560); larger shapes return
+ * 16 * n * k <= 16 MiB (n * k <= 1,048,576); larger shapes return
  * BFK_ERR_UNSUPPORTED.  It allocates nothing.  The first call on each device
- * looks the array's device address up (cudaGetSymbolAddress); make that first
- * call outside any stream capture.  All calls share the array: calls that
- * overlap on the GPU (other streams or threads) race and must be serialised by
- * the caller.
+ * looks the array's device address up (cudaGetSymbolAddress) and keeps it for
+ * the life of the process; make that first call outside any stream capture, and
+ * do not call cudaDeviceReset between calls (the kept address would be stale).
+ * All calls share the array: calls that overlap on the GPU (other streams or
+ * threads) race and must be serialised by the caller.
  */
 BFK_API bfk_status_t bfk_search_noalloc(const float *Q, int64_t n, const float *X, int64_t m,
                                         int32_t d, int32_t k, int64_t id_offset,

@@ -18,7 +18,8 @@ Only the GPU-side oracle pin (tests marked ``gpu``) loads these libraries,
 to check the C oracle against the reference's real kernels.  Generated
 sources stay under ``oracle/_ref/``; nothing of the reference is committed.
 
-    python oracle/build_ref.py [--ref /path/to/reference]
+    python oracle/build_ref.py --ref /path/to/reference
+    GPU_ALGO_REFERENCE=/path/to/reference python oracle/build_ref.py
 """
 from __future__ import annotations
 
@@ -32,7 +33,13 @@ import types
 
 HERE = os.path.dirname(os.path.abspath(__file__))
 OUT = os.path.join(HERE, "_ref")
-DEFAULT_REF = "/root/reference"
+# where the reference checkout is: --ref, or this environment variable
+REF_ENV = "GPU_ALGO_REFERENCE"
+
+
+def reference_dir() -> str | None:
+    """The reference checkout named by the environment, if any."""
+    return os.environ.get(REF_ENV) or None
 
 # (instance name, module, source constant, kernel name, K, D, block) -- block as the
 # reference runner would choose it (bf/fp32.py:212-221) for these shapes.
@@ -95,7 +102,7 @@ def load_reference_sources(ref: str) -> dict:
                 sys.modules[k] = v
 
 
-def build(ref: str = DEFAULT_REF, force: bool = False) -> list[str]:
+def build(ref: str, force: bool = False) -> list[str]:
     if not os.path.isdir(os.path.join(ref, "bf")):
         raise FileNotFoundError(f"reference checkout not found at {ref}")
     os.makedirs(OUT, exist_ok=True)
@@ -126,9 +133,12 @@ def build(ref: str = DEFAULT_REF, force: bool = False) -> list[str]:
 
 def main(argv=None) -> int:
     ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
-    ap.add_argument("--ref", default=DEFAULT_REF)
+    ap.add_argument("--ref", default=reference_dir(),
+                    help=f"reference checkout (default: ${REF_ENV})")
     ap.add_argument("--force", action="store_true")
     a = ap.parse_args(argv)
+    if not a.ref:
+        ap.error(f"name the reference checkout with --ref or ${REF_ENV}")
     for p in build(a.ref, a.force):
         print(p)
     return 0

@@ -1,6 +1,6 @@
 """Generate tests/golden/block_choices.json from the reference's own heuristics.
 
-    python tests/golden/make_block_choices.py [path to the reference checkout]
+    python tests/golden/make_block_choices.py <path to the reference checkout>
 
 The reference's `choose_block` (bf/fp32.py:212-221) and `choose_qgroup_block`
 (bf/fp32_qgroup.py:217-225) are public helpers that callers report; this package
@@ -24,7 +24,11 @@ QPBS = (1, 2, 4, 8, 16)
 
 
 def main(argv: list[str]) -> int:
-    ref = argv[1] if len(argv) > 1 else "/root/reference"
+    ref = argv[1] if len(argv) > 1 else os.environ.get("GPU_ALGO_REFERENCE")
+    if not ref:
+        print("usage: make_block_choices.py <reference checkout> (or $GPU_ALGO_REFERENCE)",
+              file=sys.stderr)
+        return 2
     sys.modules.setdefault("cupy", types.ModuleType("cupy"))
     sys.path.insert(0, ref)
     fp32 = importlib.import_module("bf.fp32")

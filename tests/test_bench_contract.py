@@ -26,7 +26,10 @@ def test_reference_arm_prints_one_contract_line():
     assert j["metric"] == "queries/sec, exact FP32 k-NN" and j["unit"] == "queries/s"
     assert j["value"] > 0 and j["ms_per_step"] > 0 and j["higher_is_better"] is True
     assert (j["steps"], j["warmup"], j["n_gpus"]) == (2, 1, 1)
-    assert j["config"] == {"workload": "plumbing", "N": 65_536, "Q": 1_024, "d": 128, "k": 10}
+    # the same config dict the repository arm prints for this run
+    assert j["config"] == {"workload": "plumbing", "N": 65_536, "Q": 1_024, "d": 128, "k": 10,
+                           "parallelism": "rowshard1", "rows_prepared_once": False,
+                           "l2": "inputs larger than L2 (database 0.03 GB), no flush"}
     cb = j["cpu_baseline"]
     assert cb["kind"] == "port" and cb["cores"] >= 1 and cb["value"] == j["value"]
     assert "8 queries" in cb["sample"]

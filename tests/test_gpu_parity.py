@@ -278,6 +278,14 @@ def test_bf_dropin_runners(plumbing):
         assert res["ms"] > 0 and res["block"] > 0
     r = fp32_tiled.run_bf_fp32_tiled(Qd, Xd, 10, tile_size=20_000, reps=1)
     assert r["n_tiles"] == 4 and r["tile_size"] == 20_000
+    # the merge the tiled runner reports is the merge kernel that ran: 4 lists of 10
+    # go through the rank merge, whose shared memory is the lists' keys
+    assert r["merge_shared_mem_bytes"] == 4 * 10 * 8
+    assert r["merge_kernel_attrs"]["num_regs"] > 0
+    assert r["merge_kernel_attrs"]["kernel_variant"] == "merge of 4 lists"
+    assert r["merge_kernel_attrs"] != r["partial_kernel_attrs"]
+    g = fp32_qgroup.run_bf_fp32_qgroup(Qd, Xd, 10, qpb=8, reps=1)
+    assert "qpb_note" in g
     fn, out_ids, out_dists, block, smem, attrs = fp32.build_bf_fp32_runner(Qd, Xd, 10)
     fn()
     torch.cuda.synchronize()

@@ -58,6 +58,11 @@ def test_argument_validation_without_gpu(lib):
     # invalid arguments are rejected before any device work
     assert lib.bfk_search(None, 4, None, 4, 8, 1, 0, None, None, None, 0, None, None) == 1
     assert lib.bfk_merge(None, None, 4, 0, 1, None, None, None) == 1
+    a = _lib.Attrs()
+    assert lib.bfk_merge_attrs(0, 10, ctypes.byref(a)) == 1
+    assert lib.bfk_merge_attrs(4, 0, ctypes.byref(a)) == 1
+    assert lib.bfk_merge_attrs(4, 10, None) == 1
+    assert lib.bfk_merge_attrs(4, 5000, ctypes.byref(a)) == 2
 
 
 def test_workspace_has_room_for_partials(lib):
