@@ -38,6 +38,8 @@ EXPORTS = (
     "bfk_merge",
     "bfk_kernel_attrs",
     "bfk_merge_attrs",
+    "bfk_filter_values_workspace",
+    "bfk_filter_values",
     "bfk_search_stats",
     "bfk_search_noalloc",
     "bfk_prepared_size",
@@ -121,6 +123,10 @@ def load() -> ctypes.CDLL:
         lib.bfk_kernel_attrs.argtypes = [i32, i32, i32, ctypes.POINTER(Attrs)]
         lib.bfk_merge_attrs.restype = i32
         lib.bfk_merge_attrs.argtypes = [i32, i32, ctypes.POINTER(Attrs)]
+        lib.bfk_filter_values_workspace.restype = i32
+        lib.bfk_filter_values_workspace.argtypes = [i64, i64, i32, ctypes.POINTER(u64)]
+        lib.bfk_filter_values.restype = i32
+        lib.bfk_filter_values.argtypes = [vp, i64, vp, i64, i32, vp, vp, i32p, vp, u64, vp]
         lib.bfk_prepared_size.restype = i32
         lib.bfk_prepared_size.argtypes = [i64, i32, ctypes.POINTER(u64)]
         lib.bfk_prepare.restype = i32

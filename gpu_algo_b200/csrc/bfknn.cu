@@ -14,6 +14,7 @@ namespace {
 
 constexpr int kMaxK = 1024;
 constexpr int kMaxD = 4096;
+constexpr int64_t kMaxAuditPairs = (int64_t)1 << 28;  // bfk_filter_values: (query, row) pairs
 
 size_t align256(size_t x) { return (x + 255) & ~(size_t)255; }
 
@@ -351,6 +352,42 @@ bfk_status_t bfk_prepare(const float *X, int64_t m, int32_t d, void *prepared, u
   if (s != BFK_OK) return s;
   return tc_prepare(X, m, d, prepared, reinterpret_cast<cudaStream_t>(stream)) == 0 ? BFK_OK
                                                                                     : BFK_ERR_CUDA;
+}
+
+bfk_status_t bfk_filter_values_workspace(int64_t n, int64_t m, int32_t d, uint64_t *bytes) {
+  if (!bytes || n <= 0 || m <= 0 || d <= 0) return BFK_ERR_INVALID_ARGUMENT;
+  if (n > INT32_MAX || m > INT32_MAX || n * m > kMaxAuditPairs || !tc_supported(d, 1))
+    return BFK_ERR_UNSUPPORTED;
+  TcPlan p;
+  if (!tc_make_values_plan(n, m, d, &p)) return BFK_ERR_UNSUPPORTED;
+  *bytes = p.total;
+  return BFK_OK;
+}
+
+bfk_status_t bfk_filter_values(const float *Q, int64_t n, const float *X, int64_t m, int32_t d,
+                               float *out_v, float *out_qinfo, int32_t *exact_only,
+                               void *workspace, uint64_t workspace_bytes, void *stream) {
+  uint64_t need = 0;
+  const bfk_status_t s = bfk_filter_values_workspace(n, m, d, &need);
+  if (s != BFK_OK) return s;
+  if (!Q || !X || !out_v || !out_qinfo || !exact_only || !workspace)
+    return BFK_ERR_INVALID_ARGUMENT;
+  if ((reinterpret_cast<uintptr_t>(Q) | reinterpret_cast<uintptr_t>(X) |
+       reinterpret_cast<uintptr_t>(out_v) | reinterpret_cast<uintptr_t>(out_qinfo)) & 3u)
+    return BFK_ERR_INVALID_ARGUMENT;
+  if ((reinterpret_cast<uintptr_t>(workspace) & 255u) || workspace_bytes < need)
+    return BFK_ERR_WORKSPACE;
+  const bfk_status_t dev = check_device();
+  if (dev != BFK_OK) return dev;
+  TcPlan p;
+  tc_make_values_plan(n, m, d, &p);
+  int eo = 0;
+  const int rc = tc_filter_values(Q, X, out_v, out_qinfo, &eo, workspace, p,
+                                  reinterpret_cast<cudaStream_t>(stream));
+  if (rc == 1) return BFK_ERR_CUDA;
+  if (rc == 2) return BFK_ERR_DEVICE_TIMEOUT;
+  *exact_only = eo;
+  return BFK_OK;
 }
 
 bfk_status_t bfk_merge(const float *cand_dists, const int32_t *cand_ids, int64_t n,

@@ -97,6 +97,13 @@ int tc_run(const float *Q, const float *X, int64_t id_offset, float *out_d, int3
            void *ws, const TcPlan &p, cudaStream_t stream, cudaEvent_t t0, cudaEvent_t t1,
            int *launches, LevelHook hook, void *hook_user, int shards,
            const void *prepared = nullptr);
+// The filter value of every (query, row) pair (margin audit, test infrastructure):
+// a one-level plan whose regions hold every column, and the run that fills out_v
+// (n, m) (NaN where no value was reported) and out_qinfo (n, 2) (||q||^2 in FP32,
+// margin).  Returns 0 ok, 1 CUDA error, 2 device timeout.
+bool tc_make_values_plan(int64_t n, int64_t m, int d, TcPlan *p);
+int tc_filter_values(const float *Q, const float *X, float *out_v, float *out_qinfo,
+                     int *exact_only, void *ws, const TcPlan &p, cudaStream_t stream);
 const void *tc_kernel_ptr(int d, int k);
 size_t tc_smem_bytes(int d, int k);
 int tc_threads();

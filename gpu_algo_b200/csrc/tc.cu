@@ -1558,6 +1558,33 @@ static int choose_slices(int q_tiles, int64_t tiles, int sms, int max_s) {
   return best;
 }
 
+// Workspace offsets of a plan (its sizes set): every array 256-byte aligned.
+static void layout_workspace(TcPlan &P) {
+  const int64_t n = P.n, m = P.m;
+  const int d = P.d, k = P.k, max_s = P.max_slices;
+  const bool prepared = P.prepared;
+  const int64_t q_rows = (int64_t)P.q_tiles * kBM;
+  size_t off = sizeof(WsHeader);
+  // the row arrays live in the workspace unless a prepared buffer holds them
+  const size_t rows_f = prepared ? 0 : 1;
+  P.off_xh = off;       off = al256(off + rows_f * (size_t)m * P.d_pad * 2);
+  P.off_xnorm = off;    off = al256(off + rows_f * (size_t)P.x_tiles * kBN * 4);
+  P.off_xscale = off;   off = al256(off + rows_f * (size_t)P.x_tiles * kColGroups * 4);
+  P.off_invsq = off;    off = al256(off + 16);
+  P.off_qh = off;       off = al256(off + (size_t)q_rows * P.d_pad * 2);
+  P.off_qinfo = off;    off = al256(off + (size_t)q_rows * 8);
+  P.off_rlev = off;     off = al256(off + (size_t)n * 8);  // two bounds per query
+  P.off_cand = off;     off = al256(off + (size_t)n * P.cand_cap * 8);
+  P.off_ccount = off;   off = al256(off + (size_t)n * kColGroups * max_s * 4);
+  P.off_flags = off;    off = al256(off + (size_t)n * 4);
+  P.off_fbq = off;      off = al256(off + (size_t)n * d * 4);
+  P.off_fbd = off;      off = al256(off + (size_t)n * k * 4);
+  P.off_fbi = off;      off = al256(off + (size_t)n * k * 4);
+  P.off_fbpart_d = off; off = al256(off + (size_t)P.fb_slices * n * k * 4);
+  P.off_fbpart_i = off; off = al256(off + (size_t)P.fb_slices * n * k * 4);
+  P.total = off;
+}
+
 bool tc_make_plan(int64_t n, int64_t m, int d, int k, int slices, int pool, bool pair,
                   int64_t plan_rows, bool prepared, TcPlan *p) {
   if (!tc_supported(d, k) || n <= 0 || m <= 0) return false;
@@ -1627,27 +1654,8 @@ bool tc_make_plan(int64_t n, int64_t m, int d, int k, int slices, int pool, bool
   P.fb_slices = (int)((m + 262143) / 262144);
   if (P.fb_slices > 32) P.fb_slices = 32;
   if (P.fb_slices < 1) P.fb_slices = 1;
-  const int64_t q_rows = (int64_t)P.q_tiles * kBM;
-  size_t off = sizeof(WsHeader);
-  // the row arrays live in the workspace unless a prepared buffer holds them
   P.prepared = prepared;
-  const size_t rows_f = prepared ? 0 : 1;
-  P.off_xh = off;       off = al256(off + rows_f * (size_t)m * P.d_pad * 2);
-  P.off_xnorm = off;    off = al256(off + rows_f * (size_t)P.x_tiles * kBN * 4);
-  P.off_xscale = off;   off = al256(off + rows_f * (size_t)P.x_tiles * kColGroups * 4);
-  P.off_invsq = off;    off = al256(off + 16);
-  P.off_qh = off;       off = al256(off + (size_t)q_rows * P.d_pad * 2);
-  P.off_qinfo = off;    off = al256(off + (size_t)q_rows * 8);
-  P.off_rlev = off;     off = al256(off + (size_t)n * 8);  // two bounds per query
-  P.off_cand = off;     off = al256(off + (size_t)n * P.cand_cap * 8);
-  P.off_ccount = off;   off = al256(off + (size_t)n * kColGroups * max_s * 4);
-  P.off_flags = off;    off = al256(off + (size_t)n * 4);
-  P.off_fbq = off;      off = al256(off + (size_t)n * d * 4);
-  P.off_fbd = off;      off = al256(off + (size_t)n * k * 4);
-  P.off_fbi = off;      off = al256(off + (size_t)n * k * 4);
-  P.off_fbpart_d = off; off = al256(off + (size_t)P.fb_slices * n * k * 4);
-  P.off_fbpart_i = off; off = al256(off + (size_t)P.fb_slices * n * k * 4);
-  P.total = off;
+  layout_workspace(P);
   *p = P;
   return true;
 }
@@ -1976,6 +1984,131 @@ int tc_run(const float *Q, const float *X, int64_t id_offset, float *out_d, int3
   }
   *launches = nl;
   return 0;
+#undef BFK_TRY
+}
+
+// ---------------------------------------------------------------------------
+// The filter value v of every (query, row) pair, for the margin audit (test
+// infrastructure).  One level reads every tile with no bound, so the filter's
+// first-level path appends every finite v; regions hold a slice's every column.
+// ---------------------------------------------------------------------------
+__global__ void tc_scatter_values(const uint2 *__restrict__ cand, const int *__restrict__ ccount,
+                                  int64_t m, int pool, int region, int nreg, int stride,
+                                  float *__restrict__ out_v) {
+  const int64_t q = blockIdx.x;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nw = blockDim.x >> 5;
+  for (int rg = warp; rg < nreg; rg += nw) {
+    const int c = min(ccount[(size_t)q * stride + rg], region);
+    const uint2 *src = cand + (size_t)q * pool + (size_t)rg * region;
+    for (int e = lane; e < c; e += 32) {
+      const uint2 ent = src[e];
+      if (ent.x < (uint64_t)m) out_v[q * m + ent.x] = __uint_as_float(ent.y);
+    }
+  }
+}
+
+bool tc_make_values_plan(int64_t n, int64_t m, int d, TcPlan *p) {
+  if (!tc_supported(d, 1) || n <= 0 || m <= 0) return false;
+  TcPlan P{};
+  P.n = n;
+  P.m = m;
+  P.d = d;
+  P.k = 1;
+  P.d_pad = kch_for(d) * kBK;
+  P.q_tiles = (int)((n + kBM - 1) / kBM);
+  P.x_tiles = (m + kBN - 1) / kBN;
+  P.levels = 1;
+  LevelPlan &lv = P.level[0];
+  lv.tiles = P.x_tiles;
+  int s = choose_slices(P.q_tiles, lv.tiles, num_sms(), 64);
+  if (s > lv.tiles) s = (int)lv.tiles;
+  lv.tiles_per_slice = (lv.tiles + s - 1) / s;
+  lv.slices = (int)((lv.tiles + lv.tiles_per_slice - 1) / lv.tiles_per_slice);
+  lv.region = (int)(lv.tiles_per_slice * kGroupN);  // a column group's every column
+  P.cand_cap = lv.slices * kColGroups * lv.region;
+  P.max_slices = lv.slices;
+  P.slices = lv.slices;
+  P.tiles_per_slice = lv.tiles_per_slice;
+  P.fb_slices = 1;
+  P.prepared = false;
+  layout_workspace(P);
+  *p = P;
+  return true;
+}
+
+int tc_filter_values(const float *Q, const float *X, float *out_v, float *out_qinfo,
+                     int *exact_only, void *ws_, const TcPlan &p, cudaStream_t stream) {
+  unsigned char *ws = static_cast<unsigned char *>(ws_);
+  WsHeader *hdr = reinterpret_cast<WsHeader *>(ws);
+  __half *Xh = reinterpret_cast<__half *>(ws + p.off_xh);
+  float *xnorm = reinterpret_cast<float *>(ws + p.off_xnorm);
+  float *xinv = reinterpret_cast<float *>(ws + p.off_xscale);
+  float *inv_sq = reinterpret_cast<float *>(ws + p.off_invsq);
+  __half *Qh = reinterpret_cast<__half *>(ws + p.off_qh);
+  float2 *qinfo = reinterpret_cast<float2 *>(ws + p.off_qinfo);
+  uint2 *cand = reinterpret_cast<uint2 *>(ws + p.off_cand);
+  int *ccount = reinterpret_cast<int *>(ws + p.off_ccount);
+  const int64_t q_rows = (int64_t)p.q_tiles * kBM;
+  const LevelPlan &lv = p.level[0];
+#define BFK_TRY(x)                         \
+  do {                                     \
+    const cudaError_t e_ = (x);            \
+    if (e_ != cudaSuccess) {               \
+      BFK_NOTE(e_, #x);                    \
+      return 1;                            \
+    }                                      \
+  } while (0)
+  BFK_TRY(cudaMemsetAsync(hdr, 0, sizeof(WsHeader), stream));
+  // NaN (all bits set) marks a pair the filter did not report
+  BFK_TRY(cudaMemsetAsync(out_v, 0xff, (size_t)p.n * p.m * sizeof(float), stream));
+  tc_qmax_kernel<<<592, 256, 0, stream>>>(Q, p.n * p.d, hdr);
+  launch_prep_rows(X, p.m, p.d, p.d_pad, p.x_tiles, Xh, xnorm, xinv, hdr, stream);
+  tc_prep_q_kernel<<<(unsigned)(q_rows / 8), 256, 0, stream>>>(Q, p.n, p.d, p.d_pad, q_rows, Qh,
+                                                                qinfo, inv_sq, hdr);
+  BFK_TRY(cudaGetLastError());
+  CUtensorMap tq, tx;
+  if (!make_tmap(&tq, Qh, q_rows, p.d_pad, kBM) || !make_tmap(&tx, Xh, p.m, p.d_pad, kBN)) {
+    BFK_NOTE(cudaErrorInvalidValue, "cuTensorMapEncodeTiled");
+    return 1;
+  }
+  const int kch = p.d_pad / kBK;
+  const size_t smem = tc_layout(kch, false).total;
+  BFK_TRY(cudaFuncSetAttribute((const void *)knn_tc_filter_kernel<false>,
+                               cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+  FilterArgs A{};
+  A.xnorm = xnorm;
+  A.xinv = xinv;
+  A.qinfo = qinfo;
+  A.inv_sq = inv_sq;
+  A.r_in = nullptr;  // no bound: every finite v is appended
+  A.two_bounds = false;
+  A.n = p.n;
+  A.x_tiles = p.x_tiles;
+  A.level_tiles = lv.tiles;
+  A.q_tiles = p.q_tiles;
+  A.slices = lv.slices;
+  A.tiles_per_slice = (int)lv.tiles_per_slice;
+  A.region = lv.region;
+  A.pool = p.cand_cap;
+  A.max_slices = p.max_slices;
+  A.cand = cand;
+  A.ccount = ccount;
+  A.hdr = hdr;
+  knn_tc_filter_kernel<false><<<(unsigned)(p.q_tiles * lv.slices), kTcThreads, smem, stream>>>(
+      tq, tx, A, kch);
+  BFK_TRY(cudaGetLastError());
+  tc_scatter_values<<<(unsigned)p.n, 256, 0, stream>>>(cand, ccount, p.m, p.cand_cap, lv.region,
+                                                       kColGroups * lv.slices,
+                                                       kColGroups * p.max_slices, out_v);
+  BFK_TRY(cudaGetLastError());
+  // (||q||^2, margin) of each query: the first n float2 of qinfo
+  BFK_TRY(cudaMemcpyAsync(out_qinfo, qinfo, (size_t)p.n * sizeof(float2),
+                          cudaMemcpyDeviceToDevice, stream));
+  WsHeader h;
+  BFK_TRY(cudaMemcpyAsync(&h, hdr, sizeof(h), cudaMemcpyDeviceToHost, stream));
+  BFK_TRY(cudaStreamSynchronize(stream));
+  *exact_only = h.exact_only;
+  return h.error ? 2 : 0;
 #undef BFK_TRY
 }
 

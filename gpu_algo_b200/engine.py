@@ -276,3 +276,33 @@ def merge_attrs(lists: int, k: int) -> dict:
     _lib.check(_lib.load().bfk_merge_attrs(int(lists), int(k), ctypes.byref(a)),
                "bfk_merge_attrs")
     return _attrs_dict(a)
+
+
+def filter_values(Q, X) -> tuple[torch.Tensor, torch.Tensor, bool]:
+    """The tensor-core filter's value of every (query, row) pair (``bfk_filter_values``).
+
+    Returns (v (n, m), qinfo (n, 2) = (||q||^2 in FP32, margin), exact_only), v as the
+    filter computes ||x||^2 - 2 q.x, NaN where it reported none.  Test infrastructure
+    for the engine's error margin: every pair must satisfy
+    |(||q||^2 + v) - D| <= margin, D the reference distance."""
+    Q = as_device_f32(Q, "Q")
+    X = as_device_f32(X, "X")
+    n, d = Q.shape
+    m = X.shape[0]
+    if X.shape[1] != d:
+        raise ValueError(f"Q has d={d} but X has d={X.shape[1]}")
+    lib = _lib.load()
+    nb = ctypes.c_uint64()
+    _lib.check(lib.bfk_filter_values_workspace(n, m, d, ctypes.byref(nb)),
+               "bfk_filter_values_workspace")
+    with torch.cuda.device(Q.device):
+        stream = torch.cuda.current_stream()
+        ws = torch.empty(int(nb.value), dtype=torch.uint8, device=Q.device)
+        v = torch.empty((n, m), dtype=torch.float32, device=Q.device)
+        qinfo = torch.empty((n, 2), dtype=torch.float32, device=Q.device)
+        eo = ctypes.c_int32()
+        _lib.check(lib.bfk_filter_values(Q.data_ptr(), n, X.data_ptr(), m, d, v.data_ptr(),
+                                         qinfo.data_ptr(), ctypes.byref(eo), ws.data_ptr(),
+                                         ws.numel(), ctypes.c_void_p(stream.cuda_stream)),
+                   "bfk_filter_values")
+    return v, qinfo, bool(eo.value)

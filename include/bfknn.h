@@ -203,6 +203,26 @@ BFK_API bfk_status_t bfk_search_stats(const void *workspace, int64_t n, int64_t 
                               const bfk_opts_t *opts, void *stream, bfk_stats_t *out);
 
 /*
+ * Test infrastructure for the tensor-core engine's error margin.  No reference
+ * counterpart.  Runs the engine's preparation and one filter pass over every row
+ * with no bound, and reports the filter value v of every (query, row) pair:
+ *   out_v      (n, m) float32  v = ||x||^2 - 2 q.x as the filter computes it
+ *                              (NaN where the filter reported none: v not finite);
+ *   out_qinfo  (n, 2) float32  ||q||^2 in FP32 and the query's margin m_q;
+ *   exact_only                 nonzero when the inputs fall outside what the margin
+ *                              covers (a search would use the exact SIMT engine).
+ * The engine's exactness rests on |(||q||^2 + v) - D| <= m_q for every pair, D the
+ * reference distance (bf/fp32.py:74-82); tests check it against the oracle.
+ * Requires n * m <= 2^28.  Synchronises `stream`.
+ */
+BFK_API bfk_status_t bfk_filter_values_workspace(int64_t n, int64_t m, int32_t d,
+                                                 uint64_t *bytes);
+BFK_API bfk_status_t bfk_filter_values(const float *Q, int64_t n, const float *X, int64_t m,
+                                       int32_t d, float *out_v, float *out_qinfo,
+                                       int32_t *exact_only, void *workspace,
+                                       uint64_t workspace_bytes, void *stream);
+
+/*
  * Exact k-NN like bfk_search (exact SIMT engine) for callers that cannot
  * allocate device memory at search time (inside another allocator's callback,
  * on a real-time thread that must not block on cudaMalloc, or with only fixed
