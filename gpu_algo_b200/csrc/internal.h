@@ -64,11 +64,12 @@ struct TcPlan {
 // A prepared database (bfk_prepare): the TC engine's row arrays for one X, made once.
 // Layout, every part 256-byte aligned: a 256-byte status block (the rows' norm bound and
 // exact-only flag, set for a non-finite row, as the workspace header holds them), a 256-byte description
-// (PreparedInfo), the f16 rows (m, d_pad), ||x||^2 (x_tiles * 256) and the inverse scale
-// of every 64-row group (x_tiles * 4).
+// (PreparedInfo), the f16 rows (m, d_pad), ||x||^2 (x_tiles * 256) and a 32-byte record
+// of every 64-row group (x_tiles * 4): the minimum ||x||^2 of each of its 16-row chunks,
+// then its scale and the scale's inverse.
 struct PreparedInfo {
-  char magic[8];     // "BFKPREP1"
-  int32_t version;   // 1
+  char magic[8];     // "BFKPREP2"
+  int32_t version;   // 2
   int32_t d;
   int64_t m;
   int32_t d_pad;
@@ -77,7 +78,7 @@ struct PreparedInfo {
   uint64_t total;    // bytes of the whole buffer
 };
 struct PreparedLayout {
-  size_t off_status, off_info, off_xh, off_xnorm, off_xinv, total;
+  size_t off_status, off_info, off_xh, off_xnorm, off_xmeta, total;
 };
 PreparedLayout tc_prepared_layout(int64_t m, int d);
 // Fills `prep` from X on `stream` and waits for it; 0 ok, 1 CUDA error.

@@ -64,7 +64,8 @@ constexpr int kMinLevelTarget = 256;
 
 struct FilterArgs {
   const float *xnorm;    // (x_tiles*256) ||x||^2, +inf past m
-  const float *xinv;     // (x_tiles * 4) 1/scale of each 64-row group
+  const float4 *xmeta;   // (x_tiles * 4) groups of 64 rows, two float4 each: the minimum
+                         // ||x||^2 of each 16-row chunk, then (1/scale, scale, 0, 0)
   const float2 *qinfo;   // (q_tiles*128) (||q||^2, 2*margin); NaN margin for padding rows
   const float *inv_sq;   // 1/scale of the queries (device scalar)
   const float *r_in;     // (n) bound B of the previous level (B + margin), null = none
@@ -140,19 +141,34 @@ __device__ __forceinline__ float max3f(float a, float b, float c) {
   asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
   return d;
 }
-// v[i] for a lane-varying i in [0, 8), by selects (no local-memory indexing)
-__device__ __forceinline__ float pick8(const float *v, int i) {
-  const bool b0 = i & 1, b1 = i & 2, b2 = i & 4;
-  const float s0 = b0 ? v[1] : v[0], s1 = b0 ? v[3] : v[2];
-  const float s2 = b0 ? v[5] : v[4], s3 = b0 ? v[7] : v[6];
-  const float t0 = b1 ? s1 : s0, t1 = b1 ? s3 : s2;
-  return b2 ? t1 : t0;
+// v[i] for a lane-varying i in [0, 16), by selects (no local-memory indexing)
+__device__ __forceinline__ float pick16(const float *v, int i) {
+  const bool b0 = i & 1, b1 = i & 2, b2 = i & 4, b3 = i & 8;
+  float s[8], t[4], u[2];
+#pragma unroll
+  for (int j = 0; j < 8; j++) s[j] = b0 ? v[2 * j + 1] : v[2 * j];
+#pragma unroll
+  for (int j = 0; j < 4; j++) t[j] = b1 ? s[2 * j + 1] : s[2 * j];
+  u[0] = b2 ? t[1] : t[0];
+  u[1] = b2 ? t[3] : t[2];
+  return b3 ? u[1] : u[0];
 }
-// maximum of 8 accumulator values (FP32 bit patterns)
-__device__ __forceinline__ float max8u(const uint32_t *a) {
-  return max3f(max3f(__uint_as_float(a[0]), __uint_as_float(a[1]), __uint_as_float(a[2])),
-               max3f(__uint_as_float(a[3]), __uint_as_float(a[4]), __uint_as_float(a[5])),
-               fmaxf(__uint_as_float(a[6]), __uint_as_float(a[7])));
+// maximum of 16 accumulator values (FP32 bit patterns), three-input max.f32
+__device__ __forceinline__ float max16u(const uint32_t *a) {
+  const float m0 = max3f(__uint_as_float(a[0]), __uint_as_float(a[1]), __uint_as_float(a[2]));
+  const float m1 = max3f(__uint_as_float(a[3]), __uint_as_float(a[4]), __uint_as_float(a[5]));
+  const float m2 = max3f(__uint_as_float(a[6]), __uint_as_float(a[7]), __uint_as_float(a[8]));
+  const float m3 = max3f(__uint_as_float(a[9]), __uint_as_float(a[10]), __uint_as_float(a[11]));
+  const float m4 = max3f(__uint_as_float(a[12]), __uint_as_float(a[13]), __uint_as_float(a[14]));
+  return fmaxf(max3f(m0, m1, m2), max3f(m3, m4, __uint_as_float(a[15])));
+}
+// the filter values of 8 columns: v = fma(c, acc, ||x||^2), one rounding each
+__device__ __forceinline__ void exact_v8(const uint32_t *acc, float c, float4 n0, float4 n1,
+                                         float *v) {
+  fma2(__uint_as_float(acc[0]), __uint_as_float(acc[1]), c, n0.x, n0.y, v[0], v[1]);
+  fma2(__uint_as_float(acc[2]), __uint_as_float(acc[3]), c, n0.z, n0.w, v[2], v[3]);
+  fma2(__uint_as_float(acc[4]), __uint_as_float(acc[5]), c, n1.x, n1.y, v[4], v[5]);
+  fma2(__uint_as_float(acc[6]), __uint_as_float(acc[7]), c, n1.z, n1.w, v[6], v[7]);
 }
 
 // the bound a level select wrote for query q (both halves when the shards share them)
@@ -165,14 +181,15 @@ __device__ __forceinline__ float read_bound(const float *r, int64_t n, int64_t q
 // database, every tile for the full level.  A walk steps j by one with the
 // quotient and remainder of x_tiles / level_tiles (one division per walk).
 struct TileWalk {
-  int64_t tile, rem, q, r, div;
+  uint32_t tile, rem, q, r, div;  // tiles < 2^23 (m <= 2^31 rows)
   __device__ __forceinline__ TileWalk(const FilterArgs &a, int64_t j) {
-    div = a.level_tiles;
-    q = a.x_tiles / div;
-    r = a.x_tiles - q * div;
+    div = (uint32_t)a.level_tiles;
+    q = (uint32_t)(a.x_tiles / a.level_tiles);
+    r = (uint32_t)(a.x_tiles - (int64_t)q * a.level_tiles);
     const int64_t p = j * a.x_tiles;
-    tile = p / div;
-    rem = p - tile * div;
+    const int64_t t = p / a.level_tiles;
+    tile = (uint32_t)t;
+    rem = (uint32_t)(p - t * a.level_tiles);
   }
   __device__ __forceinline__ void next() {
     tile += q;
@@ -363,42 +380,52 @@ __global__ void __maxnreg__(96)
     if (valid)
       theta = a.r_in ? fminf(__fadd_ru(read_bound(a.r_in, a.n, q, a.two_bounds), margin), FLT_MAX)
                      : FLT_MAX;
+    // the next float above theta: a chunk whose bound reaches it holds no v <= theta
+    const float theta2 = theta == -INFINITY ? -INFINITY : nextafterf(theta, INFINITY);
     uint2 *region = a.cand + (size_t)(valid ? q : 0) * a.pool +
                     (size_t)(kColGroups * s + cg) * a.region;
     const int last = a.region - 1;            // a full region keeps overwriting its last slot
     int cnt = 0;
     const uint32_t taddr0 = tmem_base + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(cg * kGroupN);
     const float inv_sq = *a.inv_sq;
+    const float nhsq = -0.5f * __frcp_rn(inv_sq);  // -s_q / 2 (powers of two, exact)
     float *nxw = nxs + e * 2 * kNxStage;      // this warp's ||x||^2 staging, two buffers
-    // prefetch ||x||^2 (2 rows per lane) and the block scale of the first tile
+    // prefetch ||x||^2 (2 rows per lane) and the group record of the first tile
     float2 pre_nx = make_float2(0.f, 0.f);
-    float pre_inv = 1.f;
+    float4 pre_gmin = make_float4(0.f, 0.f, 0.f, 0.f), pre_sc = pre_gmin;
     TileWalk walk(a, j_begin);
     if (ntiles > 0) {
-      const int64_t t0 = walk.tile;
-      pre_nx = *reinterpret_cast<const float2 *>(a.xnorm + t0 * kBN + cg * kGroupN + lane * 2);
-      pre_inv = a.xinv[t0 * kColGroups + cg];
+      const uint32_t t0 = walk.tile;
+      pre_nx = *reinterpret_cast<const float2 *>(a.xnorm + (size_t)t0 * kBN + cg * kGroupN + lane * 2);
+      pre_gmin = __ldg(a.xmeta + 2 * ((size_t)t0 * kColGroups + cg));
+      pre_sc = __ldg(a.xmeta + 2 * ((size_t)t0 * kColGroups + cg) + 1);
     }
 
     for (int lt = 0; lt < ntiles; lt++) {
       const int b = lt & 1;
-      const int64_t tile = walk.tile;
+      const uint32_t tile = walk.tile;
       walk.next();  // the walk is one tile ahead from here on
-      // a role that gives up sets the abort flag, which ends the bounded wait below
       float *nxt = nxw + b * kNxStage;
       *reinterpret_cast<float2 *>(nxt + lane * 2) = pre_nx;
+      // v = fma(c, acc, ||x||^2) with c = -2 / (s_q s_x), an exact power of two
+      const float cscale = -2.0f * inv_sq * pre_sc.x;
+      // Chunk thresholds: every v of 16-column chunk j exceeds theta when the chunk's
+      // largest accumulator is <= T_j = (theta2 - min ||x||^2) / c, rounded so that
+      // T_j is below the exact quotient (c < 0; 1/c = -s_q s_x / 2, exact when normal).
+      float T[4];
       {
-        // minimum ||x||^2 of each group of 8 columns (lanes 4g .. 4g+3 hold group g)
-        float gm = fminf(pre_nx.x, pre_nx.y);
-        gm = fminf(gm, __shfl_xor_sync(0xffffffffu, gm, 1));
-        gm = fminf(gm, __shfl_xor_sync(0xffffffffu, gm, 2));
-        if ((lane & 3) == 0) nxt[kGroupN + (lane >> 2)] = gm;
+        const float inv_c = nhsq * pre_sc.y;
+        const bool ok = fabsf(inv_c) >= FLT_MIN && fabsf(inv_c) <= FLT_MAX;
+        T[0] = ok ? __fmul_rd(__fsub_ru(theta2, pre_gmin.x), inv_c) : -INFINITY;
+        T[1] = ok ? __fmul_rd(__fsub_ru(theta2, pre_gmin.y), inv_c) : -INFINITY;
+        T[2] = ok ? __fmul_rd(__fsub_ru(theta2, pre_gmin.z), inv_c) : -INFINITY;
+        T[3] = ok ? __fmul_rd(__fsub_ru(theta2, pre_gmin.w), inv_c) : -INFINITY;
       }
-      const float cscale = -2.0f * inv_sq * pre_inv;  // exact power of two, negative
       if (lt + 1 < ntiles) {
-        const int64_t tn = walk.tile;
-        pre_nx = *reinterpret_cast<const float2 *>(a.xnorm + tn * kBN + cg * kGroupN + lane * 2);
-        pre_inv = a.xinv[tn * kColGroups + cg];
+        const uint32_t tn = walk.tile;
+        pre_nx = *reinterpret_cast<const float2 *>(a.xnorm + (size_t)tn * kBN + cg * kGroupN + lane * 2);
+        pre_gmin = __ldg(a.xmeta + 2 * ((size_t)tn * kColGroups + cg));
+        pre_sc = __ldg(a.xmeta + 2 * ((size_t)tn * kColGroups + cg) + 1);
       }
       // tcgen05.ld is warp-collective: the whole warp proceeds or none of it
       const bool got = __all_sync(0xffffffffu, mbar_wait_bounded(acc_full + b, (lt >> 1) & 1,
@@ -408,7 +435,7 @@ __global__ void __maxnreg__(96)
         break;
       }
       tc_fence_after();
-      const uint32_t row0 = (uint32_t)(tile * kBN + cg * kGroupN);
+      const uint32_t row0 = tile * kBN + (uint32_t)(cg * kGroupN);
       // 16 columns at a time; the load of the next 16 is in flight while these are checked
       uint32_t ra[16], rb[16];
       tmem_ld_32x32b_x16(taddr0 + (uint32_t)(b * kBN), ra);
@@ -419,53 +446,36 @@ __global__ void __maxnreg__(96)
         uint32_t (&cur)[16] = (qq & 1) ? rb : ra;
         uint32_t (&nxb)[16] = (qq & 1) ? ra : rb;
         if (qq < 3) tmem_ld_32x32b_x16(taddr0 + (uint32_t)(b * kBN + (qq + 1) * 16), nxb);
+        const float4 *nx4 = reinterpret_cast<const float4 *>(nxt + qq * 16);
+        const uint32_t rg = row0 + (uint32_t)(qq * 16);
         if (all_pass) {
-          const float4 *nx4 = reinterpret_cast<const float4 *>(nxt + qq * 16);
+          // no bound yet: every finite v is kept, one predicated store per column
 #pragma unroll
           for (int g = 0; g < 2; g++) {
-            const uint32_t *acc = cur + 8 * g;
-            const float4 n0 = nx4[2 * g], n1 = nx4[2 * g + 1];
             float v[8];
-            fma2(__uint_as_float(acc[0]), __uint_as_float(acc[1]), cscale, n0.x, n0.y, v[0], v[1]);
-            fma2(__uint_as_float(acc[2]), __uint_as_float(acc[3]), cscale, n0.z, n0.w, v[2], v[3]);
-            fma2(__uint_as_float(acc[4]), __uint_as_float(acc[5]), cscale, n1.x, n1.y, v[4], v[5]);
-            fma2(__uint_as_float(acc[6]), __uint_as_float(acc[7]), cscale, n1.z, n1.w, v[6], v[7]);
-            const uint32_t rg = row0 + qq * 16 + 8 * g;
+            exact_v8(cur + 8 * g, cscale, nx4[2 * g], nx4[2 * g + 1], v);
 #pragma unroll
             for (int i = 0; i < 8; i++) {
               const bool keep = v[i] <= theta;
-              if (keep) region[min(cnt, last)] = make_uint2(rg + i, __float_as_uint(v[i]));
+              if (keep) region[min(cnt, last)] = make_uint2(rg + 8 * g + i, __float_as_uint(v[i]));
               cnt += keep ? 1 : 0;
             }
           }
         } else {
-          const float2 gn = reinterpret_cast<const float2 *>(nxt + kGroupN)[qq];
-          float gb[2];
-          gb[0] = __fmaf_rn(cscale, max8u(cur), gn.x);
-          gb[1] = __fmaf_rn(cscale, max8u(cur + 8), gn.y);
-          if (__any_sync(0xffffffffu, fminf(gb[0], gb[1]) <= theta)) {
-            const float4 *nx4 = reinterpret_cast<const float4 *>(nxt + qq * 16);
+          // one bound for the chunk: its largest accumulator against T
+          const bool pass = max16u(cur) > T[qq];
+          if (pass) {
+            float v[16];
+            exact_v8(cur, cscale, nx4[0], nx4[1], v);
+            exact_v8(cur + 8, cscale, nx4[2], nx4[3], v + 8);
+            unsigned keep = 0;
 #pragma unroll
-            for (int g = 0; g < 2; g++) {
-              if (__any_sync(0xffffffffu, gb[g] <= theta)) {
-                const uint32_t *acc = cur + 8 * g;
-                const float4 n0 = nx4[2 * g], n1 = nx4[2 * g + 1];
-                float v[8];
-                fma2(__uint_as_float(acc[0]), __uint_as_float(acc[1]), cscale, n0.x, n0.y, v[0], v[1]);
-                fma2(__uint_as_float(acc[2]), __uint_as_float(acc[3]), cscale, n0.z, n0.w, v[2], v[3]);
-                fma2(__uint_as_float(acc[4]), __uint_as_float(acc[5]), cscale, n1.x, n1.y, v[4], v[5]);
-                fma2(__uint_as_float(acc[6]), __uint_as_float(acc[7]), cscale, n1.z, n1.w, v[6], v[7]);
-                unsigned keep = 0;
-#pragma unroll
-                for (int i = 0; i < 8; i++) keep |= (v[i] <= theta ? 1u : 0u) << i;
-                const uint32_t rg = row0 + qq * 16 + 8 * g;
-                while (keep) {
-                  const int i = __ffs(keep) - 1;
-                  keep &= keep - 1;
-                  region[min(cnt, last)] = make_uint2(rg + i, __float_as_uint(pick8(v, i)));
-                  cnt++;
-                }
-              }
+            for (int i = 0; i < 16; i++) keep |= (v[i] <= theta ? 1u : 0u) << i;
+            while (keep) {
+              const int i = __ffs(keep) - 1;
+              keep &= keep - 1;
+              region[min(cnt, last)] = make_uint2(rg + i, __float_as_uint(pick16(v, i)));
+              cnt++;
             }
           }
         }
@@ -519,8 +529,8 @@ template <bool VEC, int W4>
 __global__ void __launch_bounds__(256) tc_prep_x_kernel(const float *__restrict__ X, int64_t m,
                                                         int d, int d_pad, __half *__restrict__ Xh,
                                                         float *__restrict__ xnorm,
-                                                        float *__restrict__ xinv, WsHeader *hdr) {
-  __shared__ float s_max[8], s_rn[8];
+                                                        float4 *__restrict__ xmeta, WsHeader *hdr) {
+  __shared__ float s_max[8], s_rn[8], s_min[8];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int64_t grp = blockIdx.x;
   const int64_t row_base = grp * kScaleRows + warp * 8;
@@ -554,7 +564,7 @@ __global__ void __launch_bounds__(256) tc_prep_x_kernel(const float *__restrict_
       }
     }
   }
-  float wmax = 0.f, wrn = 0.f;
+  float wmax = 0.f, wrn = 0.f, wmin = INFINITY;
   bool bad = false;
 #pragma unroll
   for (int u = 0; u < 8; u++) {
@@ -568,11 +578,12 @@ __global__ void __launch_bounds__(256) tc_prep_x_kernel(const float *__restrict_
       if (!isfinite(ss[u])) bad = true;
       wmax = fmaxf(wmax, mx[u]);
       wrn = fmaxf(wrn, sqrtf(ss[u]));
+      wmin = fminf(wmin, ss[u]);
     }
     // rows past m: v = +inf never passes a finite threshold
     if (lane == u) xnorm[row] = row < m ? ss[u] : INFINITY;
   }
-  if (lane == 0) { s_max[warp] = wmax; s_rn[warp] = wrn; }
+  if (lane == 0) { s_max[warp] = wmax; s_rn[warp] = wrn; s_min[warp] = wmin; }
   if (bad && lane == 0) atomicOr(&hdr->exact_only, 1);
   __syncthreads();
   float gmax = 0.f, rn = 0.f;
@@ -580,7 +591,11 @@ __global__ void __launch_bounds__(256) tc_prep_x_kernel(const float *__restrict_
   for (int w = 0; w < 8; w++) { gmax = fmaxf(gmax, s_max[w]); rn = fmaxf(rn, s_rn[w]); }
   const float sc = pow2_scale_for(gmax);
   if (threadIdx.x == 0) {
-    xinv[grp] = 1.f / sc;
+    // the group's record: min ||x||^2 of each 16-row chunk (warps 2j, 2j+1; +inf for a
+    // chunk of padding rows), then the scale and its inverse
+    xmeta[2 * grp] = make_float4(fminf(s_min[0], s_min[1]), fminf(s_min[2], s_min[3]),
+                                 fminf(s_min[4], s_min[5]), fminf(s_min[6], s_min[7]));
+    xmeta[2 * grp + 1] = make_float4(1.f / sc, sc, 0.f, 0.f);
     // sqrt of an FP32 sum of d squares: (1 + 2^-10) covers its rounding for d <= 4096;
     // the bound only grows, and non-negative floats order like their bit patterns
     if (isfinite(rn)) atomicMax(&hdr->rx_bits, __float_as_uint(rn * (1.f + 0.0009765625f)));
@@ -629,14 +644,14 @@ __global__ void __launch_bounds__(256) tc_prep_x_wide_kernel(const float *__rest
                                                              int64_t m, int d, int d_pad,
                                                              __half *__restrict__ Xh,
                                                              float *__restrict__ xnorm,
-                                                             float *__restrict__ xinv,
+                                                             float4 *__restrict__ xmeta,
                                                              WsHeader *hdr) {
-  __shared__ float s_max[8], s_rn[8];
+  __shared__ float s_max[8], s_rn[8], s_min[8];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int64_t grp = blockIdx.x;
   const int64_t row_base = grp * kScaleRows + warp * 8;
   const int d4 = d >> 2, dp4 = d_pad >> 2;
-  float wmax = 0.f, wrn = 0.f;
+  float wmax = 0.f, wrn = 0.f, wmin = INFINITY;
   bool bad = false;
   for (int u = 0; u < 8; u++) {
     const int64_t row = row_base + u;
@@ -669,11 +684,12 @@ __global__ void __launch_bounds__(256) tc_prep_x_wide_kernel(const float *__rest
       if (!isfinite(ss)) bad = true;
       wmax = fmaxf(wmax, mx);
       wrn = fmaxf(wrn, sqrtf(ss));
+      wmin = fminf(wmin, ss);
     }
     // rows past m: v = +inf never passes a finite threshold
     if (lane == 0) xnorm[row] = row < m ? ss : INFINITY;
   }
-  if (lane == 0) { s_max[warp] = wmax; s_rn[warp] = wrn; }
+  if (lane == 0) { s_max[warp] = wmax; s_rn[warp] = wrn; s_min[warp] = wmin; }
   if (bad && lane == 0) atomicOr(&hdr->exact_only, 1);
   __syncthreads();
   float gmax = 0.f, rn = 0.f;
@@ -681,7 +697,11 @@ __global__ void __launch_bounds__(256) tc_prep_x_wide_kernel(const float *__rest
   for (int w = 0; w < 8; w++) { gmax = fmaxf(gmax, s_max[w]); rn = fmaxf(rn, s_rn[w]); }
   const float sc = pow2_scale_for(gmax);
   if (threadIdx.x == 0) {
-    xinv[grp] = 1.f / sc;
+    // the group's record: min ||x||^2 of each 16-row chunk (warps 2j, 2j+1; +inf for a
+    // chunk of padding rows), then the scale and its inverse
+    xmeta[2 * grp] = make_float4(fminf(s_min[0], s_min[1]), fminf(s_min[2], s_min[3]),
+                                 fminf(s_min[4], s_min[5]), fminf(s_min[6], s_min[7]));
+    xmeta[2 * grp + 1] = make_float4(1.f / sc, sc, 0.f, 0.f);
     // sqrt of an FP32 sum of d squares: (1 + 2^-10) covers its rounding for d <= 4096;
     // the bound only grows, and non-negative floats order like their bit patterns
     if (isfinite(rn)) atomicMax(&hdr->rx_bits, __float_as_uint(rn * (1.f + 0.0009765625f)));
@@ -1569,7 +1589,7 @@ static void layout_workspace(TcPlan &P) {
   const size_t rows_f = prepared ? 0 : 1;
   P.off_xh = off;       off = al256(off + rows_f * (size_t)m * P.d_pad * 2);
   P.off_xnorm = off;    off = al256(off + rows_f * (size_t)P.x_tiles * kBN * 4);
-  P.off_xscale = off;   off = al256(off + rows_f * (size_t)P.x_tiles * kColGroups * 4);
+  P.off_xscale = off;   off = al256(off + rows_f * (size_t)P.x_tiles * kColGroups * 32);
   P.off_invsq = off;    off = al256(off + 16);
   P.off_qh = off;       off = al256(off + (size_t)q_rows * P.d_pad * 2);
   P.off_qinfo = off;    off = al256(off + (size_t)q_rows * 8);
@@ -1691,18 +1711,18 @@ static bool make_tmap(CUtensorMap *map, const void *base, int64_t rows, int cols
 // rows -> f16 in 64-row scale groups, ||x||^2, inverse scales; norm bound and
 // exact-only flag (set for a non-finite row) into hdr
 static void launch_prep_rows(const float *X, int64_t m, int d, int d_pad, int64_t x_tiles,
-                             __half *Xh, float *xnorm, float *xinv, WsHeader *hdr,
+                             __half *Xh, float *xnorm, float4 *xmeta, WsHeader *hdr,
                              cudaStream_t stream) {
   const unsigned groups = (unsigned)(x_tiles * kColGroups);  // 64-row scale groups
   const bool vec = (d & 3) == 0 && (reinterpret_cast<uintptr_t>(X) & 15) == 0;
   if (vec && d_pad <= 128)
-    tc_prep_x_kernel<true, 1><<<groups, 256, 0, stream>>>(X, m, d, d_pad, Xh, xnorm, xinv, hdr);
+    tc_prep_x_kernel<true, 1><<<groups, 256, 0, stream>>>(X, m, d, d_pad, Xh, xnorm, xmeta, hdr);
   else if (vec && d_pad <= 256)
-    tc_prep_x_kernel<true, 2><<<groups, 256, 0, stream>>>(X, m, d, d_pad, Xh, xnorm, xinv, hdr);
+    tc_prep_x_kernel<true, 2><<<groups, 256, 0, stream>>>(X, m, d, d_pad, Xh, xnorm, xmeta, hdr);
   else if (vec)
-    tc_prep_x_wide_kernel<<<groups, 256, 0, stream>>>(X, m, d, d_pad, Xh, xnorm, xinv, hdr);
+    tc_prep_x_wide_kernel<<<groups, 256, 0, stream>>>(X, m, d, d_pad, Xh, xnorm, xmeta, hdr);
   else
-    tc_prep_x_kernel<false, 1><<<groups, 256, 0, stream>>>(X, m, d, d_pad, Xh, xnorm, xinv, hdr);
+    tc_prep_x_kernel<false, 1><<<groups, 256, 0, stream>>>(X, m, d, d_pad, Xh, xnorm, xmeta, hdr);
 }
 
 PreparedLayout tc_prepared_layout(int64_t m, int d) {
@@ -1714,15 +1734,15 @@ PreparedLayout tc_prepared_layout(int64_t m, int d) {
   L.off_info = off;   off = al256(off + sizeof(PreparedInfo));
   L.off_xh = off;     off = al256(off + (size_t)m * d_pad * 2);
   L.off_xnorm = off;  off = al256(off + (size_t)x_tiles * kBN * 4);
-  L.off_xinv = off;   off = al256(off + (size_t)x_tiles * kColGroups * 4);
+  L.off_xmeta = off;  off = al256(off + (size_t)x_tiles * kColGroups * 32);
   L.total = off;
   return L;
 }
 
 static PreparedInfo prepared_info(int64_t m, int d) {
   PreparedInfo I{};
-  memcpy(I.magic, "BFKPREP1", 8);
-  I.version = 1;
+  memcpy(I.magic, "BFKPREP2", 8);
+  I.version = 2;
   I.d = d;
   I.m = m;
   I.d_pad = kch_for(d) * kBK;
@@ -1742,7 +1762,7 @@ int tc_prepare(const float *X, int64_t m, int d, void *prep, cudaStream_t stream
   if (e == cudaSuccess) {
     launch_prep_rows(X, m, d, I.d_pad, I.x_tiles, reinterpret_cast<__half *>(pb + L.off_xh),
                      reinterpret_cast<float *>(pb + L.off_xnorm),
-                     reinterpret_cast<float *>(pb + L.off_xinv), status, stream);
+                     reinterpret_cast<float4 *>(pb + L.off_xmeta), status, stream);
     e = cudaGetLastError();
   }
   // the description is copied from this stack frame: wait before returning
@@ -1774,14 +1794,14 @@ int tc_run(const float *Q, const float *X, int64_t id_offset, float *out_d, int3
   WsHeader *hdr = reinterpret_cast<WsHeader *>(ws);
   __half *Xh = reinterpret_cast<__half *>(ws + p.off_xh);
   float *xnorm = reinterpret_cast<float *>(ws + p.off_xnorm);
-  float *xinv = reinterpret_cast<float *>(ws + p.off_xscale);
+  float4 *xmeta = reinterpret_cast<float4 *>(ws + p.off_xscale);
   float *inv_sq = reinterpret_cast<float *>(ws + p.off_invsq);
   const unsigned char *pb = static_cast<const unsigned char *>(prepared);
   if (prepared) {
     const PreparedLayout PL = tc_prepared_layout(p.m, p.d);
     Xh = reinterpret_cast<__half *>(const_cast<unsigned char *>(pb) + PL.off_xh);
     xnorm = reinterpret_cast<float *>(const_cast<unsigned char *>(pb) + PL.off_xnorm);
-    xinv = reinterpret_cast<float *>(const_cast<unsigned char *>(pb) + PL.off_xinv);
+    xmeta = reinterpret_cast<float4 *>(const_cast<unsigned char *>(pb) + PL.off_xmeta);
   }
   __half *Qh = reinterpret_cast<__half *>(ws + p.off_qh);
   float2 *qinfo = reinterpret_cast<float2 *>(ws + p.off_qinfo);
@@ -1810,7 +1830,7 @@ int tc_run(const float *Q, const float *X, int64_t id_offset, float *out_d, int3
     tc_take_row_status<<<1, 32, 0, stream>>>(
         reinterpret_cast<const WsHeader *>(pb + PL.off_status), hdr);
   } else {
-    launch_prep_rows(X, p.m, p.d, p.d_pad, p.x_tiles, Xh, xnorm, xinv, hdr, stream);
+    launch_prep_rows(X, p.m, p.d, p.d_pad, p.x_tiles, Xh, xnorm, xmeta, hdr, stream);
   }
   tc_prep_q_kernel<<<(unsigned)(q_rows / 8), 256, 0, stream>>>(Q, p.n, p.d, p.d_pad, q_rows, Qh,
                                                                 qinfo, inv_sq, hdr);
@@ -1838,7 +1858,7 @@ int tc_run(const float *Q, const float *X, int64_t id_offset, float *out_d, int3
                                cudaFuncAttributeMaxDynamicSharedMemorySize, (int)wsmem));
   FilterArgs A{};
   A.xnorm = xnorm;
-  A.xinv = xinv;
+  A.xmeta = xmeta;
   A.qinfo = qinfo;
   A.inv_sq = inv_sq;
   A.n = p.n;
@@ -2042,7 +2062,7 @@ int tc_filter_values(const float *Q, const float *X, float *out_v, float *out_qi
   WsHeader *hdr = reinterpret_cast<WsHeader *>(ws);
   __half *Xh = reinterpret_cast<__half *>(ws + p.off_xh);
   float *xnorm = reinterpret_cast<float *>(ws + p.off_xnorm);
-  float *xinv = reinterpret_cast<float *>(ws + p.off_xscale);
+  float4 *xmeta = reinterpret_cast<float4 *>(ws + p.off_xscale);
   float *inv_sq = reinterpret_cast<float *>(ws + p.off_invsq);
   __half *Qh = reinterpret_cast<__half *>(ws + p.off_qh);
   float2 *qinfo = reinterpret_cast<float2 *>(ws + p.off_qinfo);
@@ -2062,7 +2082,7 @@ int tc_filter_values(const float *Q, const float *X, float *out_v, float *out_qi
   // NaN (all bits set) marks a pair the filter did not report
   BFK_TRY(cudaMemsetAsync(out_v, 0xff, (size_t)p.n * p.m * sizeof(float), stream));
   tc_qmax_kernel<<<592, 256, 0, stream>>>(Q, p.n * p.d, hdr);
-  launch_prep_rows(X, p.m, p.d, p.d_pad, p.x_tiles, Xh, xnorm, xinv, hdr, stream);
+  launch_prep_rows(X, p.m, p.d, p.d_pad, p.x_tiles, Xh, xnorm, xmeta, hdr, stream);
   tc_prep_q_kernel<<<(unsigned)(q_rows / 8), 256, 0, stream>>>(Q, p.n, p.d, p.d_pad, q_rows, Qh,
                                                                 qinfo, inv_sq, hdr);
   BFK_TRY(cudaGetLastError());
@@ -2077,7 +2097,7 @@ int tc_filter_values(const float *Q, const float *X, float *out_v, float *out_qi
                                cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
   FilterArgs A{};
   A.xnorm = xnorm;
-  A.xinv = xinv;
+  A.xmeta = xmeta;
   A.qinfo = qinfo;
   A.inv_sq = inv_sq;
   A.r_in = nullptr;  // no bound: every finite v is appended

@@ -133,3 +133,64 @@ def test_filter_drops_infinite_distances_above_the_guard():
     _, ids = oracle_knn(Q, X, X.shape[0])
     q = int(np.argmax(lost.any(axis=1)))
     assert np.isin(np.flatnonzero(lost[q]), ids[q]).all()  # returned by the exact search
+
+
+# ---------------------------------------------------------------------------
+# The filter kernel's chunk test (knn_tc_filter_kernel): a 16-column chunk is skipped
+# when its largest accumulator is <= T = rd(ru(succ(theta) - min ||x||^2) * (1/c)).
+# Skipping must never lose a column whose v = rn(c * acc + ||x||^2) is <= theta.
+# Restated here with exact rational arithmetic and the kernel's rounding modes.
+# ---------------------------------------------------------------------------
+from fractions import Fraction  # noqa: E402
+
+_INF32 = np.float32(np.inf)
+
+
+def _f32(fr: Fraction, mode: str) -> np.float32:
+    """fr rounded to float32: 'rd' down, 'ru' up, 'rn' to nearest (ties to even)."""
+    x = np.float32(float(fr))
+    while Fraction(float(x)) > fr:
+        x = np.nextafter(x, -_INF32)
+    while Fraction(float(np.nextafter(x, _INF32))) <= fr:
+        x = np.nextafter(x, _INF32)
+    lo = x  # the largest float32 <= fr
+    if mode == "rd" or Fraction(float(lo)) == fr:
+        return lo
+    hi = np.nextafter(lo, _INF32)
+    if mode == "ru":
+        return hi
+    dl, dh = fr - Fraction(float(lo)), Fraction(float(hi)) - fr
+    if dl != dh:
+        return lo if dl < dh else hi
+    return lo if (int(lo.view(np.uint32)) & 1) == 0 else hi
+
+
+def _chunk_skipped(acc, nx, c, theta) -> bool:
+    theta2 = np.nextafter(np.float32(theta), _INF32)
+    gmin = np.float32(nx.min())
+    inv_c = Fraction(1) / Fraction(float(c))  # an exact power of two
+    diff = _f32(Fraction(float(theta2)) - Fraction(float(gmin)), "ru")
+    T = _f32(Fraction(float(diff)) * inv_c, "rd")
+    return bool(np.float32(acc.max()) <= T)
+
+
+@pytest.mark.parametrize("seed", range(4))
+def test_chunk_skip_never_loses_a_kept_column(seed):
+    g = np.random.default_rng(seed)
+    c = np.float32(-2.0 ** int(g.integers(-30, -10)))
+    skipped = kept_in_skipped = 0
+    for _ in range(400):
+        acc = (g.standard_normal(16) * 2.0 ** int(g.integers(10, 26))).astype(np.float32)
+        nx = np.abs(g.standard_normal(16) * 4).astype(np.float32) + np.float32(1.0)
+        if g.random() < 0.5:
+            nx[:] = nx[0]  # equal norms, as unit vectors have: the tightest case
+        v = [_f32(Fraction(float(c)) * Fraction(float(a)) + Fraction(float(x)), "rn")
+             for a, x in zip(acc, nx)]
+        # theta at, just below or just above the smallest v of the chunk
+        vmin = min(v)
+        theta = [vmin, np.nextafter(vmin, -_INF32), np.nextafter(vmin, _INF32)][int(g.integers(3))]
+        if _chunk_skipped(acc, nx, c, theta):
+            skipped += 1
+            kept_in_skipped += sum(1 for x in v if x <= theta)
+    assert kept_in_skipped == 0
+    assert skipped > 0  # the rule does skip (theta just below the chunk's smallest v)
