@@ -36,6 +36,7 @@ EXPORTS = (
     "bfk_workspace_size",
     "bfk_search",
     "bfk_merge",
+    "bfk_merge_strided",
     "bfk_kernel_attrs",
     "bfk_merge_attrs",
     "bfk_filter_values_workspace",
@@ -119,6 +120,8 @@ def load() -> ctypes.CDLL:
                                    ctypes.POINTER(Opts), vp]
         lib.bfk_merge.restype = i32
         lib.bfk_merge.argtypes = [vp, vp, i64, i32, i32, vp, vp, vp]
+        lib.bfk_merge_strided.restype = i32
+        lib.bfk_merge_strided.argtypes = [vp, vp, i64, i32, i64, i32, vp, vp, vp]
         lib.bfk_kernel_attrs.restype = i32
         lib.bfk_kernel_attrs.argtypes = [i32, i32, i32, ctypes.POINTER(Attrs)]
         lib.bfk_merge_attrs.restype = i32

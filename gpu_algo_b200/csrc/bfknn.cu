@@ -416,6 +416,20 @@ static void fill_attrs(const cudaFuncAttributes &a, size_t dyn, int threads, bfk
   out->block_threads = threads;
 }
 
+bfk_status_t bfk_merge_strided(const float *cand_dists, const int32_t *cand_ids, int64_t n,
+                               int32_t lists, int64_t list_stride, int32_t k, float *out_dists,
+                               int32_t *out_ids, void *stream) {
+  if (n < 0 || lists <= 0 || k <= 0 || list_stride < n * k) return BFK_ERR_INVALID_ARGUMENT;
+  if (k > merge_max_k()) return BFK_ERR_UNSUPPORTED;
+  if (n == 0) return BFK_OK;
+  if (!cand_dists || !cand_ids || !out_dists || !out_ids) return BFK_ERR_INVALID_ARGUMENT;
+  bfk_status_t s = check_device();
+  if (s != BFK_OK) return s;
+  return cuda_status(launch_merge_strided(cand_dists, cand_ids, n, lists, k, list_stride,
+                                          out_dists, out_ids,
+                                          reinterpret_cast<cudaStream_t>(stream)));
+}
+
 bfk_status_t bfk_kernel_attrs(int32_t engine, int32_t d, int32_t k, bfk_attrs_t *out) {
   if (!out || d <= 0 || k <= 0) return BFK_ERR_INVALID_ARGUMENT;
   if (d > kMaxD || k > kMaxK) return BFK_ERR_UNSUPPORTED;

@@ -27,6 +27,10 @@ cudaError_t launch_scan(const float *Q, int64_t n, const float *X, int64_t m, in
                         cudaStream_t stream);
 cudaError_t launch_merge(const float *cand_d, const int32_t *cand_i, int64_t n, int lists, int k,
                          float *out_d, int32_t *out_i, cudaStream_t stream);
+// the same, list l's (n, k) block starting l * stride elements after the first
+cudaError_t launch_merge_strided(const float *cand_d, const int32_t *cand_i, int64_t n, int lists,
+                                 int k, int64_t stride, float *out_d, int32_t *out_i,
+                                 cudaStream_t stream);
 int merge_max_k();
 // the kernel launch_merge runs for `lists` lists of k, and its dynamic shared memory
 const void *merge_kernel_for(int lists, int k, size_t *smem);

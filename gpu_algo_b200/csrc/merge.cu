@@ -30,10 +30,10 @@ __device__ void block_bitonic_sort(uint64_t *keys, int P) {
 }
 
 // grid (n), block kMergeThreads, dynamic smem kMergeCap * 8.
-// cand (lists, n, k) -> out (n, k)
+// cand: list l's (n, k) block starts `stride` elements after list l-1's -> out (n, k)
 __global__ void __launch_bounds__(kMergeThreads) knn_merge_kernel(
     const float *__restrict__ cand_d, const int32_t *__restrict__ cand_i, int64_t n, int lists,
-    int k, float *__restrict__ out_d, int32_t *__restrict__ out_i) {
+    int k, int64_t stride, float *__restrict__ out_d, int32_t *__restrict__ out_i) {
   extern __shared__ __align__(16) uint64_t keys[];
   const int64_t qi = blockIdx.x;
   const int group = (kMergeCap - k) / k;  // lists added per round (>= 1 since k <= kMergeCap/2)
@@ -47,7 +47,7 @@ __global__ void __launch_bounds__(kMergeThreads) knn_merge_kernel(
       uint64_t key = ~0ull;
       if (e < (l1 - l0) * k) {
         const int l = l0 + e / k, j = e % k;
-        const int64_t off = ((int64_t)l * n + qi) * k + j;
+        const int64_t off = (int64_t)l * stride + qi * k + j;
         key = pair_key(cand_d[off], cand_i[off]);
       }
       keys[have + e] = key;
@@ -69,13 +69,13 @@ __global__ void __launch_bounds__(kMergeThreads) knn_merge_kernel(
 // each of the first k keys without a sort.  grid (n), dynamic smem lists*k*8.
 __global__ void __launch_bounds__(kMergeThreads) knn_merge_rank_kernel(
     const float *__restrict__ cand_d, const int32_t *__restrict__ cand_i, int64_t n, int lists,
-    int k, float *__restrict__ out_d, int32_t *__restrict__ out_i) {
+    int k, int64_t stride, float *__restrict__ out_d, int32_t *__restrict__ out_i) {
   extern __shared__ __align__(16) uint64_t keys[];
   const int64_t qi = blockIdx.x;
   const int total = lists * k;
   for (int e = threadIdx.x; e < total; e += blockDim.x) {
     const int l = e / k, j = e - l * k;
-    const int64_t off = ((int64_t)l * n + qi) * k + j;
+    const int64_t off = (int64_t)l * stride + qi * k + j;
     keys[e] = pair_key(cand_d[off], cand_i[off]);
   }
   __syncthreads();
@@ -105,6 +105,12 @@ __global__ void __launch_bounds__(kMergeThreads) knn_merge_rank_kernel(
 
 cudaError_t launch_merge(const float *cand_d, const int32_t *cand_i, int64_t n, int lists, int k,
                          float *out_d, int32_t *out_i, cudaStream_t stream) {
+  return launch_merge_strided(cand_d, cand_i, n, lists, k, n * k, out_d, out_i, stream);
+}
+
+cudaError_t launch_merge_strided(const float *cand_d, const int32_t *cand_i, int64_t n, int lists,
+                                 int k, int64_t stride, float *out_d, int32_t *out_i,
+                                 cudaStream_t stream) {
   if (n == 0) return cudaSuccess;
   // by rank for a few lists (each key binary-searches every other list); sorting for many
   if (lists <= kRankMergeLists && (int64_t)lists * k <= kMergeCap) {
@@ -114,7 +120,7 @@ cudaError_t launch_merge(const float *cand_d, const int32_t *cand_i, int64_t n, 
                                          (int)(kMergeCap * sizeof(uint64_t)));
     if (e != cudaSuccess) return e;
     knn_merge_rank_kernel<<<(unsigned)n, kMergeThreads, rsmem, stream>>>(cand_d, cand_i, n, lists,
-                                                                          k, out_d, out_i);
+                                                                          k, stride, out_d, out_i);
     return cudaGetLastError();
   }
   const size_t smem = (size_t)kMergeCap * sizeof(uint64_t);
@@ -122,7 +128,7 @@ cudaError_t launch_merge(const float *cand_d, const int32_t *cand_i, int64_t n, 
                                        cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   if (e != cudaSuccess) return e;
   knn_merge_kernel<<<(unsigned)n, kMergeThreads, smem, stream>>>(cand_d, cand_i, n, lists, k,
-                                                                 out_d, out_i);
+                                                                 stride, out_d, out_i);
   return cudaGetLastError();
 }
 

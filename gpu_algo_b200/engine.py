@@ -262,6 +262,27 @@ def _attrs_dict(a: "_lib.Attrs") -> dict:
     }
 
 
+def merge_packed(blocks: torch.Tensor, k: int):
+    """Merge gathered (lists, 2, n, k) int32 blocks -- list l's distance bits in
+    [l, 0], its ids in [l, 1] -- into the k best per query, read in place."""
+    if blocks.dim() != 4 or blocks.shape[1] != 2 or blocks.dtype != torch.int32:
+        raise ValueError("blocks must be (lists, 2, n, k) int32")
+    lists, _, n, kk = blocks.shape
+    if kk != k:
+        raise ValueError("list length must equal k")
+    blocks = blocks.contiguous()
+    with torch.cuda.device(blocks.device):
+        stream = torch.cuda.current_stream()
+        out_d = torch.empty((n, k), dtype=torch.float32, device=blocks.device)
+        out_i = torch.empty((n, k), dtype=torch.int32, device=blocks.device)
+        base = blocks.data_ptr()
+        _lib.check(_lib.load().bfk_merge_strided(base, base + 4 * n * k, n, lists, 2 * n * k, k,
+                                                 out_d.data_ptr(), out_i.data_ptr(),
+                                                 ctypes.c_void_p(stream.cuda_stream)),
+                   "bfk_merge_strided")
+    return out_d, out_i
+
+
 def kernel_attrs(engine: str, d: int, k: int) -> dict:
     """Attributes of the main kernel an engine launches for (d, k)."""
     a = _lib.Attrs()

@@ -2,9 +2,10 @@
 
 The database is split by rows across the ranks of a process group; every
 rank searches its own shard (global row index = shard start + local row),
-one all-gather moves each rank's (n, k) sorted (distance, index) lists to
-every rank, and the on-device merge kernel (``bfk_merge``) reduces the
-(world, n, k) candidates to the final k per query.  The reference has no
+one all-gather moves each rank's (n, k) sorted (distance, index) lists, packed
+into one block, to every rank, and the on-device merge kernel
+(``bfk_merge_strided``) reduces the world * k candidates per query to the
+final k, reading the gathered blocks in place.  The reference has no
 multi-GPU path; this is the exchange step its split-N partial/merge design
 (bf/fp32_tiled.py:182-239) implies once the tiles live on different GPUs.
 """
@@ -25,15 +26,25 @@ def shard_range(total_rows: int, rank: int, world: int) -> tuple[int, int]:
     return begin, begin + base + (1 if rank < rem else 0)
 
 
-def gather_lists(d_: torch.Tensor, i_: torch.Tensor, group=None) -> tuple[torch.Tensor, torch.Tensor]:
-    """All-gather (n, k) lists into (world, n, k) on every rank."""
+def pack_lists(d_: torch.Tensor, i_: torch.Tensor) -> torch.Tensor:
+    """One rank's (n, k) distances and ids as one int32 block [distance bits | ids]."""
+    return torch.cat((d_.contiguous().view(torch.int32).view(-1), i_.contiguous().view(-1)))
+
+
+def gather_lists(d_: torch.Tensor, i_: torch.Tensor, group=None) -> torch.Tensor:
+    """One all-gather of every rank's packed (distance, index) block: (world, 2, n, k)
+    int32 on every rank, rank r's distance bits in [r, 0] and its ids in [r, 1]."""
     world = dist.get_world_size(group)
     n, k = d_.shape
-    all_d = torch.empty((world * n * k,), dtype=d_.dtype, device=d_.device)
-    all_i = torch.empty((world * n * k,), dtype=i_.dtype, device=i_.device)
-    dist.all_gather_into_tensor(all_d, d_.contiguous().view(-1), group=group)
-    dist.all_gather_into_tensor(all_i, i_.contiguous().view(-1), group=group)
-    return all_d.view(world, n, k), all_i.view(world, n, k)
+    send = pack_lists(d_, i_)
+    recv = torch.empty((world * send.numel(),), dtype=torch.int32, device=d_.device)
+    dist.all_gather_into_tensor(recv, send, group=group)
+    return recv.view(world, 2, n, k)
+
+
+def unpack_lists(blocks: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
+    """(world, 2, n, k) packed blocks -> (world, n, k) distances and ids (copies)."""
+    return blocks[:, 0].contiguous().view(torch.float32), blocks[:, 1].contiguous()
 
 
 def make_local_search(group=None, plan_rows: int = 0, **search_kwargs) -> Callable:
@@ -90,16 +101,19 @@ def sharded_search(Q, X_shard, k: int, row_begin: int, group=None,
     looked up with an all-reduce when 0) gives every shard the same levels, so
     all ranks take the same collective steps.
 
-    `local_search(Q, X, k, id_offset)` and `merge_fn(all_d, all_i, k)` default
-    to the CUDA engine; tests substitute CPU stand-ins to exercise the
-    orchestration over gloo.  `search_kwargs` go to `engine.search`.
+    The exchange is one all-gather of each rank's packed (n, k) lists, distance bits
+    then ids (8 n k bytes per rank), merged in place on every rank.
+
+    `local_search(Q, X, k, id_offset)` and `merge_fn(blocks, k)` (blocks: the
+    gathered (world, 2, n, k) int32 lists) default to the CUDA engine; tests
+    substitute CPU stand-ins to exercise the orchestration over gloo.
+    `search_kwargs` go to `engine.search`.
     """
     if local_search is None:
         local_search = make_local_search(group, plan_rows, **search_kwargs)
     if merge_fn is None:
-        from .engine import merge as merge_fn
+        from .engine import merge_packed as merge_fn
     d_, i_ = local_search(Q, X_shard, k, row_begin)
     if not dist.is_initialized() or dist.get_world_size(group) == 1:
         return d_, i_
-    all_d, all_i = gather_lists(d_, i_, group)
-    return merge_fn(all_d, all_i, k)
+    return merge_fn(gather_lists(d_, i_, group), k)

@@ -181,6 +181,16 @@ BFK_API bfk_status_t bfk_merge(const float *cand_dists, const int32_t *cand_ids,
                        void *stream);
 
 /*
+ * bfk_merge with list l's (n, k) block of distances (ids) starting l * list_stride
+ * elements after cand_dists (cand_ids); list_stride >= n * k.  No reference
+ * counterpart: a sharded search all-gathers each rank's distances and ids as one
+ * block per rank ([distances | ids], list_stride = 2 n k) and merges them in place.
+ */
+BFK_API bfk_status_t bfk_merge_strided(const float *cand_dists, const int32_t *cand_ids,
+                                       int64_t n, int32_t lists, int64_t list_stride, int32_t k,
+                                       float *out_dists, int32_t *out_ids, void *stream);
+
+/*
  * Attributes of the main kernel an engine launches for (d, k).  Replaces
  * kernel_attrs (bf/fp32.py:238-249, CuPy RawKernel.attributes).
  */

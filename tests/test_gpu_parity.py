@@ -189,6 +189,25 @@ def test_merge_rank_and_grouped_paths(lists, k):
     assert_exact(md.cpu().numpy(), mi.cpu().numpy(), ed, ei, f"merge {lists}x{k}")
 
 
+@pytest.mark.parametrize("lists,k", [(2, 10), (8, 100), (40, 100)])
+def test_packed_merge_matches_merge(lists, k):
+    """The sharded exchange's layout: each list's distances then ids in one int32
+    block per list, merged in place (bfk_merge_strided)."""
+    from gpu_algo_b200.sharded import pack_lists
+    rng = np.random.Generator(np.random.PCG64(lists + 7 * k))
+    n = 96
+    cd = np.sort(rng.standard_normal((lists, n, k)).astype(np.float32) ** 2, axis=2)
+    ci = rng.permutation(lists * n * k).astype(np.int32).reshape(lists, n, k)
+    cd[-1, :, k // 2:] = np.float32(3.402823e38)
+    ci[-1, :, k // 2:] = -1
+    blocks = torch.stack([pack_lists(dev(cd[l]), dev(ci[l])) for l in range(lists)])
+    pd, pi = engine.merge_packed(blocks.view(lists, 2, n, k), k)
+    md, mi = engine.merge(dev(cd), dev(ci), k)
+    ed, ei = oracle_merge(cd, ci, k)
+    assert_exact(pd.cpu().numpy(), pi.cpu().numpy(), ed, ei, "packed merge")
+    assert_exact(md.cpu().numpy(), mi.cpu().numpy(), ed, ei, "merge")
+
+
 @pytest.mark.parametrize("n,m,d,k", [(1, 100_000, 96, 10), (3, 50_000, 33, 1), (16, 70_001, 96, 64),
                                      (9, 40_000, 300, 17), (16, 8192, 128, 10)])
 def test_small_batch_scan_is_exact(n, m, d, k):

@@ -54,7 +54,9 @@ def _rank_main(rank, world, port, k, outdir):
             torch.cuda.synchronize()
             return d_.cpu(), i_.cpu()  # gloo gathers host tensors
 
-        def merge(all_d, all_i, kk):
+        def merge(blocks, kk):
+            from gpu_algo_b200.sharded import unpack_lists
+            all_d, all_i = unpack_lists(blocks)
             from oracle import oracle_merge
             d_, i_ = oracle_merge(all_d.numpy(), all_i.numpy(), kk)
             return torch.from_numpy(d_), torch.from_numpy(i_)

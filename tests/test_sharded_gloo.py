@@ -41,7 +41,9 @@ def _rank_main(rank, world, port, outdir):
             d_, i_ = oracle_knn(Qt.numpy(), Xt.numpy(), kk, id_offset=off)
             return torch.from_numpy(d_), torch.from_numpy(i_)
 
-        def merge(all_d, all_i, kk):
+        def merge(blocks, kk):
+            from gpu_algo_b200.sharded import unpack_lists
+            all_d, all_i = unpack_lists(blocks)
             d_, i_ = oracle_merge(all_d.numpy(), all_i.numpy(), kk)
             return torch.from_numpy(d_), torch.from_numpy(i_)
 
@@ -112,3 +114,13 @@ def test_shard_range_balanced():
             assert sizes[0][0] == 0 and sizes[-1][1] == total
             lens = [b - a for a, b in sizes]
             assert max(lens) - min(lens) <= 1
+
+
+def test_pack_and_unpack_lists_round_trip():
+    from gpu_algo_b200.sharded import pack_lists, unpack_lists
+    g = np.random.default_rng(0)
+    d_ = [torch.from_numpy(g.standard_normal((5, 3)).astype(np.float32)) for _ in range(2)]
+    i_ = [torch.from_numpy(g.integers(-1, 100, (5, 3)).astype(np.int32)) for _ in range(2)]
+    blocks = torch.stack([pack_lists(a, b) for a, b in zip(d_, i_)]).view(2, 2, 5, 3)
+    all_d, all_i = unpack_lists(blocks)
+    assert torch.equal(all_d, torch.stack(d_)) and torch.equal(all_i, torch.stack(i_))
