@@ -12,7 +12,9 @@ one all-reduce of 2n floats), one NCCL all-gather moves the per-shard (n, k)
 lists and the merge kernel produces the result on every rank.  `value` is queries/sec of the whole job
 (the query batch / the max over ranks of the device-timed step).  Inputs are
 synthetic (seeded, the workload's shapes and distributions), resident in HBM
-when timing starts; the database is larger than L2, so no flush is needed.
+when timing starts.  When a GPU's inputs are larger than L2 the steps run back to
+back; when L2 could hold them, a 256 MB buffer is written before every step and
+each step is timed alone.
 
 Prints one JSON line on rank 0.
 """
@@ -69,6 +71,9 @@ def parse_args(argv=None):
                     help="queries in the bounded CPU-baseline sample")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--phases", action="store_true",
+                    help="after the timed steps, time one more step phase by phase (CUDA "
+                         "events at each phase boundary; the max over ranks is reported)")
     return ap.parse_args(argv)
 
 
@@ -166,11 +171,25 @@ def cpu_baseline(X, Q, k, sample, steps=1):
     return times, threads
 
 
+L2_BYTES = 126 * 1024 * 1024        # B200 L2
+L2_FLUSH_BYTES = 256 * 1024 * 1024  # written before each timed step when the inputs fit in L2
+
+
+def l2_resident(N, Qn, d, world=1) -> bool:
+    """Whether one GPU's inputs (its rows and the queries, in FP32) could sit in L2."""
+    return (-(-N // world) + Qn) * d * 4 <= 2 * L2_BYTES
+
+
 def bench_config(a, N, Qn, d, k):
     """The workload description both arms print (the same dict for the same run)."""
+    if l2_resident(N, Qn, d, a.gpus):
+        l2 = (f"inputs fit in L2 (database {N * d * 4 / 1e9:.3f} GB): {L2_FLUSH_BYTES >> 20} MB "
+              "written before each timed step, which is timed alone")
+    else:
+        l2 = f"inputs larger than L2 (database {N * d * 4 / 1e9:.2f} GB), no flush"
     return {"workload": a.workload, "N": N, "Q": Qn, "d": d, "k": k,
             "parallelism": f"rowshard{a.gpus}", "rows_prepared_once": bool(a.prepared),
-            "l2": f"inputs larger than L2 (database {N * d * 4 / 1e9:.2f} GB), no flush"}
+            "l2": l2}
 
 
 def run_reference(a):
@@ -231,15 +250,19 @@ def main(argv=None) -> int:
     Qd = torch.from_numpy(Q).to(device)
     torch.cuda.synchronize()
 
+    # inputs that L2 could hold are evicted before every timed step
+    flush = (torch.empty(L2_FLUSH_BYTES // 4, dtype=torch.int32, device=device)
+             if l2_resident(N, Qn, d, world) else None)
+
     # every rank plans its sampling levels for the largest shard
     plan_rows = shard_range(N, 0, world)[1] - shard_range(N, 0, world)[0]
 
     prepared = engine.PreparedRows.prepare(Xd) if a.prepared else None
 
-    def step(time_main=False, Q_=None):
+    def step(time_main=False, Q_=None, on_phase=None):
         return sharded_search(Qd if Q_ is None else Q_, Xd, k, r0, plan_rows=plan_rows,
                               engine=a.engine, time_main=time_main, cta_pair=a.cta_pair,
-                              prepared=prepared)
+                              prepared=prepared, on_phase=on_phase)
 
     def barrier():
         if world > 1:
@@ -256,16 +279,31 @@ def main(argv=None) -> int:
     torch.cuda.synchronize()
     sampler = ClockSampler(local)
     sampler.start()
-    ev0 = torch.cuda.Event(enable_timing=True)
-    ev1 = torch.cuda.Event(enable_timing=True)
-    ev0.record()
-    for _ in range(a.steps):
-        step(time_main=True)
-    ev1.record()
-    torch.cuda.synchronize()
+    if flush is None:
+        ev0 = torch.cuda.Event(enable_timing=True)
+        ev1 = torch.cuda.Event(enable_timing=True)
+        ev0.record()
+        for _ in range(a.steps):
+            step(time_main=True)
+        ev1.record()
+        torch.cuda.synchronize()
+        t_ms = ev0.elapsed_time(ev1) / a.steps
+    else:
+        # the inputs fit in L2: each step is timed alone, after a write of a buffer
+        # larger than L2 has evicted them
+        evs = []
+        for _ in range(a.steps):
+            flush.zero_()
+            e_a = torch.cuda.Event(enable_timing=True)
+            e_b = torch.cuda.Event(enable_timing=True)
+            e_a.record()
+            step(time_main=True)
+            e_b.record()
+            evs.append((e_a, e_b))
+        torch.cuda.synchronize()
+        t_ms = sum(x.elapsed_time(y) for x, y in evs) / a.steps
     barrier()
     clocks = sampler.stop()
-    t_ms = ev0.elapsed_time(ev1) / a.steps
     stats = engine.last_stats(Qd, Xd, k, **stat_opts)
     main_ms = stats["main_kernel_ms"] / max(1, stats["timed_calls"])
     tt = torch.tensor([t_ms, main_ms], device=device, dtype=torch.float64)
@@ -273,6 +311,25 @@ def main(argv=None) -> int:
         dist.all_reduce(tt, op=dist.ReduceOp.MAX)
     t_max, main_max = float(tt[0]), float(tt[1])
     value = Qn / (t_max / 1e3)
+
+    phases = None
+    if a.phases:
+        marks = []
+
+        def mark(name):
+            ev = torch.cuda.Event(enable_timing=True)
+            ev.record()
+            marks.append((name, ev))
+
+        barrier()
+        step(on_phase=mark)
+        torch.cuda.synchronize()
+        spans = [(f"{marks[i - 1][0]} -> {marks[i][0]}", marks[i - 1][1].elapsed_time(marks[i][1]))
+                 for i in range(1, len(marks))]
+        tp = torch.tensor([ms for _, ms in spans], device=device, dtype=torch.float64)
+        if world > 1:
+            dist.all_reduce(tp, op=dist.ReduceOp.MAX)
+        phases = {name: round(float(ms), 4) for (name, _), ms in zip(spans, tp.tolist())}
 
     # end to end through the public API with host buffers: queries H2D from pinned
     # memory, search, (dists, ids) D2H into pinned memory, every step
@@ -367,6 +424,7 @@ def main(argv=None) -> int:
             "e2e": e2e,
             "gpu_launches": launches * a.steps,
             "clocks": clocks,
+            "phases_ms_max_over_ranks": phases,
             "search_stats": {kk: stats[kk] for kk in ("candidates", "max_query_candidates",
                                                        "survivors", "fallback_queries", "slices")},
         }

@@ -277,12 +277,15 @@ __device__ __forceinline__ void tma_load_2d_pair(void *smem_dst, const void *tma
       "l"(reinterpret_cast<uint64_t>(tmap)), "r"(smem_u32(bar) & 0xFEFFFFFFu), "r"(x), "r"(y)
       : "memory");
 }
-// arrive on the barrier at the same offset in CTA `rank` of the cluster
+// arrive on the barrier at the same offset in CTA `rank` of the cluster.  The arrive
+// releases at CTA scope (the default): the waiting thread needs only the order of the
+// arriving thread's tensor-memory reads (fenced by tcgen05.fence::before_thread_sync),
+// not its global stores, which a cluster-scope release would first wait for.
 __device__ __forceinline__ void mbar_arrive_cluster(uint64_t *bar, uint32_t rank) {
   asm volatile(
       "{\n\t.reg .b32 ra;\n\t"
       "mapa.shared::cluster.u32 ra, %0, %1;\n\t"
-      "mbarrier.arrive.release.cluster.shared::cluster.b64 _, [ra];\n\t}" ::"r"(smem_u32(bar)),
+      "mbarrier.arrive.shared::cluster.b64 _, [ra];\n\t}" ::"r"(smem_u32(bar)),
       "r"(rank)
       : "memory");
 }

@@ -47,7 +47,8 @@ def unpack_lists(blocks: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
     return blocks[:, 0].contiguous().view(torch.float32), blocks[:, 1].contiguous()
 
 
-def make_local_search(group=None, plan_rows: int = 0, **search_kwargs) -> Callable:
+def make_local_search(group=None, plan_rows: int = 0, on_phase: Callable | None = None,
+                      **search_kwargs) -> Callable:
     """The per-shard search of `sharded_search` with the CUDA engine.
 
     Every rank must use the same `plan_rows` (the largest shard's row count);
@@ -55,15 +56,24 @@ def make_local_search(group=None, plan_rows: int = 0, **search_kwargs) -> Callab
     smallest shard, so that every rank raises if one shard is empty.  With more
     than one rank, the engine's level hook all-reduces (MIN) each query's bounds
     over `group` after every filter level; `search_kwargs` go to `engine.search`.
+    `on_phase(name)`, if given, is called at each level's all-reduce, before
+    ("level i filtered") and after it ("level i shared"), as the work is enqueued.
     """
     from .engine import search
     world = dist.get_world_size(group) if dist.is_initialized() else 1
     state = {"plan_rows": int(plan_rows)}
     empty = "every shard of a sharded search needs at least one row"
 
+    level = [0]
+
     def share_bounds(t):
         # both halves of `t` are minimised: see bfk_level_hook_t
+        if on_phase is not None:
+            on_phase(f"level {level[0]} filtered")
         dist.all_reduce(t, op=dist.ReduceOp.MIN, group=group)
+        if on_phase is not None:
+            on_phase(f"level {level[0]} shared")
+        level[0] += 1
 
     def local_search(Q_, X_, k_, id_offset):
         if world > 1 and state["plan_rows"] <= 0:
@@ -78,6 +88,7 @@ def make_local_search(group=None, plan_rows: int = 0, **search_kwargs) -> Callab
             # with `plan_rows` given there is no size exchange: the other shards learn
             # of this one when their bound all-reduce runs out of time
             raise ValueError(empty)
+        level[0] = 0
         return search(Q_, X_, k_, id_offset=id_offset,
                       bound_hook=share_bounds if world > 1 else None,
                       plan_rows=state["plan_rows"] if world > 1 else 0,
@@ -89,6 +100,7 @@ def make_local_search(group=None, plan_rows: int = 0, **search_kwargs) -> Callab
 def sharded_search(Q, X_shard, k: int, row_begin: int, group=None,
                    local_search: Callable | None = None,
                    merge_fn: Callable | None = None, plan_rows: int = 0,
+                   on_phase: Callable | None = None,
                    **search_kwargs) -> tuple[torch.Tensor, torch.Tensor]:
     """Exact k-NN over the union of every rank's shard; result on every rank.
 
@@ -107,13 +119,25 @@ def sharded_search(Q, X_shard, k: int, row_begin: int, group=None,
     `local_search(Q, X, k, id_offset)` and `merge_fn(blocks, k)` (blocks: the
     gathered (world, 2, n, k) int32 lists) default to the CUDA engine; tests
     substitute CPU stand-ins to exercise the orchestration over gloo.
-    `search_kwargs` go to `engine.search`.
+    `search_kwargs` go to `engine.search`.  `on_phase(name)`, if given, is called
+    as each phase's work has been enqueued ("start", the level phases of
+    `make_local_search`, "searched", "gathered", "merged"), e.g. to record events.
     """
+    def phase(name):
+        if on_phase is not None:
+            on_phase(name)
+
     if local_search is None:
-        local_search = make_local_search(group, plan_rows, **search_kwargs)
+        local_search = make_local_search(group, plan_rows, on_phase=on_phase, **search_kwargs)
     if merge_fn is None:
         from .engine import merge_packed as merge_fn
+    phase("start")
     d_, i_ = local_search(Q, X_shard, k, row_begin)
+    phase("searched")
     if not dist.is_initialized() or dist.get_world_size(group) == 1:
         return d_, i_
-    return merge_fn(gather_lists(d_, i_, group), k)
+    blocks = gather_lists(d_, i_, group)
+    phase("gathered")
+    out = merge_fn(blocks, k)
+    phase("merged")
+    return out

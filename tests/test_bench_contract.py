@@ -29,7 +29,8 @@ def test_reference_arm_prints_one_contract_line():
     # the same config dict the repository arm prints for this run
     assert j["config"] == {"workload": "plumbing", "N": 65_536, "Q": 1_024, "d": 128, "k": 10,
                            "parallelism": "rowshard1", "rows_prepared_once": False,
-                           "l2": "inputs larger than L2 (database 0.03 GB), no flush"}
+                           "l2": "inputs fit in L2 (database 0.034 GB): 256 MB written before "
+                                 "each timed step, which is timed alone"}
     cb = j["cpu_baseline"]
     assert cb["kind"] == "port" and cb["cores"] >= 1 and cb["value"] == j["value"]
     assert "8 queries" in cb["sample"]
