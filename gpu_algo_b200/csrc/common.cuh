@@ -154,6 +154,69 @@ __device__ __forceinline__ bool mbar_wait_bounded(uint64_t *bar, uint32_t parity
   }
 }
 
+// non-blocking test of a phase
+__device__ __forceinline__ bool mbar_test_wait(uint64_t *bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+// Wait of the single-thread roles whose reaction time is on the tensor pipe's critical
+// path (the TMA producer and the MMA issuer): tests the phase without suspending the
+// thread; the abort flag and the wall-clock limit are checked every 256 tests.
+__device__ __forceinline__ bool mbar_wait_spin(uint64_t *bar, uint32_t parity,
+                                               volatile int *abort_flag) {
+  if (mbar_test_wait(bar, parity)) return true;
+  const uint64_t t0 = globaltimer_ns();
+  for (;;) {
+    for (int i = 0; i < 256; i++)
+      if (mbar_test_wait(bar, parity)) return true;
+    if (*abort_flag) return false;
+    if (globaltimer_ns() - t0 > kWaitLimitNs) return false;
+  }
+}
+// try_wait with relaxed semantics: no acquire ordering of this thread's later memory
+// operations after the phase.
+__device__ __forceinline__ bool mbar_try_wait_relaxed(uint64_t *bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.relaxed.cta.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+__device__ __forceinline__ bool mbar_wait_relaxed(uint64_t *bar, uint32_t parity,
+                                                  volatile int *abort_flag) {
+  if (mbar_try_wait_relaxed(bar, parity)) return true;
+  const uint64_t t0 = globaltimer_ns();
+  for (;;) {
+    for (int i = 0; i < 16; i++)
+      if (mbar_try_wait_relaxed(bar, parity)) return true;
+    if (*abort_flag) return false;
+    if (globaltimer_ns() - t0 > kWaitLimitNs) return false;
+  }
+}
+// The same with try_wait and no time hint (the hardware's own suspend limit).
+__device__ __forceinline__ bool mbar_wait_try(uint64_t *bar, uint32_t parity,
+                                              volatile int *abort_flag) {
+  if (mbar_try_wait(bar, parity)) return true;
+  const uint64_t t0 = globaltimer_ns();
+  for (;;) {
+    for (int i = 0; i < 16; i++)
+      if (mbar_try_wait(bar, parity)) return true;
+    if (*abort_flag) return false;
+    if (globaltimer_ns() - t0 > kWaitLimitNs) return false;
+  }
+}
+
 // ---------------------------------------------------------------------------
 // TMA (2D tiled loads, no multicast) and bulk copies
 // ---------------------------------------------------------------------------
@@ -339,6 +402,13 @@ __device__ __forceinline__ uint64_t umma_desc_k_sw128(uint32_t addr) {
   desc |= (uint64_t)1u << 46;                          // descriptor version (sm_100) [46,48)
   desc |= (uint64_t)2u << 61;                          // layout: SWIZZLE_128B [61,64)
   return desc;
+}
+
+// a descriptor from its two 32-bit words
+__device__ __forceinline__ uint64_t desc_from(uint32_t lo, uint32_t hi) {
+  uint64_t d;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(d) : "r"(lo), "r"(hi));
+  return d;
 }
 
 // Instruction descriptor for kind::f16: f16 x f16 -> f32, both K-major, M x N.

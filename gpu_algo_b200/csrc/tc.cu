@@ -323,6 +323,13 @@ __global__ void __maxnreg__(96)
       const uint32_t stage = L.stage;
       const uint32_t a_addr = smem_u32(sA), b_addr = smem_u32(sB);
       const uint32_t boff = L.stream_a ? kAChunkBytes : 0;
+      // shared-memory descriptors, split into the 32-bit word holding the start address
+      // (which the loop advances) and the constant upper word
+      const uint64_t d0 = umma_desc_k_sw128(0);
+      const uint32_t desc_hi = (uint32_t)(d0 >> 32);
+      const uint32_t a_lo0 = (uint32_t)umma_desc_k_sw128(a_addr);
+      const uint32_t sa_lo0 = (uint32_t)umma_desc_k_sw128(b_addr);          // streamed query chunk
+      const uint32_t b_lo0 = (uint32_t)umma_desc_k_sw128(b_addr + boff);
       bool ok = L.stream_a || mbar_wait_bounded(a_full, 0, abort_flag);
       if (!ok) set_error(a.hdr, ERR_TIMEOUT_MMA, abort_flag);
       uint32_t it = 0;
@@ -343,11 +350,14 @@ __global__ void __maxnreg__(96)
             break;
           }
           tc_fence_after();
+          // descriptors of this chunk: the start-address field moves by 32 bytes per K step
+          const uint32_t b_lo = b_lo0 + st * (stage >> 4);
+          const uint32_t a_lo = L.stream_a ? sa_lo0 + st * (stage >> 4)
+                                           : a_lo0 + (uint32_t)c * (kAChunkBytes >> 4);
 #pragma unroll
           for (int kk = 0; kk < kBK / 16; kk++) {
-            const uint32_t a_chunk = L.stream_a ? b_addr + st * stage : a_addr + c * kAChunkBytes;
-            const uint64_t ad = umma_desc_k_sw128(a_chunk + kk * 32);
-            const uint64_t bd = umma_desc_k_sw128(b_addr + st * stage + boff + kk * 32);
+            const uint64_t ad = desc_from(a_lo + 2u * kk, desc_hi);
+            const uint64_t bd = desc_from(b_lo + 2u * kk, desc_hi);
             if (PAIR) tc_mma_f16_pair(d_tmem, ad, bd, idesc, (c | kk) != 0);
             else tc_mma_f16(d_tmem, ad, bd, idesc, (c | kk) != 0);
           }
