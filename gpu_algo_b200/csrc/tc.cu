@@ -50,7 +50,9 @@ constexpr int kBChunkBytes = kBN * kBK * 2;   // 32 KB
 constexpr int kEpiWarps = 16;       // four warps per TMEM lane quarter, one per 64-column group
 constexpr int kColGroups = 4;       // column groups of a tile (regions per slice)
 constexpr int kGroupN = kBN / kColGroups;  // accumulator columns an epilogue warp reads per tile
-constexpr int kTcThreads = 64 + 32 * kEpiWarps;  // warp 0 TMA, warp 1 MMA, 16 epilogue warps
+// warp 0 TMA, warps 1 and kIssuerWarp2 MMA (alternate tiles), warps 2 .. 17 epilogue
+constexpr int kIssuerWarp2 = 2 + kEpiWarps;
+constexpr int kTcThreads = 32 * (kIssuerWarp2 + 1);
 constexpr int kSmemLimit = 232448;  // 227 KB opt-in per block
 constexpr int kResidentKch = 4;     // d <= 256: the query tile stays in shared memory
 constexpr int kMaxKch = 16;         // d <= 1024: query K chunks stream with the row chunks
@@ -198,7 +200,27 @@ struct TileWalk {
   }
 };
 
-// 576 threads in one block: the launch admits at most 96 registers a thread.
+// The stage ring is split in two, one per MMA issuer: the chunks of tile lt pass
+// through ring lt & 1 (stages [base, base + count)) in order, so every ring has one
+// producer and one consumer, and a waiter is never more than one phase ahead of a
+// barrier (the condition for parity waits).
+struct StageRings {
+  uint32_t count[2], base[2];
+  __device__ __forceinline__ explicit StageRings(int ns) {
+    count[0] = (uint32_t)(ns + 1) / 2;
+    count[1] = (uint32_t)ns / 2;
+    base[0] = 0;
+    base[1] = count[0];
+  }
+  __device__ __forceinline__ uint32_t stage(int r, uint32_t pos) const {
+    return base[r] + pos % count[r];
+  }
+  __device__ __forceinline__ uint32_t parity(int r, uint32_t pos) const {
+    return (pos / count[r]) & 1u;
+  }
+};
+
+// 608 threads in one block (19 warps): at most 96 registers a thread.
 // PAIR: the kernel runs as clusters of two CTAs on two SMs.  The even CTA issues
 // tcgen05.mma.cta_group::2 with M = 256 (its query tile and its peer's) and
 // N = 256 rows, each CTA holding its query tile and half of each row tile; the
@@ -247,7 +269,7 @@ __global__ void __maxnreg__(96)
     // both CTAs' epilogues release the pair's accumulator on the even CTA's barrier
     mbar_init(acc_empty, PAIR ? 2 * kEpiWarps : kEpiWarps);
     mbar_init(acc_empty + 1, PAIR ? 2 * kEpiWarps : kEpiWarps);
-    mbar_init(drain, 1);
+    mbar_init(drain, 2);  // both MMA issuers commit
     *abort_flag = 0;
     *epi_stop = 0;
     fence_mbar_init();
@@ -281,17 +303,20 @@ __global__ void __maxnreg__(96)
           else tma_load_2d(sA + c * kAChunkBytes, &tmap_q, a_full, c * kBK, qt * kBM);
         }
       }
-      uint32_t it = 0;
+      uint32_t issued[2] = {0u, 0u};  // chunks loaded into each ring
       bool ok = true;
       const uint32_t bchunk = L.bchunk, stage = L.stage;
       const uint32_t boff = L.stream_a ? kAChunkBytes : 0;  // row chunk after the query chunk
       const uint32_t tx = (PAIR ? 2 : 1) * (bchunk + (L.stream_a ? kAChunkBytes : 0));
+      const StageRings R(ns);
       TileWalk walk(a, j_begin);
       for (int lt = 0; lt < ntiles && ok; lt++, walk.next()) {
+        const int rg = lt & 1;
         // a pair's CTAs load rows [0, 128) and [128, 256) of the tile
         const int32_t row0 = (int32_t)(walk.tile * kBN) + (int32_t)(rank * (kBN / 2));
-        for (int c = 0; c < kch; c++, it++) {
-          const uint32_t st = it % ns, ph = (it / ns) & 1;
+        for (int c = 0; c < kch; c++) {
+          const uint32_t pos = issued[rg];
+          const uint32_t st = R.stage(rg, pos), ph = R.parity(rg, pos);
           if (!mbar_wait_bounded(empty + st, ph ^ 1, abort_flag)) {
             set_error(a.hdr, ERR_TIMEOUT_PRODUCER, abort_flag);
             ok = false;
@@ -305,20 +330,28 @@ __global__ void __maxnreg__(96)
           }
           if (PAIR) tma_load_2d_pair(sst + boff, &tmap_x, full + st, c * kBK, row0);
           else tma_load_2d(sst + boff, &tmap_x, full + st, c * kBK, row0);
+          issued[rg] = pos + 1;
         }
       }
       // every issued copy must land before the CTA may exit; in a pair the even
       // CTA's barriers count the peer's copies too, and the peer waits for it below
       if (rank == 0) {
-        const uint32_t first = it > (uint32_t)ns ? it - ns : 0;
-        for (uint32_t i = first; i < it; i++)
-          mbar_wait_bounded(full + (i % ns), (i / ns) & 1, abort_flag);
+        for (int rg = 0; rg < 2; rg++) {
+          const uint32_t first = issued[rg] > R.count[rg] ? issued[rg] - R.count[rg] : 0u;
+          for (uint32_t i = first; i < issued[rg]; i++)
+            mbar_wait_bounded(full + R.stage(rg, i), R.parity(rg, i), abort_flag);
+        }
         if (!L.stream_a) mbar_wait_bounded(a_full, 0, abort_flag);
       }
     }
-  } else if (warp == 1) {
-    // ---------------- MMA issuer ----------------
+  } else if (warp == 1 || warp == kIssuerWarp2) {
+    // ---------------- MMA issuers ----------------
+    // Two threads issue the MMAs, issuer X taking tiles X, X + 2, ... (accumulator
+    // buffer X).  A thread that waits on a barrier stops issuing for a while, and the
+    // tensor pipe keeps little work queued; with two issuers, one issues while the
+    // other waits.
     if (lane == 0 && ntiles > 0 && rank == 0) {
+      const int X = warp == 1 ? 0 : 1;
       constexpr uint32_t idesc = idesc_f16_f32(PAIR ? 2 * kBM : kBM, kBN);
       const uint32_t stage = L.stage;
       const uint32_t a_addr = smem_u32(sA), b_addr = smem_u32(sB);
@@ -332,9 +365,10 @@ __global__ void __maxnreg__(96)
       const uint32_t b_lo0 = (uint32_t)umma_desc_k_sw128(b_addr + boff);
       bool ok = L.stream_a || mbar_wait_bounded(a_full, 0, abort_flag);
       if (!ok) set_error(a.hdr, ERR_TIMEOUT_MMA, abort_flag);
-      uint32_t it = 0;
-      for (int lt = 0; lt < ntiles && ok; lt++) {
+      const StageRings R(ns);
+      for (int lt = X; lt < ntiles && ok; lt += 2) {
         const int b = lt & 1;
+        uint32_t pos = (uint32_t)(lt >> 1) * (uint32_t)kch;  // this tile's first chunk in ring X
         if (!mbar_wait_bounded(acc_empty + b, ((lt >> 1) & 1) ^ 1, abort_flag)) {
           set_error(a.hdr, ERR_TIMEOUT_MMA, abort_flag);
           ok = false;
@@ -342,8 +376,8 @@ __global__ void __maxnreg__(96)
         }
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + (uint32_t)(b * kBN);
-        for (int c = 0; c < kch && ok; c++, it++) {
-          const uint32_t st = it % ns, ph = (it / ns) & 1;
+        for (int c = 0; c < kch && ok; c++, pos++) {
+          const uint32_t st = R.stage(X, pos), ph = R.parity(X, pos);
           if (!mbar_wait_bounded(full + st, ph, abort_flag)) {
             set_error(a.hdr, ERR_TIMEOUT_MMA, abort_flag);
             ok = false;
@@ -374,7 +408,7 @@ __global__ void __maxnreg__(96)
       else tc_commit(drain);
       mbar_wait_bounded(drain, 0, abort_flag);
     }
-  } else {
+  } else if (warp < 2 + kEpiWarps) {
     // ------------- epilogue: one query per thread, 64 columns of each tile per warp -------------
     const int e = warp - 2;                   // 0..15
     const int quarter = warp & 3;             // TMEM lanes this warp may access (warp % 4)
