@@ -44,7 +44,8 @@ def _rank_main(rank, world, port, k, outdir):
         Q = torch.from_numpy(data.generate("mixture", 3, DIM, 0, N_QUERIES, centre_seed=2)).cuda()
         calls = []
         plan_rows = shard_range(N_ROWS, 0, world)[1]  # the largest shard is the first
-        inner = make_local_search(plan_rows=plan_rows, engine="tc_f16")
+        phases = []
+        inner = make_local_search(plan_rows=plan_rows, engine="tc_f16", on_phase=phases.append)
 
         def local(Qt, Xt, kk, off):
             d_, i_ = inner(Qt, Xt, kk, off)
@@ -62,6 +63,10 @@ def _rank_main(rank, world, port, k, outdir):
             return torch.from_numpy(d_), torch.from_numpy(i_)
 
         d_, i_ = sharded_search(Q, X, k, r0, local_search=local, merge_fn=merge)
+        # every filter level shares its bounds, and reports before and after doing so
+        levels = len(phases) // 2
+        assert levels >= 2 and phases == [f"level {i} {w}" for i in range(levels)
+                                          for w in ("filtered", "shared")], phases
         np.savez(os.path.join(outdir, f"r{rank}.npz"), d=d_.numpy(), i=i_.numpy(),
                  survivors=calls[0]["survivors"], err=calls[0]["device_error"])
     finally:

@@ -47,8 +47,10 @@ def _rank_main(rank, world, port, outdir):
             d_, i_ = oracle_merge(all_d.numpy(), all_i.numpy(), kk)
             return torch.from_numpy(d_), torch.from_numpy(i_)
 
+        phases = []
         d_, i_ = sharded_search(torch.from_numpy(Q), torch.from_numpy(X), k, r0,
-                                local_search=local, merge_fn=merge)
+                                local_search=local, merge_fn=merge, on_phase=phases.append)
+        assert phases == ["start", "searched", "gathered", "merged"], phases
         np.savez(os.path.join(outdir, f"r{rank}.npz"), d=d_.numpy(), i=i_.numpy(), r0=r0, r1=r1)
     finally:
         dist.destroy_process_group()
