@@ -87,13 +87,16 @@ struct FilterArgs {
 // ---------------------------------------------------------------------------
 // shared-memory layout of the filter kernel
 // ---------------------------------------------------------------------------
+// per epilogue warp and accumulator buffer: the group's 64 ||x||^2 values and the
+// minimum of each group of 8 of them
+constexpr int kNxStage = kGroupN + 8;
 
 struct TcLayout {
   int kch, ns;
   bool stream_a;    // the query tile's K chunks travel through the stages with the rows'
   uint32_t bchunk;  // bytes of one row-tile K chunk in this CTA (half of it in a CTA pair)
   uint32_t stage;   // bytes of one stage: [query chunk if stream_a] + row chunk
-  size_t a_off, b_off, bar_off, total;
+  size_t a_off, b_off, nx_off, bar_off, total;
 };
 __host__ __device__ inline TcLayout tc_layout(int kch, bool pair) {
   TcLayout L{};
@@ -103,11 +106,12 @@ __host__ __device__ inline TcLayout tc_layout(int kch, bool pair) {
   L.stage = L.bchunk + (L.stream_a ? kAChunkBytes : 0);
   L.a_off = 0;
   L.b_off = L.stream_a ? 0 : (size_t)kch * kAChunkBytes;
-  const size_t fixed = 256;  // barriers
+  const size_t fixed = (size_t)kEpiWarps * 2 * kNxStage * 4 + 256;
   size_t ns = ((size_t)kSmemLimit - 1024 - L.b_off - fixed) / L.stage;
   if (ns > 12) ns = 12;
   L.ns = (int)ns;
-  L.bar_off = L.b_off + (size_t)L.ns * L.stage;
+  L.nx_off = L.b_off + (size_t)L.ns * L.stage;
+  L.bar_off = L.nx_off + (size_t)kEpiWarps * 2 * kNxStage * 4;
   L.total = L.bar_off + 256 + 1024;  // + alignment slack
   return L;
 }
@@ -161,19 +165,12 @@ __device__ __forceinline__ float max16u(const uint32_t *a) {
   return fmaxf(max3f(m0, m1, m2), max3f(m3, m4, __uint_as_float(a[15])));
 }
 // the filter values of 8 columns: v = fma(c, acc, ||x||^2), one rounding each
-__device__ __forceinline__ void exact_v8(const uint32_t *acc, float c, const float *n, float *v) {
-#pragma unroll
-  for (int i = 0; i < 8; i += 2)
-    fma2(__uint_as_float(acc[i]), __uint_as_float(acc[i + 1]), c, n[i], n[i + 1], v[i], v[i + 1]);
-}
-// ||x||^2 of the 16 rows of chunk j of a warp's 64-row group, from the lanes that hold
-// them (lane l holds rows 2l and 2l + 1); warp-collective
-__device__ __forceinline__ void chunk_norms(float2 nx, int j, float *n) {
-#pragma unroll
-  for (int i = 0; i < 8; i++) {
-    n[2 * i] = __shfl_sync(0xffffffffu, nx.x, 8 * j + i);
-    n[2 * i + 1] = __shfl_sync(0xffffffffu, nx.y, 8 * j + i);
-  }
+__device__ __forceinline__ void exact_v8(const uint32_t *acc, float c, float4 n0, float4 n1,
+                                         float *v) {
+  fma2(__uint_as_float(acc[0]), __uint_as_float(acc[1]), c, n0.x, n0.y, v[0], v[1]);
+  fma2(__uint_as_float(acc[2]), __uint_as_float(acc[3]), c, n0.z, n0.w, v[2], v[3]);
+  fma2(__uint_as_float(acc[4]), __uint_as_float(acc[5]), c, n1.x, n1.y, v[4], v[5]);
+  fma2(__uint_as_float(acc[6]), __uint_as_float(acc[7]), c, n1.z, n1.w, v[6], v[7]);
 }
 
 // the bound a level select wrote for query q (both halves when the shards share them)
@@ -236,6 +233,7 @@ __global__ void __maxnreg__(96)
   const TcLayout L = tc_layout(kch, PAIR);
   unsigned char *sA = smem + L.a_off;
   unsigned char *sB = smem + L.b_off;
+  float *nxs = reinterpret_cast<float *>(smem + L.nx_off);
   uint64_t *bars = reinterpret_cast<uint64_t *>(smem + L.bar_off);
   uint64_t *full = bars;                 // [ns]
   uint64_t *empty = bars + L.ns;         // [ns]
@@ -433,17 +431,44 @@ __global__ void __maxnreg__(96)
     const uint32_t taddr0 = tmem_base + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(cg * kGroupN);
     const float inv_sq = *a.inv_sq;
     const float nhsq = -0.5f * __frcp_rn(inv_sq);  // -s_q / 2 (powers of two, exact)
+    float *nxw = nxs + e * 2 * kNxStage;      // this warp's ||x||^2 staging, two buffers
+    // prefetch ||x||^2 (2 rows per lane) and the group record of the first tile
+    float2 pre_nx = make_float2(0.f, 0.f);
+    float4 pre_gmin = make_float4(0.f, 0.f, 0.f, 0.f), pre_sc = pre_gmin;
     TileWalk walk(a, j_begin);
+    if (ntiles > 0) {
+      const uint32_t t0 = walk.tile;
+      pre_nx = *reinterpret_cast<const float2 *>(a.xnorm + (size_t)t0 * kBN + cg * kGroupN + lane * 2);
+      pre_gmin = __ldg(a.xmeta + 2 * ((size_t)t0 * kColGroups + cg));
+      pre_sc = __ldg(a.xmeta + 2 * ((size_t)t0 * kColGroups + cg) + 1);
+    }
+
     for (int lt = 0; lt < ntiles; lt++) {
       const int b = lt & 1;
       const uint32_t tile = walk.tile;
-      walk.next();
-      // this tile's ||x||^2 (rows 2 lane, 2 lane + 1 of the warp's 64) and the group's
-      // record, loaded before the accumulator wait, which hides their latency
-      const size_t grp = (size_t)tile * kColGroups + cg;
-      const float2 nx = *reinterpret_cast<const float2 *>(a.xnorm + grp * kGroupN + lane * 2);
-      const float4 gmin = __ldg(a.xmeta + 2 * grp);
-      const float4 gsc = __ldg(a.xmeta + 2 * grp + 1);
+      walk.next();  // the walk is one tile ahead from here on
+      float *nxt = nxw + b * kNxStage;
+      *reinterpret_cast<float2 *>(nxt + lane * 2) = pre_nx;
+      // v = fma(c, acc, ||x||^2) with c = -2 / (s_q s_x), an exact power of two
+      const float cscale = -2.0f * inv_sq * pre_sc.x;
+      // Chunk thresholds: every v of 16-column chunk j exceeds theta when the chunk's
+      // largest accumulator is <= T_j = (theta2 - min ||x||^2) / c, rounded so that
+      // T_j is below the exact quotient (c < 0; 1/c = -s_q s_x / 2, exact when normal).
+      float T[4];
+      {
+        const float inv_c = nhsq * pre_sc.y;
+        const bool ok = fabsf(inv_c) >= FLT_MIN && fabsf(inv_c) <= FLT_MAX;
+        T[0] = ok ? __fmul_rd(__fsub_ru(theta2, pre_gmin.x), inv_c) : -INFINITY;
+        T[1] = ok ? __fmul_rd(__fsub_ru(theta2, pre_gmin.y), inv_c) : -INFINITY;
+        T[2] = ok ? __fmul_rd(__fsub_ru(theta2, pre_gmin.z), inv_c) : -INFINITY;
+        T[3] = ok ? __fmul_rd(__fsub_ru(theta2, pre_gmin.w), inv_c) : -INFINITY;
+      }
+      if (lt + 1 < ntiles) {
+        const uint32_t tn = walk.tile;
+        pre_nx = *reinterpret_cast<const float2 *>(a.xnorm + (size_t)tn * kBN + cg * kGroupN + lane * 2);
+        pre_gmin = __ldg(a.xmeta + 2 * ((size_t)tn * kColGroups + cg));
+        pre_sc = __ldg(a.xmeta + 2 * ((size_t)tn * kColGroups + cg) + 1);
+      }
       // tcgen05.ld is warp-collective: the whole warp proceeds or none of it
       const bool got = __all_sync(0xffffffffu, mbar_wait_bounded(acc_full + b, (lt >> 1) & 1,
                                                                  abort_flag));
@@ -452,39 +477,25 @@ __global__ void __maxnreg__(96)
         break;
       }
       tc_fence_after();
-      // v = fma(c, acc, ||x||^2) with c = -2 / (s_q s_x), an exact power of two
-      const float cscale = -2.0f * inv_sq * gsc.x;
-      // Chunk thresholds: every v of 16-column chunk j exceeds theta when the chunk's
-      // largest accumulator is <= T_j = (theta2 - min ||x||^2) / c, rounded so that
-      // T_j is below the exact quotient (c < 0; 1/c = -s_q s_x / 2, exact when normal).
-      float T[4];
-      {
-        const float inv_c = nhsq * gsc.y;
-        const bool ok = fabsf(inv_c) >= FLT_MIN && fabsf(inv_c) <= FLT_MAX;
-        T[0] = ok ? __fmul_rd(__fsub_ru(theta2, gmin.x), inv_c) : -INFINITY;
-        T[1] = ok ? __fmul_rd(__fsub_ru(theta2, gmin.y), inv_c) : -INFINITY;
-        T[2] = ok ? __fmul_rd(__fsub_ru(theta2, gmin.z), inv_c) : -INFINITY;
-        T[3] = ok ? __fmul_rd(__fsub_ru(theta2, gmin.w), inv_c) : -INFINITY;
-      }
       const uint32_t row0 = tile * kBN + (uint32_t)(cg * kGroupN);
       // 16 columns at a time; the load of the next 16 is in flight while these are checked
       uint32_t ra[16], rb[16];
       tmem_ld_32x32b_x16(taddr0 + (uint32_t)(b * kBN), ra);
       tmem_ld_wait(ra);
+      __syncwarp();  // the ||x||^2 staging written above is visible to every lane
 #pragma unroll
       for (int qq = 0; qq < 4; qq++) {
         uint32_t (&cur)[16] = (qq & 1) ? rb : ra;
         uint32_t (&nxb)[16] = (qq & 1) ? ra : rb;
         if (qq < 3) tmem_ld_32x32b_x16(taddr0 + (uint32_t)(b * kBN + (qq + 1) * 16), nxb);
+        const float4 *nx4 = reinterpret_cast<const float4 *>(nxt + qq * 16);
         const uint32_t rg = row0 + (uint32_t)(qq * 16);
         if (all_pass) {
           // no bound yet: every finite v is kept, one predicated store per column
-          float n16[16];
-          chunk_norms(nx, qq, n16);
 #pragma unroll
           for (int g = 0; g < 2; g++) {
             float v[8];
-            exact_v8(cur + 8 * g, cscale, n16 + 8 * g, v);
+            exact_v8(cur + 8 * g, cscale, nx4[2 * g], nx4[2 * g + 1], v);
 #pragma unroll
             for (int i = 0; i < 8; i++) {
               const bool keep = v[i] <= theta;
@@ -495,13 +506,10 @@ __global__ void __maxnreg__(96)
         } else {
           // one bound for the chunk: its largest accumulator against T
           const bool pass = max16u(cur) > T[qq];
-          if (__any_sync(0xffffffffu, pass)) {
-            float n16[16];
-            chunk_norms(nx, qq, n16);  // warp-collective
-            if (pass) {
+          if (pass) {
             float v[16];
-            exact_v8(cur, cscale, n16, v);
-            exact_v8(cur + 8, cscale, n16 + 8, v + 8);
+            exact_v8(cur, cscale, nx4[0], nx4[1], v);
+            exact_v8(cur + 8, cscale, nx4[2], nx4[3], v + 8);
             unsigned keep = 0;
 #pragma unroll
             for (int i = 0; i < 16; i++) keep |= (v[i] <= theta ? 1u : 0u) << i;
@@ -510,7 +518,6 @@ __global__ void __maxnreg__(96)
               keep &= keep - 1;
               region[min(cnt, last)] = make_uint2(rg + i, __float_as_uint(pick16(v, i)));
               cnt++;
-            }
             }
           }
         }
@@ -525,6 +532,7 @@ __global__ void __maxnreg__(96)
           }
         }
       }
+      __syncwarp();  // the staging buffer of this tile is reused two tiles later
     }
     if (valid) a.ccount[(size_t)q * kColGroups * a.max_slices + kColGroups * s + cg] = cnt;
   }
