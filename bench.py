@@ -63,7 +63,9 @@ def parse_args(argv=None):
     ap.add_argument("--queries", type=int, default=None, help="override the query count")
     ap.add_argument("--engine", default="auto", choices=["auto", "direct", "tc_f16"])
     ap.add_argument("--cta-pair", action="store_true",
-                    help="TC engine: CTA pairs (tcgen05.mma.cta_group::2)")
+                    help="TC engine: force CTA pairs (tcgen05.mma.cta_group::2)")
+    ap.add_argument("--single-cta", action="store_true",
+                    help="TC engine: no CTA pairs (by default the engine picks)")
     ap.add_argument("--prepared", action="store_true",
                     help="index use: the rows' TC form is prepared once, outside the timed "
                          "steps (bfk_prepare); the default step converts them every time")
@@ -259,9 +261,11 @@ def main(argv=None) -> int:
 
     prepared = engine.PreparedRows.prepare(Xd) if a.prepared else None
 
+    cta_pair = True if a.cta_pair else (False if a.single_cta else None)
+
     def step(time_main=False, Q_=None, on_phase=None):
         return sharded_search(Qd if Q_ is None else Q_, Xd, k, r0, plan_rows=plan_rows,
-                              engine=a.engine, time_main=time_main, cta_pair=a.cta_pair,
+                              engine=a.engine, time_main=time_main, cta_pair=cta_pair,
                               prepared=prepared, on_phase=on_phase)
 
     def barrier():
@@ -273,7 +277,7 @@ def main(argv=None) -> int:
     torch.cuda.synchronize()
     # the stats calls pass the search's own plan options (same workspace size)
     stat_opts = dict(engine=a.engine, plan_rows=plan_rows if world > 1 else 0,
-                     shards=world if world > 1 else 0, prepared=a.prepared)
+                     shards=world if world > 1 else 0, prepared=a.prepared, cta_pair=cta_pair)
     engine.last_stats(Qd, Xd, k, **stat_opts)  # clear timing records
     barrier()
     torch.cuda.synchronize()
@@ -419,6 +423,7 @@ def main(argv=None) -> int:
             "data": "synthetic",
             "config": bench_config(a, N, Qn, d, k),
             "engine": stats["engine"],
+            "cta_pair": stats["cta_pair"],
             "roofline": roofline,
             "cpu_baseline": cpu,
             "e2e": e2e,

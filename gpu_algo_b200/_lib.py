@@ -74,7 +74,7 @@ class Stats(ctypes.Structure):
                 ("slices", ctypes.c_int32), ("survivors", ctypes.c_int64),
                 ("device_error", ctypes.c_int32), ("kernel_launches", ctypes.c_int32),
                 ("timed_calls", ctypes.c_int32), ("main_kernel_ms", ctypes.c_float),
-                ("reserved", ctypes.c_int32 * 2)]
+                ("cta_pair", ctypes.c_int32), ("reserved", ctypes.c_int32 * 1)]
 
 
 class BfkError(RuntimeError):
@@ -161,6 +161,7 @@ def check(status: int, what: str) -> None:
 FLAG_TIME_MAIN = 1
 FLAG_CTA_PAIR = 2
 FLAG_PREPARED = 4
+FLAG_SINGLE_CTA = 8
 
 
 def make_opts(engine: str | int = "auto", slices: int = 0, max_candidates: int = 0,

@@ -75,8 +75,10 @@ DirectPlan direct_plan(int64_t n, int64_t m, int d, int k, int slices_req) {
 
 // the TC engine's plan under these options (BFK_FLAG_PREPARED: rows from a prepared buffer)
 bool make_plan(int64_t n, int64_t m, int32_t d, int32_t k, const bfk_opts_t *opts, TcPlan *p) {
+  const int flags = opts ? opts->flags : 0;
+  const int pair_mode = (flags & BFK_FLAG_CTA_PAIR) ? 1 : (flags & BFK_FLAG_SINGLE_CTA) ? -1 : 0;
   return tc_make_plan(n, m, d, k, opts ? opts->slices : 0, opts ? opts->max_candidates : 0,
-                      opts && (opts->flags & BFK_FLAG_CTA_PAIR), opts ? opts->plan_rows : 0,
+                      pair_mode, opts ? opts->plan_rows : 0,
                       opts && (opts->flags & BFK_FLAG_PREPARED), p);
 }
 
@@ -86,7 +88,10 @@ bool opts_ok(const bfk_opts_t *o) {
     if (o->reserved[i] != 0) return false;
   return o->engine >= BFK_ENGINE_AUTO && o->engine <= BFK_ENGINE_TC_F16 && o->slices >= 0 &&
          o->max_candidates >= 0 && o->plan_rows >= 0 && o->shards >= 0 &&
-         (o->flags & ~(BFK_FLAG_TIME_MAIN | BFK_FLAG_CTA_PAIR | BFK_FLAG_PREPARED)) == 0;
+         (o->flags & ~(BFK_FLAG_TIME_MAIN | BFK_FLAG_CTA_PAIR | BFK_FLAG_PREPARED |
+                       BFK_FLAG_SINGLE_CTA)) == 0 &&
+         (o->flags & (BFK_FLAG_CTA_PAIR | BFK_FLAG_SINGLE_CTA)) !=
+             (BFK_FLAG_CTA_PAIR | BFK_FLAG_SINGLE_CTA);
 }
 
 int choose_engine(int64_t n, int64_t m, int d, int k, const bfk_opts_t *o) {
@@ -499,8 +504,10 @@ bfk_status_t bfk_search_stats(const void *workspace, int64_t n, int64_t m, int32
   out->main_kernel_ms = total;
   if (eng == BFK_ENGINE_TC_F16) {
     TcPlan p;
-    if (make_plan(n, m, d, k, opts, &p))
+    if (make_plan(n, m, d, k, opts, &p)) {
       out->slices = p.slices;
+      out->cta_pair = p.pair ? 1 : 0;
+    }
   } else {
     out->slices = direct_plan(n, m, d, k, opts ? opts->slices : 0).slices;
   }

@@ -91,7 +91,9 @@ int tc_prepare(const float *X, int64_t m, int d, void *prep, cudaStream_t stream
 // error, 3 mismatch.
 int tc_check_prepared(const void *prep, int64_t m, int d);
 bool tc_supported(int d, int k);
-bool tc_make_plan(int64_t n, int64_t m, int d, int k, int slices, int cand_cap, bool pair,
+// pair_mode: 1 CTA pairs, -1 single CTAs, 0 tc_pair_default
+bool tc_pair_default(int d, int64_t n);
+bool tc_make_plan(int64_t n, int64_t m, int d, int k, int slices, int cand_cap, int pair_mode,
                   int64_t plan_rows, bool prepared, TcPlan *p);
 // Returns 0 ok, 1 CUDA error, 2 device timeout.  t0/t1 (may be null) are
 // recorded around the main kernel; *launches counts the kernels launched.

@@ -206,8 +206,8 @@ struct TileWalk {
 // barrier (the condition for parity waits).
 struct StageRings {
   uint32_t count0, count1;  // stages of ring 0 (first) and ring 1
-  __device__ __forceinline__ explicit StageRings(int ns)
-      : count0((uint32_t)(ns + 1) / 2), count1((uint32_t)ns / 2) {}
+  __device__ __forceinline__ StageRings(int ns, bool split)
+      : count0(split ? (uint32_t)(ns + 1) / 2 : (uint32_t)ns), count1(split ? (uint32_t)ns / 2 : 1u) {}
   __device__ __forceinline__ uint32_t count(int r) const { return r ? count1 : count0; }
   __device__ __forceinline__ uint32_t stage(int r, uint32_t pos) const {
     return r ? count0 + pos % count1 : pos % count0;
@@ -216,6 +216,10 @@ struct StageRings {
     return (pos / count(r)) & 1u;
   }
 };
+
+// Two MMA issuers only for tiles of at most two chunks (d <= 128): a longer tile does
+// not fit in half of the ring, and its loads would wait for the other issuer's tile.
+__host__ __device__ inline bool two_issuers(int kch) { return kch <= 2; }
 
 // 608 threads in one block (19 warps): at most 96 registers a thread.
 // PAIR: the kernel runs as clusters of two CTAs on two SMs.  The even CTA issues
@@ -266,7 +270,7 @@ __global__ void __maxnreg__(96)
     // both CTAs' epilogues release the pair's accumulator on the even CTA's barrier
     mbar_init(acc_empty, PAIR ? 2 * kEpiWarps : kEpiWarps);
     mbar_init(acc_empty + 1, PAIR ? 2 * kEpiWarps : kEpiWarps);
-    mbar_init(drain, 2);  // both MMA issuers commit
+    mbar_init(drain, two_issuers(kch) ? 2 : 1);  // every MMA issuer commits
     *abort_flag = 0;
     *epi_stop = 0;
     fence_mbar_init();
@@ -305,10 +309,11 @@ __global__ void __maxnreg__(96)
       const uint32_t bchunk = L.bchunk, stage = L.stage;
       const uint32_t boff = L.stream_a ? kAChunkBytes : 0;  // row chunk after the query chunk
       const uint32_t tx = (PAIR ? 2 : 1) * (bchunk + (L.stream_a ? kAChunkBytes : 0));
-      const StageRings R(ns);
+      const bool split = two_issuers(kch);
+      const StageRings R(ns, split);
       TileWalk walk(a, j_begin);
       for (int lt = 0; lt < ntiles && ok; lt++, walk.next()) {
-        const int rg = lt & 1;
+        const int rg = split ? (lt & 1) : 0;
         // a pair's CTAs load rows [0, 128) and [128, 256) of the tile
         const int32_t row0 = (int32_t)(walk.tile * kBN) + (int32_t)(rank * (kBN / 2));
         for (int c = 0; c < kch; c++) {
@@ -344,12 +349,14 @@ __global__ void __maxnreg__(96)
     }
   } else if (warp == 1 || warp == kIssuerWarp2) {
     // ---------------- MMA issuers ----------------
-    // Two threads issue the MMAs, issuer X taking tiles X, X + 2, ... (accumulator
-    // buffer X).  A thread that waits on a barrier stops issuing for a while, and the
-    // tensor pipe keeps little work queued; with two issuers, one issues while the
-    // other waits.
-    if (lane == 0 && ntiles > 0 && rank == 0) {
+    // For tiles of one or two chunks, two threads issue the MMAs, issuer X taking tiles
+    // X, X + 2, ... (accumulator buffer X): a thread that waits on a barrier stops
+    // issuing for a while, and the tensor pipe keeps little work queued, so with short
+    // tiles one issuer issues while the other waits.  Longer tiles use issuer 0 alone.
+    const bool split = two_issuers(kch);
+    if (lane == 0 && ntiles > 0 && rank == 0 && (split || warp == 1)) {
       const int X = warp == 1 ? 0 : 1;
+      const int step = split ? 2 : 1;
       constexpr uint32_t idesc = idesc_f16_f32(PAIR ? 2 * kBM : kBM, kBN);
       const uint32_t stage = L.stage;
       const uint32_t a_addr = smem_u32(sA), b_addr = smem_u32(sB);
@@ -363,10 +370,10 @@ __global__ void __maxnreg__(96)
       const uint32_t b_lo0 = (uint32_t)umma_desc_k_sw128(b_addr + boff);
       bool ok = L.stream_a || mbar_wait_bounded(a_full, 0, abort_flag);
       if (!ok) set_error(a.hdr, ERR_TIMEOUT_MMA, abort_flag);
-      const StageRings R(ns);
-      for (int lt = X; lt < ntiles && ok; lt += 2) {
+      const StageRings R(ns, split);
+      for (int lt = X; lt < ntiles && ok; lt += step) {
         const int b = lt & 1;
-        uint32_t pos = (uint32_t)(lt >> 1) * (uint32_t)kch;  // this tile's first chunk in ring X
+        uint32_t pos = (uint32_t)(lt / step) * (uint32_t)kch;  // this tile's first chunk in ring X
         if (!mbar_wait_bounded(acc_empty + b, ((lt >> 1) & 1) ^ 1, abort_flag)) {
           set_error(a.hdr, ERR_TIMEOUT_MMA, abort_flag);
           ok = false;
@@ -488,6 +495,17 @@ __global__ void __maxnreg__(96)
         uint32_t (&cur)[16] = (qq & 1) ? rb : ra;
         uint32_t (&nxb)[16] = (qq & 1) ? ra : rb;
         if (qq < 3) tmem_ld_32x32b_x16(taddr0 + (uint32_t)(b * kBN + (qq + 1) * 16), nxb);
+        if (qq == 2) {
+          // the last 16 columns are in registers: release the accumulator buffer to the
+          // MMA issuer before checking chunks 2 and 3
+          tmem_ld_wait(nxb);
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) {
+            if (PAIR) mbar_arrive_cluster(acc_empty + b, 0);
+            else mbar_arrive(acc_empty + b);
+          }
+        }
         const float4 *nx4 = reinterpret_cast<const float4 *>(nxt + qq * 16);
         const uint32_t rg = row0 + (uint32_t)(qq * 16);
         if (all_pass) {
@@ -505,32 +523,33 @@ __global__ void __maxnreg__(96)
           }
         } else {
           // one bound for the chunk: its largest accumulator against T
+          // The detail below is rare (a chunk with a candidate in some lane): a
+          // warp-uniform branch marked unlikely keeps the compiler from predicating it
+          // into every chunk.
           const bool pass = max16u(cur) > T[qq];
-          if (pass) {
-            float v[16];
-            exact_v8(cur, cscale, nx4[0], nx4[1], v);
-            exact_v8(cur + 8, cscale, nx4[2], nx4[3], v + 8);
-            unsigned keep = 0;
+          if (__builtin_expect(__any_sync(0xffffffffu, pass), 0) && pass) {
+            // a column can hold v <= theta only if its own accumulator exceeds T (the
+            // chunk test, column by column); those few get their exact v, the same
+            // single-rounding fma as exact_v8
+            float acc16[16];
+            unsigned maybe = 0;
 #pragma unroll
-            for (int i = 0; i < 16; i++) keep |= (v[i] <= theta ? 1u : 0u) << i;
-            while (keep) {
-              const int i = __ffs(keep) - 1;
-              keep &= keep - 1;
-              region[min(cnt, last)] = make_uint2(rg + i, __float_as_uint(pick16(v, i)));
-              cnt++;
+            for (int i = 0; i < 16; i++) {
+              acc16[i] = __uint_as_float(cur[i]);
+              maybe |= (acc16[i] > T[qq] ? 1u : 0u) << i;
+            }
+            while (maybe) {
+              const int i = __ffs(maybe) - 1;
+              maybe &= maybe - 1;
+              const float v = __fmaf_rn(pick16(acc16, i), cscale, nxt[qq * 16 + i]);
+              if (v <= theta) {
+                region[min(cnt, last)] = make_uint2(rg + i, __float_as_uint(v));
+                cnt++;
+              }
             }
           }
         }
-        if (qq < 3) tmem_ld_wait(nxb);
-        if (qq == 2) {
-          // every column of this warp is in registers: release them to the MMA warp
-          tc_fence_before();
-          __syncwarp();
-          if (lane == 0) {
-            if (PAIR) mbar_arrive_cluster(acc_empty + b, 0);
-            else mbar_arrive(acc_empty + b);
-          }
-        }
+        if (qq < 2) tmem_ld_wait(nxb);
       }
       __syncwarp();  // the staging buffer of this tile is reused two tiles later
     }
@@ -1647,7 +1666,13 @@ static void layout_workspace(TcPlan &P) {
   P.total = off;
 }
 
-bool tc_make_plan(int64_t n, int64_t m, int d, int k, int slices, int pool, bool pair,
+bool tc_pair_default(int d, int64_t n) {
+  // CTA pairs halve the row bytes each SM streams and measured faster for short tiles
+  // (d <= 256, the query tile resident); they need two query tiles
+  return kch_for(d) <= kResidentKch && n > kBM;
+}
+
+bool tc_make_plan(int64_t n, int64_t m, int d, int k, int slices, int pool, int pair_mode,
                   int64_t plan_rows, bool prepared, TcPlan *p) {
   if (!tc_supported(d, k) || n <= 0 || m <= 0) return false;
   TcPlan P{};
@@ -1657,8 +1682,10 @@ bool tc_make_plan(int64_t n, int64_t m, int d, int k, int slices, int pool, bool
   P.k = k;
   P.d_pad = kch_for(d) * kBK;
   P.q_tiles = (int)((n + kBM - 1) / kBM);
-  // CTA pairs (M = 256) on request, given two query tiles; the tile count is then even
-  P.pair = pair && P.q_tiles >= 2;
+  // CTA pairs (M = 256): forced (pair_mode > 0), off (< 0) or by tc_pair_default; they need
+  // two query tiles, and the tile count is then even
+  const bool want = pair_mode > 0 || (pair_mode == 0 && tc_pair_default(d, n));
+  P.pair = want && P.q_tiles >= 2;
   if (P.pair) P.q_tiles += P.q_tiles & 1;
   P.x_tiles = (m + kBN - 1) / kBN;
   P.cand_cap = pool > 0 ? pool : kDefaultPool;

@@ -64,9 +64,16 @@ class _DeviceArray:
                                          "version": 3, "strides": None, "stream": None}
 
 
+def _pair_flags(cta_pair) -> int:
+    """cta_pair: True forces CTA pairs, False single CTAs, None the engine's default."""
+    if cta_pair is None:
+        return 0
+    return _lib.FLAG_CTA_PAIR if cta_pair else _lib.FLAG_SINGLE_CTA
+
+
 def search(Q, X, k: int, *, engine: str = "auto", slices: int = 0, max_candidates: int = 0,
            id_offset: int = 0, out: tuple[torch.Tensor, torch.Tensor] | None = None,
-           ws: torch.Tensor | None = None, time_main: bool = False, cta_pair: bool = False,
+           ws: torch.Tensor | None = None, time_main: bool = False, cta_pair: bool | None = None,
            bound_hook=None, plan_rows: int = 0, shards: int = 0, prepared=None):
     """Exact k-NN on the GPU.  Returns (dists, ids) device tensors.
 
@@ -92,7 +99,7 @@ def search(Q, X, k: int, *, engine: str = "auto", slices: int = 0, max_candidate
     lib = _lib.load()
     opts = _lib.make_opts(engine, slices, max_candidates,
                           (_lib.FLAG_TIME_MAIN if time_main else 0) |
-                          (_lib.FLAG_CTA_PAIR if cta_pair else 0))
+                          _pair_flags(cta_pair))
     opts.plan_rows = int(plan_rows)
     opts.shards = int(shards)
     if prepared is not None:
@@ -194,14 +201,14 @@ class PreparedRows:
 
 def last_stats(Q, X, k: int, *, engine: str = "auto", slices: int = 0,
                max_candidates: int = 0, plan_rows: int = 0, shards: int = 0,
-               prepared: bool = False) -> dict:
+               prepared: bool = False, cta_pair: bool | None = None) -> dict:
     """Statistics of the last search of this shape on the current stream's workspace
     (pass the search's own engine options)."""
     Q = as_device_f32(Q, "Q")
     X = as_device_f32(X, "X")
     n, d = Q.shape
     m = X.shape[0]
-    opts = _lib.make_opts(engine, slices, max_candidates)
+    opts = _lib.make_opts(engine, slices, max_candidates, _pair_flags(cta_pair))
     opts.plan_rows = int(plan_rows)
     opts.shards = int(shards)
     if prepared:
@@ -224,6 +231,7 @@ def last_stats(Q, X, k: int, *, engine: str = "auto", slices: int = 0,
         "kernel_launches": s.kernel_launches,
         "timed_calls": s.timed_calls,
         "main_kernel_ms": s.main_kernel_ms,
+        "cta_pair": bool(s.cta_pair),
     }
 
 

@@ -54,9 +54,12 @@ typedef enum {
 } bfk_engine_t;
 
 #define BFK_FLAG_TIME_MAIN 1 /* time the main kernel of every call with CUDA events      */
-#define BFK_FLAG_CTA_PAIR 2  /* TC engine: CTA pairs (tcgen05.mma.cta_group::2, M = 256)  */
+#define BFK_FLAG_CTA_PAIR 2  /* TC engine: CTA pairs (tcgen05.mma.cta_group::2, M = 256);
+                                without it or BFK_FLAG_SINGLE_CTA, pairs are used for
+                                d <= 256 and more than 128 queries                      */
 #define BFK_FLAG_PREPARED 4  /* the search reads its rows' TC form from a prepared buffer
                                 (bfk_search_prepared); the workspace then holds no rows */
+#define BFK_FLAG_SINGLE_CTA 8 /* TC engine: one CTA per query tile (no CTA pairs)         */
 
 /*
  * Called by the TC engine after each filter level with `bound` (device, `count`
@@ -110,7 +113,8 @@ typedef struct {
   int32_t kernel_launches;     /* kernels the last call launched                         */
   int32_t timed_calls;         /* calls timed since the last read (BFK_FLAG_TIME_MAIN)   */
   float main_kernel_ms;        /* summed main-kernel time of those calls                 */
-  int32_t reserved[2];
+  int32_t cta_pair;            /* TC engine: the plan uses CTA pairs                     */
+  int32_t reserved[1];
 } bfk_stats_t;
 
 /* Library version.  No reference counterpart. */

@@ -243,10 +243,10 @@ def test_tc_streamed_query_tiles_high_d(d):
     Q = rng.standard_normal((200, d), dtype=np.float32)
     assert tc_ok(d, 100)
     ed, ei = oracle_knn(Q, X, 100)
-    for pair in (True, False):  # the stats below read the last (single-CTA) search
+    for pair in (True, None, False):  # the stats below read the last (single-CTA) search
         d_, i_ = run(Q, X, 100, engine="tc_f16", cta_pair=pair)
         assert_exact(d_, i_, ed, ei, f"tc d={d} pair={pair}")
-    st = engine.last_stats(dev(Q), dev(X), 100, engine="tc_f16")
+    st = engine.last_stats(dev(Q), dev(X), 100, engine="tc_f16", cta_pair=False)
     assert st["engine"] == "tc_f16" and st["device_error"] == 0
 
 
@@ -314,6 +314,12 @@ def test_bf_dropin_runners(plumbing):
 
 def test_tc_cta_pair_bit_exact(plumbing):
     X, Q, gd, gi = plumbing
+    # one CTA per query tile, and the engine's own choice (pairs for this shape)
+    for choice, want in ((False, False), (None, True)):
+        d_, i_ = engine.search(dev(Q), dev(X), 10, engine="tc_f16", cta_pair=choice)
+        st = engine.last_stats(dev(Q), dev(X), 10, engine="tc_f16", cta_pair=choice)
+        assert st["cta_pair"] is want
+        assert_exact(d_.cpu().numpy(), i_.cpu().numpy(), gd, gi, f"cta_pair={choice}")
     d_, i_ = engine.search(dev(Q), dev(X), 10, engine="tc_f16", cta_pair=True)
     torch.cuda.synchronize()
     assert_exact(d_.cpu().numpy(), i_.cpu().numpy(), gd, gi, "cta pair")

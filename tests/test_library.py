@@ -49,6 +49,8 @@ def test_argument_validation_without_gpu(lib):
     assert lib.bfk_workspace_size(10, 10, 8, 5000, ctypes.byref(o), ctypes.byref(nb)) == 2
     o.reserved[2] = 1
     assert lib.bfk_workspace_size(10, 10, 8, 1, ctypes.byref(o), ctypes.byref(nb)) == 1
+    o = _lib.make_opts(flags=_lib.FLAG_CTA_PAIR | _lib.FLAG_SINGLE_CTA)  # contradictory
+    assert lib.bfk_workspace_size(10, 10, 8, 1, ctypes.byref(o), ctypes.byref(nb)) == 1
     o = _lib.make_opts()
     o.shards = -1
     assert lib.bfk_workspace_size(10, 10, 8, 1, ctypes.byref(o), ctypes.byref(nb)) == 1
