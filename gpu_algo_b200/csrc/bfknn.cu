@@ -79,6 +79,7 @@ bool make_plan(int64_t n, int64_t m, int32_t d, int32_t k, const bfk_opts_t *opt
   const int pair_mode = (flags & BFK_FLAG_CTA_PAIR) ? 1 : (flags & BFK_FLAG_SINGLE_CTA) ? -1 : 0;
   return tc_make_plan(n, m, d, k, opts ? opts->slices : 0, opts ? opts->max_candidates : 0,
                       pair_mode, opts ? opts->plan_rows : 0,
+                      opts && opts->level_hook ? opts->shards : 0,
                       opts && (opts->flags & BFK_FLAG_PREPARED), p);
 }
 

@@ -77,6 +77,16 @@ __device__ __forceinline__ void warp_insert(float *ld, int32_t *li, int &cnt, in
   cnt = newcnt;
 }
 
+// Database slices of the exact fallback for `count` queries: as many as its partial
+// lists (part_entries entries) hold, at most 512 and one per 1024 rows, at least one.
+__host__ __device__ inline int64_t fallback_slices(int64_t count, int64_t m, int k,
+                                                   int64_t part_entries) {
+  int64_t s = count > 0 ? part_entries / (count * (int64_t)k) : 1;
+  if (s > 512) s = 512;
+  if (s > (m + 1023) / 1024) s = (m + 1023) / 1024;
+  return s < 1 ? 1 : s;
+}
+
 // The reference kernels' distance step (bf/fp32.py:80), spelled out so that
 // no other contraction can happen: dif = q - x (rounded), acc = fma(dif, dif, acc).
 __device__ __forceinline__ float dist_step(float q, float x, float acc) {

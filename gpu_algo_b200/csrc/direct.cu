@@ -18,27 +18,21 @@ namespace bfk {
 constexpr int kDirRT = 128;  // database rows per tile
 constexpr int kDirDC = 32;   // dimensions per chunk
 
-// grid (ceil(n / QB), slices); block 256 threads.
-// Slice s covers rows [s*slice_len, min((s+1)*slice_len, m)).  With one slice
-// the sorted top-k goes to (out_d, out_i) (n, k); with more, slice s writes
-// its sorted list to out + s*n*k for a later merge.
+// One block's work: queries [qb0, qb0 + QB) against rows [rbeg, rend), the sorted top-k of
+// each written to (out_d, out_i) (n, k).
 template <int TQ>
-__global__ void __launch_bounds__(256) knn_direct_kernel(const float *__restrict__ Q, int64_t n,
-                                                         const float *__restrict__ X, int64_t m,
-                                                         int d, int k, int64_t slice_len,
-                                                         int64_t id_offset, float *out_d,
-                                                         int32_t *out_i) {
+__device__ __forceinline__ void direct_block(const float *__restrict__ Q, int64_t n,
+                                             const float *__restrict__ X, int d, int k,
+                                             int64_t qb0, int64_t rbeg, int64_t rend,
+                                             int64_t id_offset, float *out_d, int32_t *out_i,
+                                             unsigned char *smem_raw) {
   constexpr int QB = 8 * TQ;
-  extern __shared__ __align__(16) unsigned char smem_raw[];
   float *xs = reinterpret_cast<float *>(smem_raw);          // [kDirRT][kDirDC + 1]
   float *qs = xs + kDirRT * (kDirDC + 1);                    // [kDirDC][QB]
   float *lists_d = qs + kDirDC * QB;                         // [QB][k]
   int32_t *lists_i = reinterpret_cast<int32_t *>(lists_d + QB * k);  // [QB][k]
 
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  const int64_t qb0 = (int64_t)blockIdx.x * QB;
-  const int64_t rbeg = (int64_t)blockIdx.y * slice_len;
-  const int64_t rend = rbeg + slice_len < m ? rbeg + slice_len : m;
 
   int cnt[TQ];
   float kth_d[TQ];
@@ -119,7 +113,6 @@ __global__ void __launch_bounds__(256) knn_direct_kernel(const float *__restrict
 
   // emit
   __syncwarp();
-  const bool partial = gridDim.y > 1;
 #pragma unroll
   for (int i = 0; i < TQ; i++) {
     const int ql = warp * TQ + i;
@@ -127,13 +120,59 @@ __global__ void __launch_bounds__(256) knn_direct_kernel(const float *__restrict
     if (qi >= n) continue;
     const float *ld = lists_d + ql * k;
     const int32_t *li = lists_i + ql * k;
-    float *od = out_d + (partial ? (int64_t)blockIdx.y * n * k : 0) + qi * k;
-    int32_t *oi = out_i + (partial ? (int64_t)blockIdx.y * n * k : 0) + qi * k;
+    float *od = out_d + qi * k;
+    int32_t *oi = out_i + qi * k;
     for (int e = lane; e < k; e += 32) {
       const bool have = e < cnt[i];
       od[e] = have ? ld[e] : BFK_PAD_DIST;
       oi[e] = have ? li[e] : -1;
     }
+  }
+}
+
+// grid (ceil(n / QB), slices); block 256 threads.
+// Slice s covers rows [s*slice_len, min((s+1)*slice_len, m)).  With one slice
+// the sorted top-k goes to (out_d, out_i) (n, k); with more, slice s writes
+// its sorted list to out + s*n*k for a later merge.
+template <int TQ>
+__global__ void __launch_bounds__(256) knn_direct_kernel(const float *__restrict__ Q, int64_t n,
+                                                         const float *__restrict__ X, int64_t m,
+                                                         int d, int k, int64_t slice_len,
+                                                         int64_t id_offset, float *out_d,
+                                                         int32_t *out_i) {
+  extern __shared__ __align__(16) unsigned char smem_raw[];
+  const int64_t rbeg = (int64_t)blockIdx.y * slice_len;
+  const int64_t rend = rbeg + slice_len < m ? rbeg + slice_len : m;
+  const int64_t off = gridDim.y > 1 ? (int64_t)blockIdx.y * n * k : 0;
+  direct_block<TQ>(Q, n, X, d, k, (int64_t)blockIdx.x * (8 * TQ), rbeg, rend, id_offset,
+                   out_d + off, out_i + off, smem_raw);
+}
+
+// The same search for a query count known only on the device (*count): the exact
+// fallback of the tensor-core engine, launched whether or not any query needs it, so
+// the host never waits for the count.  Runs only when lo <= *count < hi (one launch
+// per block shape).  The (query block, slice) items are taken grid-stride; the slice
+// count is fallback_slices(*count, ...), and slice s writes its sorted lists to
+// out + s * count * k.
+template <int TQ>
+__global__ void __launch_bounds__(256) knn_direct_count_kernel(
+    const float *__restrict__ Q, const int *__restrict__ count, int lo, int hi,
+    const float *__restrict__ X, int64_t m, int d, int k, int64_t id_offset,
+    int64_t part_entries, float *out_d, int32_t *out_i) {
+  extern __shared__ __align__(16) unsigned char smem_raw[];
+  const int64_t n = *count;
+  if (n < lo || n >= hi || n == 0) return;
+  constexpr int QB = 8 * TQ;
+  const int64_t slices = fallback_slices(n, m, k, part_entries);
+  const int64_t slice_len = ((m + slices - 1) / slices + kDirRT - 1) / kDirRT * kDirRT;
+  const int64_t qblocks = (n + QB - 1) / QB;
+  for (int64_t item = blockIdx.x; item < qblocks * slices; item += gridDim.x) {
+    const int64_t qb = item / slices, sl = item - qb * slices;
+    const int64_t rbeg = sl * slice_len;
+    const int64_t rend = rbeg + slice_len < m ? rbeg + slice_len : m;
+    __syncthreads();  // the previous item's lists are no longer read
+    direct_block<TQ>(Q, n, X, d, k, qb * QB, rbeg, rend, id_offset, out_d + sl * n * k,
+                     out_i + sl * n * k, smem_raw);
   }
 }
 
@@ -145,6 +184,27 @@ size_t direct_smem_bytes(int tq, int k) {
 
 const void *direct_kernel_ptr(int tq) {
   return tq >= 4 ? (const void *)knn_direct_kernel<4> : (const void *)knn_direct_kernel<1>;
+}
+
+cudaError_t launch_direct_count(const float *Q, const int *count, const float *X, int64_t m,
+                                int d, int k, int64_t id_offset, int64_t part_entries,
+                                float *out_d, int32_t *out_i, cudaStream_t stream) {
+  // few queries: 8 per block; many: 32 per block
+  const int grid = 2 * 148;
+  for (int tq : {1, 4}) {
+    const size_t smem = direct_smem_bytes(tq, k);
+    const void *fn = tq == 4 ? (const void *)knn_direct_count_kernel<4>
+                             : (const void *)knn_direct_count_kernel<1>;
+    cudaError_t e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (e != cudaSuccess) return e;
+    if (tq == 4)
+      knn_direct_count_kernel<4><<<grid, 256, smem, stream>>>(Q, count, 64, 0x7fffffff, X, m, d, k,
+                                                              id_offset, part_entries, out_d, out_i);
+    else
+      knn_direct_count_kernel<1><<<grid, 256, smem, stream>>>(Q, count, 1, 64, X, m, d, k,
+                                                              id_offset, part_entries, out_d, out_i);
+  }
+  return cudaGetLastError();
 }
 
 cudaError_t launch_direct(const float *Q, int64_t n, const float *X, int64_t m, int d, int k,

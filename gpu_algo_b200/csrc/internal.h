@@ -17,6 +17,12 @@ cudaError_t launch_direct(const float *Q, int64_t n, const float *X, int64_t m, 
                           int64_t id_offset, int slices, int tq, float *out_d, int32_t *out_i,
                           cudaStream_t stream);
 
+// the exact search for a query count held on the device (the tensor-core engine's
+// fallback): lists of fallback_slices(*count, ...) slices, slice s at out + s * count * k
+cudaError_t launch_direct_count(const float *Q, const int *count, const float *X, int64_t m,
+                                int d, int k, int64_t id_offset, int64_t part_entries,
+                                float *out_d, int32_t *out_i, cudaStream_t stream);
+
 // merge.cu -- sorted-list merge
 // streaming scan for n <= 16 queries (scan.cu): `blocks` row ranges, each writing its
 // sorted top-k per query to out + b*n*k
@@ -32,6 +38,10 @@ cudaError_t launch_merge_strided(const float *cand_d, const int32_t *cand_i, int
                                  int k, int64_t stride, float *out_d, int32_t *out_i,
                                  cudaStream_t stream);
 int merge_max_k();
+// merge of launch_direct_count's lists, query q written to output row list[q]
+cudaError_t launch_merge_count(const float *cand_d, const int32_t *cand_i, const int *count,
+                               int64_t m, int k, int64_t part_entries, const int *list,
+                               float *out_d, int32_t *out_i, cudaStream_t stream);
 // the kernel launch_merge runs for `lists` lists of k, and its dynamic shared memory
 const void *merge_kernel_for(int lists, int k, size_t *smem);
 int merge_threads();
@@ -60,7 +70,7 @@ struct TcPlan {
   int cand_cap;     // candidate entries per query
   // workspace offsets (bytes from the workspace base)
   size_t off_xh, off_xnorm, off_xscale, off_qh, off_qinfo, off_rlev, off_cand, off_ccount,
-      off_flags, off_fbq, off_fbd, off_fbi, off_fbpart_d, off_fbpart_i, off_invsq, total;
+      off_flags, off_fbq, off_fbpart_d, off_fbpart_i, off_invsq, total;
   int fb_slices;
   bool prepared;    // the rows' f16 form, norms and scales come from a prepared buffer
 };
@@ -93,9 +103,11 @@ int tc_check_prepared(const void *prep, int64_t m, int d);
 bool tc_supported(int d, int k);
 // pair_mode: 1 CTA pairs, -1 single CTAs, 0 tc_pair_default
 bool tc_pair_default(int d, int64_t n);
+// shards > 1: the number of shards that share level bounds (their first level is smaller)
 bool tc_make_plan(int64_t n, int64_t m, int d, int k, int slices, int cand_cap, int pair_mode,
-                  int64_t plan_rows, bool prepared, TcPlan *p);
-// Returns 0 ok, 1 CUDA error, 2 device timeout.  t0/t1 (may be null) are
+                  int64_t plan_rows, int shards, bool prepared, TcPlan *p);
+// Returns 0 ok, 1 CUDA error; it does not wait for the stream (a device timeout is
+// left in the workspace header for bfk_search_stats).  t0/t1 (may be null) are
 // recorded around the main kernel; *launches counts the kernels launched.
 // `hook` (may be null) is called after every level with the level's bounds;
 // `shards` > 1 shards share them, which doubles the bounds handed to the hook.

@@ -29,13 +29,12 @@ __device__ void block_bitonic_sort(uint64_t *keys, int P) {
   __syncthreads();
 }
 
-// grid (n), block kMergeThreads, dynamic smem kMergeCap * 8.
-// cand: list l's (n, k) block starts `stride` elements after list l-1's -> out (n, k)
-__global__ void __launch_bounds__(kMergeThreads) knn_merge_kernel(
-    const float *__restrict__ cand_d, const int32_t *__restrict__ cand_i, int64_t n, int lists,
-    int k, int64_t stride, float *__restrict__ out_d, int32_t *__restrict__ out_i) {
-  extern __shared__ __align__(16) uint64_t keys[];
-  const int64_t qi = blockIdx.x;
+// The k best of query qi's `lists` sorted lists (list l at cand + l * stride + qi * k) into
+// (od, oi) (k entries), by one block: the lists are taken in groups so that any number
+// fits in kMergeCap keys, each group sorted with the survivors of the previous ones.
+__device__ void merge_block(const float *__restrict__ cand_d, const int32_t *__restrict__ cand_i,
+                            int64_t qi, int lists, int k, int64_t stride, float *od, int32_t *oi,
+                            uint64_t *keys) {
   const int group = (kMergeCap - k) / k;  // lists added per round (>= 1 since k <= kMergeCap/2)
   int have = 0;                           // keys carried from the previous round (sorted)
   for (int l0 = 0; l0 < lists; l0 += group) {
@@ -58,8 +57,37 @@ __global__ void __launch_bounds__(kMergeThreads) knn_merge_kernel(
   for (int j = threadIdx.x; j < k; j += blockDim.x) {
     const uint64_t key = keys[j];
     const bool pad = key == ~0ull;
-    out_d[qi * k + j] = pad ? BFK_PAD_DIST : ord2f((uint32_t)(key >> 32));
-    out_i[qi * k + j] = pad ? -1 : (int32_t)(uint32_t)(key & 0xffffffffu);
+    od[j] = pad ? BFK_PAD_DIST : ord2f((uint32_t)(key >> 32));
+    oi[j] = pad ? -1 : (int32_t)(uint32_t)(key & 0xffffffffu);
+  }
+  __syncthreads();  // the keys are reused by the block's next query
+}
+
+// grid (n), block kMergeThreads, dynamic smem kMergeCap * 8.
+// cand: list l's (n, k) block starts `stride` elements after list l-1's -> out (n, k)
+__global__ void __launch_bounds__(kMergeThreads) knn_merge_kernel(
+    const float *__restrict__ cand_d, const int32_t *__restrict__ cand_i, int64_t n, int lists,
+    int k, int64_t stride, float *__restrict__ out_d, int32_t *__restrict__ out_i) {
+  extern __shared__ __align__(16) uint64_t keys[];
+  const int64_t qi = blockIdx.x;
+  merge_block(cand_d, cand_i, qi, lists, k, stride, out_d + qi * k, out_i + qi * k, keys);
+}
+
+// The exact fallback's merge, for a query count known only on the device (*count):
+// the partial lists of fallback_slices(*count, ...) slices, laid out with stride
+// count * k, merged per query (grid-stride over the queries) and written to the row of
+// the output that list[q] names.
+__global__ void __launch_bounds__(kMergeThreads) knn_merge_count_kernel(
+    const float *__restrict__ cand_d, const int32_t *__restrict__ cand_i,
+    const int *__restrict__ count, int64_t m, int k, int64_t part_entries,
+    const int *__restrict__ list, float *__restrict__ out_d, int32_t *__restrict__ out_i) {
+  extern __shared__ __align__(16) uint64_t keys[];
+  const int64_t n = *count;
+  if (n == 0) return;
+  const int lists = (int)fallback_slices(n, m, k, part_entries);
+  for (int64_t qi = blockIdx.x; qi < n; qi += gridDim.x) {
+    const int64_t row = list[qi];
+    merge_block(cand_d, cand_i, qi, lists, k, n * k, out_d + row * k, out_i + row * k, keys);
   }
 }
 
@@ -133,6 +161,18 @@ cudaError_t launch_merge_strided(const float *cand_d, const int32_t *cand_i, int
 }
 
 int merge_max_k() { return kMergeCap / 2; }
+
+cudaError_t launch_merge_count(const float *cand_d, const int32_t *cand_i, const int *count,
+                               int64_t m, int k, int64_t part_entries, const int *list,
+                               float *out_d, int32_t *out_i, cudaStream_t stream) {
+  const size_t smem = (size_t)kMergeCap * sizeof(uint64_t);
+  cudaError_t e = cudaFuncSetAttribute((const void *)knn_merge_count_kernel,
+                                       cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  if (e != cudaSuccess) return e;
+  knn_merge_count_kernel<<<2 * 148, kMergeThreads, smem, stream>>>(
+      cand_d, cand_i, count, m, k, part_entries, list, out_d, out_i);
+  return cudaGetLastError();
+}
 
 const void *merge_kernel_for(int lists, int k, size_t *smem) {
   if (lists <= kRankMergeLists && (int64_t)lists * k <= kMergeCap) {

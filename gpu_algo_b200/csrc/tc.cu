@@ -1576,22 +1576,13 @@ __global__ void __launch_bounds__(kWarpFinalQueries * 32) tc_final_select_warp_k
   }
 }
 
-// fallback helpers: gather rows of Q; scatter merged rows back
+// fallback helper: the rows of Q that the final select listed (*count of them)
 __global__ void tc_gather_rows(const float *__restrict__ Q, int d, const int *__restrict__ list,
-                               int count, float *__restrict__ out) {
-  for (int64_t e = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; e < (int64_t)count * d;
+                               const int *__restrict__ count, float *__restrict__ out) {
+  const int64_t total = (int64_t)*count * d;
+  for (int64_t e = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; e < total;
        e += (int64_t)gridDim.x * blockDim.x)
     out[e] = Q[(int64_t)list[e / d] * d + e % d];
-}
-__global__ void tc_scatter_rows(const float *__restrict__ sd, const int32_t *__restrict__ si,
-                                int k, const int *__restrict__ list, int count,
-                                float *__restrict__ out_d, int32_t *__restrict__ out_i) {
-  for (int64_t e = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; e < (int64_t)count * k;
-       e += (int64_t)gridDim.x * blockDim.x) {
-    const int64_t q = list[e / k];
-    out_d[q * k + e % k] = sd[e];
-    out_i[q * k + e % k] = si[e];
-  }
 }
 
 // ---------------------------------------------------------------------------
@@ -1659,8 +1650,6 @@ static void layout_workspace(TcPlan &P) {
   P.off_ccount = off;   off = al256(off + (size_t)n * kColGroups * max_s * 4);
   P.off_flags = off;    off = al256(off + (size_t)n * 4);
   P.off_fbq = off;      off = al256(off + (size_t)n * d * 4);
-  P.off_fbd = off;      off = al256(off + (size_t)n * k * 4);
-  P.off_fbi = off;      off = al256(off + (size_t)n * k * 4);
   P.off_fbpart_d = off; off = al256(off + (size_t)P.fb_slices * n * k * 4);
   P.off_fbpart_i = off; off = al256(off + (size_t)P.fb_slices * n * k * 4);
   P.total = off;
@@ -1673,7 +1662,7 @@ bool tc_pair_default(int d, int64_t n) {
 }
 
 bool tc_make_plan(int64_t n, int64_t m, int d, int k, int slices, int pool, int pair_mode,
-                  int64_t plan_rows, bool prepared, TcPlan *p) {
+                  int64_t plan_rows, int shards, bool prepared, TcPlan *p) {
   if (!tc_supported(d, k) || n <= 0 || m <= 0) return false;
   TcPlan P{};
   P.n = n;
@@ -1719,6 +1708,16 @@ bool tc_make_plan(int64_t n, int64_t m, int d, int k, int slices, int pool, int 
     if (s > sizes[l - 1]) s = sizes[l - 1];
     if (s < 1) s = 1;
     sizes[l] = s;
+  }
+  // Shards that share bounds pool their first level: its bound is the smallest over the
+  // shards of each one's k-th value and the largest of each one's ceil(k / shards)-th, so
+  // each shard's first level needs only 2 ceil(k / shards) rows, and the shards together
+  // sample about as many rows as one search alone would.
+  if (shards > 1 && nl >= 3) {
+    const int64_t k2 = ((int64_t)k + shards - 1) / shards;
+    int64_t s0 = (sizes[nl - 1] + shards - 1) / shards;
+    if (s0 * kBN < 2 * k2) s0 = (2 * k2 + kBN - 1) / kBN;
+    if (s0 < sizes[nl - 1]) sizes[nl - 1] = s0;
   }
   P.levels = nl;
   const int sms = num_sms();
@@ -2038,38 +2037,22 @@ int tc_run(const float *Q, const float *X, int64_t id_offset, float *out_d, int3
   nl++;
   BFK_TRY(cudaGetLastError());
 
-  // queries the filter could not finish -> exact SIMT engine
-  int32_t h_fb = 0, h_err = 0;
-  BFK_TRY(cudaMemcpyAsync(&h_fb, &hdr->fallback, 4, cudaMemcpyDeviceToHost, stream));
-  BFK_TRY(cudaMemcpyAsync(&h_err, &hdr->error, 4, cudaMemcpyDeviceToHost, stream));
-  BFK_TRY(cudaStreamSynchronize(stream));
-  if (h_err) {
-    *launches = nl;
-    return 2;
-  }
-  if (h_fb > 0) {
+  // Queries the filter could not finish -> exact SIMT engine.  Their count stays on the
+  // device: the three kernels below run whether or not there are any (they return at
+  // once for none), so the host never waits for the stream here.
+  {
     float *Qf = reinterpret_cast<float *>(ws + p.off_fbq);
-    float *fd = reinterpret_cast<float *>(ws + p.off_fbd);
-    int32_t *fi = reinterpret_cast<int32_t *>(ws + p.off_fbi);
     float *pd = reinterpret_cast<float *>(ws + p.off_fbpart_d);
     int32_t *pi = reinterpret_cast<int32_t *>(ws + p.off_fbpart_i);
-    // as many database slices as the partial buffer holds for this many queries
+    const int *count = &hdr->fallback;
     const int64_t part_entries = (int64_t)p.fb_slices * p.n * p.k;
-    int64_t fbs = part_entries / ((int64_t)h_fb * p.k);
-    if (fbs > 512) fbs = 512;
-    if (fbs > (p.m + 1023) / 1024) fbs = (p.m + 1023) / 1024;
-    if (fbs < 1) fbs = 1;
-    tc_gather_rows<<<256, 256, 0, stream>>>(Q, p.d, fb_list, h_fb, Qf);
-    BFK_TRY(launch_direct(Qf, h_fb, X, p.m, p.d, p.k, id_offset, (int)fbs, h_fb >= 64 ? 4 : 1,
-                          fbs > 1 ? pd : fd, fbs > 1 ? pi : fi, stream));
-    nl += 2;
-    if (fbs > 1) {
-      BFK_TRY(launch_merge(pd, pi, h_fb, (int)fbs, p.k, fd, fi, stream));
-      nl++;
-    }
-    tc_scatter_rows<<<256, 256, 0, stream>>>(fd, fi, p.k, fb_list, h_fb, out_d, out_i);
-    nl++;
+    tc_gather_rows<<<256, 256, 0, stream>>>(Q, p.d, fb_list, count, Qf);
     BFK_TRY(cudaGetLastError());
+    BFK_TRY(launch_direct_count(Qf, count, X, p.m, p.d, p.k, id_offset, part_entries, pd, pi,
+                                stream));
+    BFK_TRY(launch_merge_count(pd, pi, count, p.m, p.k, part_entries, fb_list, out_d, out_i,
+                               stream));
+    nl += 4;
   }
   *launches = nl;
   return 0;

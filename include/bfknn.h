@@ -4,10 +4,11 @@
  * Drop-in boundary for the reference's `bf/` kernels (hantaoyu-theory/gpu_algo).
  * Every entry point takes plain pointers and sizes; device pointers are
  * caller-owned CUDA device memory, `stream` is a cudaStream_t (NULL = the
- * legacy default stream).  Launches go on that stream; the SIMT engine and
- * bfk_merge return without waiting for them, while a search on the tensor-core
- * engine waits for its stream before it returns (it reads back how many queries
- * need the exact fallback).  No entry point allocates device memory, calls
+ * legacy default stream).  Launches go on that stream, and the searches and
+ * bfk_merge return without waiting for them (bfk_prepare, bfk_filter_values and
+ * bfk_search_stats wait).  A kernel's bounded wait that runs out (a device fault the
+ * search cannot report at return) is recorded in the workspace and read back by
+ * bfk_search_stats as device_error.  No entry point allocates device memory, calls
  * exit(), or throws.  Results:
  *   out_dists (n, k) float32  squared L2 distances, ascending;
  *   out_ids   (n, k) int32    id_offset + database row, ties by lower index;
@@ -165,7 +166,8 @@ BFK_API bfk_status_t bfk_prepare(const float *X, int64_t m, int32_t d, void *pre
                                  uint64_t bytes, void *stream);
 /* bfk_search with the rows' TC form from `prepared`; `opts` must carry BFK_FLAG_PREPARED
  * (bfk_workspace_size with that flag sizes the smaller workspace).  A buffer made for other
- * (m, d) is rejected with BFK_ERR_INVALID_ARGUMENT.  Shapes that the SIMT engine takes
+ * (m, d) is rejected with BFK_ERR_INVALID_ARGUMENT: every such search reads the buffer's
+ * description back (a synchronous copy of 256 bytes) before it launches anything.  Shapes that the SIMT engine takes
  * ignore the buffer. */
 BFK_API bfk_status_t bfk_search_prepared(const float *Q, int64_t n, const float *X,
                                          const void *prepared, int64_t m, int32_t d, int32_t k,
