@@ -19,9 +19,11 @@ struct WsHeader {
                           // outside its range): every query goes to the exact SIMT engine
   int32_t fallback;       // queries routed to the exact SIMT engine
   int32_t max_cand;       // max candidates of one query
+  uint32_t ex_bits;       // max over rows of ||x - f16 form of x|| (float bits, rounded up)
+  int32_t pad0;
   unsigned long long candidates;  // total candidates appended by the filter
   unsigned long long survivors;   // total rows re-ranked exactly
-  int32_t pad[54];
+  int32_t pad[52];
 };
 static_assert(sizeof(WsHeader) == 256, "header is 256 bytes");
 

@@ -82,8 +82,8 @@ struct TcPlan {
 // of every 64-row group (x_tiles * 4): the minimum ||x||^2 of each of its 16-row chunks,
 // then its scale and the scale's inverse.
 struct PreparedInfo {
-  char magic[8];     // "BFKPREP2"
-  int32_t version;   // 2
+  char magic[8];     // "BFKPREP3"
+  int32_t version;   // 3
   int32_t d;
   int64_t m;
   int32_t d_pad;

@@ -581,6 +581,40 @@ __device__ __forceinline__ float pow2_scale_for(float maxabs) {
   return ldexpf(1.f, p);
 }
 
+// Squared rounding error of four values against their f16 forms h (scaled by 1/inv),
+// accumulated into acc.  v - h * inv is exact (h * inv is a power-of-two scaling of a
+// value within 2^-11 of v, so the difference is exact by Sterbenz' lemma, up to
+// underflow below the margin's own FP32 terms).
+__device__ __forceinline__ float round_err4(float4 v, __half2 lo, __half2 hi, float inv,
+                                            float acc) {
+  const float2 a = __half22float2(lo), b = __half22float2(hi);
+  float e = v.x - a.x * inv;
+  acc = __fmaf_rn(e, e, acc);
+  e = v.y - a.y * inv;
+  acc = __fmaf_rn(e, e, acc);
+  e = v.z - b.x * inv;
+  acc = __fmaf_rn(e, e, acc);
+  e = v.w - b.y * inv;
+  return __fmaf_rn(e, e, acc);
+}
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+// A warp's largest row rounding error (sum of squares) into hdr->ex_bits as a norm,
+// rounded up (non-negative floats, +inf included, order like their bit patterns).
+__device__ __forceinline__ float norm_up(float sum_sq, int d);
+__device__ __forceinline__ void note_row_error(float emax2, int d, WsHeader *hdr) {
+  if ((threadIdx.x & 31) == 0 && emax2 > 0.f)  // NaN rows are exact-only already
+    atomicMax(&hdr->ex_bits, __float_as_uint(norm_up(emax2, d)));
+}
+// sqrt of an FP32 sum of d squares, rounded so that it bounds the exact norm: each of the
+// d + 2 roundings (sum, square root) is at most 2^-24 relative
+__device__ __forceinline__ float norm_up(float sum_sq, int d) {
+  return __fmul_ru(__fsqrt_ru(sum_sq), 1.f + (float)(d + 3) * 5.9604645e-8f);
+}
+
 // Database rows -> f16.  Each group of 64 rows (one epilogue warp's columns of a
 // tile) shares a power-of-two scale.  grid (ceil(m / 64)), block 256: eight warps
 // of eight rows each.  VEC (d % 4 == 0, d <= 256): each row is read once, as
@@ -661,11 +695,15 @@ __global__ void __launch_bounds__(256) tc_prep_x_kernel(const float *__restrict_
     // the bound only grows, and non-negative floats order like their bit patterns
     if (isfinite(rn)) atomicMax(&hdr->rx_bits, __float_as_uint(rn * (1.f + 0.0009765625f)));
   }
+  // the conversion, and each row's rounding error ||x - f16 form|| (its largest into hdr)
+  const float inv = 1.f / sc;
+  float emax = 0.f;
 #pragma unroll
   for (int u = 0; u < 8; u++) {
     const int64_t row = row_base + u;
     if (row >= m) break;
     __half *xh = Xh + row * d_pad;
+    float e2 = 0.f;
     if (VEC) {
       // four halves (8 bytes) per lane and step; columns past d are zero
 #pragma unroll
@@ -675,6 +713,7 @@ __global__ void __launch_bounds__(256) tc_prep_x_kernel(const float *__restrict_
           const float4 v = xr[u][h];
           __half2 lo = __floats2half2_rn(v.x * sc, v.y * sc);
           __half2 hi = __floats2half2_rn(v.z * sc, v.w * sc);
+          e2 = round_err4(v, lo, hi, inv, e2);
           uint2 pk;
           pk.x = *reinterpret_cast<uint32_t *>(&lo);
           pk.y = *reinterpret_cast<uint32_t *>(&hi);
@@ -683,15 +722,24 @@ __global__ void __launch_bounds__(256) tc_prep_x_kernel(const float *__restrict_
       }
     } else {
       const float *x = X + row * d;
-      for (int c = lane; c < d_pad; c += 32) xh[c] = __float2half_rn(c < d ? x[c] * sc : 0.f);
+      for (int c = lane; c < d_pad; c += 32) {
+        const float v = c < d ? x[c] : 0.f;
+        const __half hv = __float2half_rn(v * sc);
+        const float e = v - __half2float(hv) * inv;
+        e2 = __fmaf_rn(e, e, e2);
+        xh[c] = hv;
+      }
     }
+    emax = fmaxf(emax, warp_sum(e2));
   }
+  note_row_error(emax, d, hdr);
 }
 
 // A prepared database's row status (norm bound, non-finite rows) into this search's header.
 __global__ void tc_take_row_status(const WsHeader *src, WsHeader *dst) {
   if (threadIdx.x == 0) {
     dst->rx_bits = src->rx_bits;
+    dst->ex_bits = src->ex_bits;
     dst->exact_only = src->exact_only;
   }
 }
@@ -767,11 +815,14 @@ __global__ void __launch_bounds__(256) tc_prep_x_wide_kernel(const float *__rest
     // the bound only grows, and non-negative floats order like their bit patterns
     if (isfinite(rn)) atomicMax(&hdr->rx_bits, __float_as_uint(rn * (1.f + 0.0009765625f)));
   }
+  const float inv = 1.f / sc;
+  float emax = 0.f;
   for (int u = 0; u < 8; u++) {
     const int64_t row = row_base + u;
     if (row >= m) break;
     const float4 *x4 = reinterpret_cast<const float4 *>(X + row * d);
     uint2 *xh2 = reinterpret_cast<uint2 *>(Xh + row * d_pad);
+    float e2 = 0.f;
     for (int c0 = lane; c0 < dp4; c0 += 4 * 32) {
       float4 v[4];
 #pragma unroll
@@ -786,6 +837,7 @@ __global__ void __launch_bounds__(256) tc_prep_x_wide_kernel(const float *__rest
           // four halves (8 bytes) per lane and step; columns past d are zero
           __half2 lo = __floats2half2_rn(v[h].x * sc, v[h].y * sc);
           __half2 hi = __floats2half2_rn(v[h].z * sc, v[h].w * sc);
+          e2 = round_err4(v[h], lo, hi, inv, e2);
           uint2 pk;
           pk.x = *reinterpret_cast<uint32_t *>(&lo);
           pk.y = *reinterpret_cast<uint32_t *>(&hi);
@@ -793,7 +845,9 @@ __global__ void __launch_bounds__(256) tc_prep_x_wide_kernel(const float *__rest
         }
       }
     }
+    emax = fmaxf(emax, warp_sum(e2));
   }
+  note_row_error(emax, d, hdr);
 }
 
 // max |Q| -> hdr->qmax_bits
@@ -831,32 +885,36 @@ __global__ void __launch_bounds__(256) tc_prep_q_kernel(const float *__restrict_
     return;
   }
   const float *qp = Q + row * d;
-  float ss = 0.f;
+  const float inv_sq = 1.f / sq;
+  float ss = 0.f, e2 = 0.f;  // ||q||^2 and ||q - f16 form of q||^2
   for (int c = lane; c < d_pad; c += 32) {
     const float v = c < d ? qp[c] : 0.f;
     ss = __fmaf_rn(v, v, ss);
-    qh[c] = __float2half_rn(v * sq);
+    const __half h = __float2half_rn(v * sq);
+    const float e = v - __half2float(h) * inv_sq;
+    e2 = __fmaf_rn(e, e, e2);
+    qh[c] = h;
   }
-#pragma unroll
-  for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+  ss = warp_sum(ss);
+  e2 = warp_sum(e2);
   if (lane == 0) {
     if (!isfinite(ss)) atomicOr(&hdr->exact_only, 1);
-    // Error margin.  With u = 2^-11 the f16 unit roundoff, qn >= ||q||, Rx >= max ||x||:
-    //   e_q = u qn + sqrt(d) 2^-25 / s_q        (f16 rounding of q, incl. subnormals)
-    //   e_x = (u + sqrt(d) 2^-38) Rx             (row groups scaled to [2^13, 2^14))
-    //   dot rounding  <= e_q Rx + qn e_x + e_q e_x
+    // Error margin.  With qn >= ||q||, Rx >= max ||x|| and the measured f16 rounding
+    // errors (q~ the f16 form of q scaled back, x~ likewise, both exact in FP32):
+    //   e_q >= ||q - q~||,  e_x >= max over rows ||x - x~||   (at most 2^-11 ||q||,
+    //                       2^-11 ||x|| above the f16 subnormal range; measured instead)
+    //   dot rounding  <= e_q Rx + qn e_x + e_q e_x      (|q~.x~ - q.x|, Cauchy-Schwarz)
     //   accumulation  <= (d_pad + 16) 2^-22 (qn + e_q)(Rx + e_x)   (tensor-core FP32 sums)
     //   FP32 terms    <= 2 (d + 8) 2^-24 (qn + Rx)^2  (norms, the fused epilogue step,
     //                                                  and the reference's own rounding)
     //   margin = 2 (dot rounding + accumulation) + FP32 terms.
     // Then |(||q||^2 + v) - D| <= margin for every row, v the epilogue value and D
     // the reference kernel's FP32 distance.
-    const double u = 1.0 / 2048.0;
     const double qn = sqrt((double)ss) * (1.0 + ldexp(1.0, -10));
     const double rx = (double)__uint_as_float(hdr->rx_bits);
-    const double sd = sqrt((double)d);
-    const double eq = u * qn + sd * ldexp(1.0, -25) / (double)sq;
-    const double ex = (u + sd * ldexp(1.0, -38)) * rx;
+    // the FP32 sum of d squares is within (d + 2) 2^-24 of the exact one, its root half that
+    const double eq = sqrt((double)e2) * (1.0 + (double)(d + 3) * ldexp(1.0, -24));
+    const double ex = (double)__uint_as_float(hdr->ex_bits);
     const double dotr = eq * rx + qn * ex + eq * ex;
     const double acc = (double)(d_pad + 16) * ldexp(1.0, -22) * (qn + eq) * (rx + ex);
     const double f32 = 2.0 * (double)(d + 8) * ldexp(1.0, -24) * (qn + rx) * (qn + rx);
@@ -1809,8 +1867,8 @@ PreparedLayout tc_prepared_layout(int64_t m, int d) {
 
 static PreparedInfo prepared_info(int64_t m, int d) {
   PreparedInfo I{};
-  memcpy(I.magic, "BFKPREP2", 8);
-  I.version = 2;
+  memcpy(I.magic, "BFKPREP3", 8);
+  I.version = 3;
   I.d = d;
   I.m = m;
   I.d_pad = kch_for(d) * kBK;

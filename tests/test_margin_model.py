@@ -7,7 +7,8 @@ batch, rows by one per 64-row group, each max |value| into [2^13, 2^14)) and
 c = -2 / (s_q s_x).  tc_prep_q_kernel bounds |(||q||^2 + v) - D_j| by a per-query
 margin, D_j being the reference kernel's FP32 distance.  This restates that arithmetic
 in NumPy (the tensor core modelled as an exact sum rounded once to FP32; the margin's
-accumulation term covers the rest) and checks:
+accumulation term covers the rest; the f16 rounding errors of q and of the rows measured
+as the prep kernels measure them) and checks:
 * the bound holds, with room, from data scales of 1e6 down to norms near 2^-48;
 * below that it fails (c underflows to zero, FP32 rounding goes subnormal), and from
   ||q|| + max ||x|| = 2^63 on v can overflow to +inf, so that the filter never keeps a
@@ -56,17 +57,20 @@ def filter_model(Q: np.ndarray, X: np.ndarray) -> dict:
         sc = _pow2_scale_for(np.abs(X[g:g + GROUP_ROWS]).max())
         xh[g:g + GROUP_ROWS] = (X[g:g + GROUP_ROWS] * sc).astype(np.float16)
         xinv[g:g + GROUP_ROWS] = np.float32(1.0) / sc
+    # the f16 rounding errors, measured as the prep kernels measure them (v - h / s is
+    # exact in FP32), each norm rounded up by (d + 3) 2^-24
+    up = 1.0 + (d + 3) * 2.0 ** -24
+    dq = Q - qh.astype(np.float32) * (np.float32(1.0) / sq)
+    dx = X - xh.astype(np.float32) * xinv[:, None]
+    eq = np.sqrt(np.einsum("ij,ij->i", dq, dq, dtype=np.float32).astype(np.float64)) * up
+    ex = float(np.sqrt(np.einsum("ij,ij->i", dx, dx, dtype=np.float32).max())) * up
     acc = (qh.astype(np.float64) @ xh.astype(np.float64).T).astype(np.float32)
     c = (np.float32(-2.0) * (np.float32(1.0) / sq)) * xinv  # FP32, may underflow to 0
     with np.errstate(over="ignore"):  # v may overflow to +inf, as in FP32 on the GPU
         v = (c.astype(np.float64)[None, :] * acc.astype(np.float64)
              + ssx.astype(np.float64)[None, :]).astype(np.float32)
     # the margin, as tc_prep_q_kernel forms it
-    u = 2.0 ** -11
     qn = np.sqrt(ssq.astype(np.float64)) * (1.0 + 2.0 ** -10)
-    sd = math.sqrt(d)
-    eq = u * qn + sd * 2.0 ** -25 / float(sq)
-    ex = (u + sd * 2.0 ** -38) * rx
     dotr = eq * rx + qn * ex + eq * ex
     accr = (d_pad + 16) * 2.0 ** -22 * (qn + eq) * (rx + ex)
     f32t = 2.0 * (d + 8) * 2.0 ** -24 * (qn + rx) ** 2
@@ -95,7 +99,17 @@ def test_margin_bounds_the_filter_error(q_scale, x_scale, d):
     f = filter_model(Q, X)
     assert ((f["norms"] >= LOW) & (f["norms"] < HIGH)).all()
     assert np.isfinite(f["v"]).all() and np.isfinite(f["D"]).all()
-    assert f["ratio"].max() <= 0.5, f["ratio"].max()
+    assert f["ratio"].max() <= 0.8, f["ratio"].max()
+
+
+def test_measured_rounding_beats_the_worst_case():
+    """The measured f16 rounding errors are well inside the worst case 2^-11 ||.||,
+    which is what makes the margin about half the worst-case one on Gaussian data."""
+    Q, X = _data(7, 24, 640, 128, 1.0, 1.0)
+    qh = (Q * _pow2_scale_for(np.abs(Q).max())).astype(np.float16)
+    dq = Q - qh.astype(np.float32) / _pow2_scale_for(np.abs(Q).max())
+    ratio = np.linalg.norm(dq, axis=1) / (2.0 ** -11 * np.linalg.norm(Q, axis=1))
+    assert ratio.max() < 0.7
 
 
 def test_rows_of_mixed_scale_in_one_group():
@@ -105,7 +119,7 @@ def test_rows_of_mixed_scale_in_one_group():
     X[::64] *= 1e4
     X[1::64] *= 1e-8
     f = filter_model(Q, X)
-    assert f["ratio"].max() <= 0.5, f["ratio"].max()
+    assert f["ratio"].max() <= 0.8, f["ratio"].max()
 
 
 @pytest.mark.parametrize("scale", [1e-20, 1e-22])
