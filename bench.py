@@ -27,6 +27,7 @@ import os
 import statistics
 import subprocess
 import sys
+import threading
 import time
 
 import numpy as np
@@ -100,29 +101,45 @@ class ClockSampler:
         self.dev = device_index
         self.proc = None
         self.err = None
+        self.lines = []
+        self.reader = None
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line)
 
     def start(self):
+        """Starts sampling every 100 ms and returns once the first sample is in (up to
+        2 s), so that a timed region shorter than the interval still has the sample
+        taken as it begins, under the warm-up's load."""
         try:
             self.proc = subprocess.Popen(
                 ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
-                 "-lms", "200", "-i", str(self.dev)],
+                 "-lms", "100", "-i", str(self.dev)],
                 stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
         except Exception as e:  # nvidia-smi missing
             self.err = str(e)
+            return
+        self.reader = threading.Thread(target=self._read, daemon=True)
+        self.reader.start()
+        t_end = time.monotonic() + 2.0
+        while not self.lines and time.monotonic() < t_end and self.proc.poll() is None:
+            time.sleep(0.005)
 
     def stop(self) -> dict:
         if self.proc is None:
             return {"unavailable": self.err or "nvidia-smi not started"}
-        time.sleep(0.25)
+        time.sleep(0.15)
         self.proc.terminate()
         try:
-            out, _ = self.proc.communicate(timeout=5)
+            self.proc.wait(timeout=5)
         except subprocess.TimeoutExpired:
             self.proc.kill()
-            out, _ = self.proc.communicate()
+            self.proc.wait()
+        self.reader.join(timeout=5)
         sm, smax, reasons = [], [], set()
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        for line in out.strip().splitlines():
+        for line in self.lines:
             parts = [p.strip() for p in line.split(",")]
             if len(parts) < 9:
                 continue
@@ -378,22 +395,42 @@ def main(argv=None) -> int:
     per_row = TRAFFIC_READ_PER_ROW.get((a.workload, Qn, d, k))
     if per_row is not None and stats["engine"] == "tc_f16":
         traffic = per_row * m_shard + TRAFFIC_WRITE_PER_CANDIDATE * stats["candidates"]
-    flops = 2.0 * Qn * m_shard * d  # algorithmic, per launch of the main kernel on one GPU
-    achieved = flops / (main_max / 1e3) / 1e12 if main_max > 0 else None
+    # The dominant kernel's algorithmic work per launch on one GPU: 2*Q*N_shard*d flops,
+    # and the rows it must read (f16 for the tensor-core filter, FP32 for the SIMT
+    # engines).  Its bound is whichever takes longer at the measured peaks; the SIMT
+    # engines stream the database and are taken as HBM-bound.
+    flops = 2.0 * Qn * m_shard * d
+    tc = stats["engine"] == "tc_f16"
+    kbytes = float(m_shard * d * (2 if tc else 4))
+    t_tensor = flops / (peaks["bf16_tflops"] * 1e12)
+    t_hbm = kbytes / (peaks["hbm_gbs"] * 1e9)
+    bound = "tensor" if tc and t_tensor >= t_hbm else "hbm"
+    main_s = main_max / 1e3 if main_max > 0 else None
+    if bound == "tensor":
+        achieved = flops / main_s / 1e12 if main_s else None
+        peak, unit, peak_kind = peaks["bf16_tflops"], "TFLOP/s", "dense bf16 (burst)"
+        algorithmic = "2*Q*N_shard*d flops per launch"
+    else:
+        achieved = kbytes / main_s / 1e9 if main_s else None
+        peak, unit, peak_kind = peaks["hbm_gbs"], "GB/s", "HBM copy"
+        algorithmic = (f"N_shard*d*{2 if tc else 4} bytes per launch "
+                       f"({'f16' if tc else 'FP32'} rows read once)")
     roofline = {
-        "bound": "tensor",
+        "bound": bound,
         "kernel": stats["engine"],
         "achieved": achieved,
-        "peak": peaks["bf16_tflops"],
-        "unit": "TFLOP/s",
-        "frac": (achieved / peaks["bf16_tflops"]) if achieved else None,
+        "peak": peak,
+        "unit": unit,
+        "frac": (achieved / peak) if achieved else None,
         "traffic": traffic,
         "traffic_source": (f"ncu dram__bytes of a 3M-row sample: {per_row} B read per row x "
                            f"{m_shard} rows + {TRAFFIC_WRITE_PER_CANDIDATE} B written per "
                            f"candidate x {stats['candidates']}") if traffic else None,
-        "peak_source": f"{peaks['source']} dense bf16 (burst)",
+        "peak_source": f"{peaks['source']} {peak_kind}",
         "main_kernel_ms": main_max,
-        "algorithmic": "2*Q*N_shard*d flops per launch",
+        "algorithmic": algorithmic,
+        "flops_per_launch": flops,
+        "bytes_per_launch": kbytes,
         "db_bytes_per_launch": m_shard * d * 4,
     }
     launches = stats["kernel_launches"] + (1 if world > 1 else 0)

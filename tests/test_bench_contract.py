@@ -61,3 +61,20 @@ def test_clock_sampler_reads_clocks_and_active_reasons(tmp_path, monkeypatch):
     time.sleep(0.5)
     assert s.stop() == {"sm_mhz": 1850.0, "sm_max_mhz": 1965.0, "reasons": ["sw_power_cap"],
                         "samples": 3}
+
+
+def test_clock_sampler_has_a_sample_for_a_short_timed_region(tmp_path, monkeypatch):
+    """start() returns only once the first sample is in, so a timed region shorter than
+    the sampling interval still has one."""
+    fake = tmp_path / "nvidia-smi"
+    fake.write_text(
+        "#!/bin/sh\n"
+        "sleep 0.3\n"
+        "echo '0, 1965, 1965, 650.0, 0x0, Not Active, Not Active, Not Active, Not Active'\n"
+        "exec sleep 30\n")
+    fake.chmod(0o755)
+    monkeypatch.setenv("PATH", f"{tmp_path}{os.pathsep}{os.environ['PATH']}")
+    import bench
+    s = bench.ClockSampler(0)
+    s.start()
+    assert s.stop() == {"sm_mhz": 1965.0, "sm_max_mhz": 1965.0, "reasons": [], "samples": 1}
