@@ -46,10 +46,10 @@ DEFAULT_WORKLOAD = "unit-10m"
 PUBLISHED_QPS = {("published-d8", 1_000_000, 128_000, 8, 1): 607_025.0}
 # DRAM bytes read per database row by one main-filter launch, keyed by (workload, queries,
 # d, k): ncu dram__bytes_read.sum of the launch over all rows of a 3,000,000-row sample
-# (1.242 GB / 3M rows), single-CTA kernel.  Its writes are the candidate appends, 8 bytes
-# each (0.386 GB for the sample's 41.3M candidates, 9.3 B each with write granularity).
-TRAFFIC_READ_PER_ROW = {("unit-10m", 10_000, 128, 100): 414}
-TRAFFIC_WRITE_PER_CANDIDATE = 9.3  # 0.385 GB for 41.3M candidates in the latest capture
+# (1.213 GB / 3M rows), CTA pairs.  Its writes are the candidate appends, 8 bytes each
+# (0.323 GB for the sample's 35.8M candidates, 9.0 B each with write granularity).
+TRAFFIC_READ_PER_ROW = {("unit-10m", 10_000, 128, 100): 404}
+TRAFFIC_WRITE_PER_CANDIDATE = 9.0
 
 
 def parse_args(argv=None):

@@ -76,8 +76,9 @@ struct TcPlan {
 };
 
 // A prepared database (bfk_prepare): the TC engine's row arrays for one X, made once.
-// Layout, every part 256-byte aligned: a 256-byte status block (the rows' norm bound and
-// exact-only flag, set for a non-finite row, as the workspace header holds them), a 256-byte description
+// Layout, every part 256-byte aligned: a 256-byte status block (the rows' norm bound, their
+// largest f16 rounding error and the exact-only flag, set for a non-finite row, as the
+// workspace header holds them), a 256-byte description
 // (PreparedInfo), the f16 rows (m, d_pad), ||x||^2 (x_tiles * 256) and a 32-byte record
 // of every 64-row group (x_tiles * 4): the minimum ||x||^2 of each of its 16-row chunks,
 // then its scale and the scale's inverse.
