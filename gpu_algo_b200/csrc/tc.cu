@@ -522,30 +522,26 @@ __global__ void __maxnreg__(96)
             }
           }
         } else {
-          // one bound for the chunk: its largest accumulator against T
-          // The detail below is rare (a chunk with a candidate in some lane): a
-          // warp-uniform branch marked unlikely keeps the compiler from predicating it
-          // into every chunk.
+          // one bound for the chunk: its largest accumulator against T; a lane whose
+          // chunk passes computes every exact v of it (packed FMAs) and appends the kept
+          // ones.  A plain per-lane branch measured fastest: a warp vote with the detail
+          // marked unlikely, or exact values only for the columns whose own accumulator
+          // passes, made 1M x d=8 queries twice as slow and 1M x d=128 ones 14 % slower
+          // (norms that vary within a chunk loosen T, so chunks pass often there), and
+          // did not help the 10M-row unit-vector pass.
           const bool pass = max16u(cur) > T[qq];
-          if (__builtin_expect(__any_sync(0xffffffffu, pass), 0) && pass) {
-            // a column can hold v <= theta only if its own accumulator exceeds T (the
-            // chunk test, column by column); those few get their exact v, the same
-            // single-rounding fma as exact_v8
-            float acc16[16];
-            unsigned maybe = 0;
+          if (pass) {
+            float v[16];
+            exact_v8(cur, cscale, nx4[0], nx4[1], v);
+            exact_v8(cur + 8, cscale, nx4[2], nx4[3], v + 8);
+            unsigned keep = 0;
 #pragma unroll
-            for (int i = 0; i < 16; i++) {
-              acc16[i] = __uint_as_float(cur[i]);
-              maybe |= (acc16[i] > T[qq] ? 1u : 0u) << i;
-            }
-            while (maybe) {
-              const int i = __ffs(maybe) - 1;
-              maybe &= maybe - 1;
-              const float v = __fmaf_rn(pick16(acc16, i), cscale, nxt[qq * 16 + i]);
-              if (v <= theta) {
-                region[min(cnt, last)] = make_uint2(rg + i, __float_as_uint(v));
-                cnt++;
-              }
+            for (int i = 0; i < 16; i++) keep |= (v[i] <= theta ? 1u : 0u) << i;
+            while (keep) {
+              const int i = __ffs(keep) - 1;
+              keep &= keep - 1;
+              region[min(cnt, last)] = make_uint2(rg + i, __float_as_uint(pick16(v, i)));
+              cnt++;
             }
           }
         }

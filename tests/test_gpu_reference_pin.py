@@ -70,3 +70,60 @@ def test_reference_kernel_d96(plumbing):
     rd, ri = run_ref("bf_fp32_k10_d96", Q, X, 10)
     od, oi = oracle_knn(Q, X, 10)
     compare(rd, ri, od, oi)
+
+
+def _time_ms(fn, reps=3):
+    """Mean CUDA-event time of fn() on the current stream, after one untimed call."""
+    fn()
+    torch.cuda.synchronize()
+    ts = []
+    for _ in range(reps):
+        a = torch.cuda.Event(enable_timing=True)
+        b = torch.cuda.Event(enable_timing=True)
+        a.record()
+        fn()
+        b.record()
+        torch.cuda.synchronize()
+        ts.append(a.elapsed_time(b))
+    return sum(ts) / len(ts)
+
+
+@pytest.mark.parametrize("inst,workload,rows,nq", [
+    ("bf_fp32_k10_d128", "plumbing", 65_536, 1_024),
+    ("bf_fp32_k100_d128", "plumbing", 65_536, 1_024),
+    ("bf_fp32_k10_d128", "mixture-k-sweep", 1_000_000, 2_368),
+])
+def test_reference_kernel_timed_beside_the_engine(inst, workload, rows, nq):
+    """The reference's own kernel and this engine on the same device-resident inputs, timed
+    alike (CUDA events, one warm-up call, mean of three).  Prints both rates; asserts that
+    the two return the same distances, bit for bit."""
+    man = manifest()
+    if inst not in man:
+        pytest.skip(f"{inst} not built")
+    from gpu_algo_b200 import data, engine
+    k = man[inst]["k"]
+    X, Q = data.workload_arrays(workload, n_rows=rows, n_queries=nq)
+    lib = ctypes.CDLL(os.path.join(REF, f"ref_{inst}.so"))
+    lib.ref_launch.restype = ctypes.c_int
+    lib.ref_launch.argtypes = [ctypes.c_void_p] * 4 + [ctypes.c_int, ctypes.c_int, ctypes.c_void_p]
+    Qd = torch.from_numpy(Q).cuda()
+    Xd = torch.from_numpy(X).cuda()
+    ids = torch.zeros((nq, k), dtype=torch.int32, device="cuda")
+    dists = torch.zeros((nq, k), dtype=torch.float32, device="cuda")
+
+    def ref():
+        rc = lib.ref_launch(Qd.data_ptr(), Xd.data_ptr(), ids.data_ptr(), dists.data_ptr(), nq,
+                            rows, ctypes.c_void_p(torch.cuda.current_stream().cuda_stream))
+        assert rc == 0
+
+    out = {}
+
+    def ours():
+        out["r"] = engine.search(Qd, Xd, k)
+
+    t_ref = _time_ms(ref)
+    t_ours = _time_ms(ours)
+    print(f"\nreference kernel {inst} on {workload} ({rows} rows, {nq} queries, k={k}): "
+          f"{t_ref:.3f} ms, {nq / t_ref * 1e3:,.0f} queries/s; this engine: {t_ours:.3f} ms, "
+          f"{nq / t_ours * 1e3:,.0f} queries/s ({t_ref / t_ours:.1f}x)")
+    np.testing.assert_array_equal(dists.cpu().numpy(), out["r"][0].cpu().numpy())
