@@ -296,10 +296,13 @@ def main(argv=None) -> int:
     stat_opts = dict(engine=a.engine, plan_rows=plan_rows if world > 1 else 0,
                      shards=world if world > 1 else 0, prepared=a.prepared, cta_pair=cta_pair)
     engine.last_stats(Qd, Xd, k, **stat_opts)  # clear timing records
-    barrier()
-    torch.cuda.synchronize()
+    # the sampler starts first: its start waits for the first sample, for a time that
+    # differs between ranks, and the barrier after it lines the ranks up again so that
+    # no rank's timed steps wait on a rank still starting its sampler
     sampler = ClockSampler(local)
     sampler.start()
+    barrier()
+    torch.cuda.synchronize()
     if flush is None:
         ev0 = torch.cuda.Event(enable_timing=True)
         ev1 = torch.cuda.Event(enable_timing=True)
