@@ -47,3 +47,15 @@ def test_full_size_sampled_distances_and_lists_are_exact(unit10m):
     ed, ei = oracle_knn(Q[sel], X, 100)
     np.testing.assert_array_equal(ii[sel], ei)
     np.testing.assert_array_equal(dd[sel], ed)
+
+
+def test_full_size_every_query_equals_the_simt_engine(unit10m):
+    """All 10,000 lists against the exact SIMT engine, an independent full scan with the
+    reference arithmetic (pinned to the oracle by the parity tests): distances and ids
+    equal, every query."""
+    X, Q, dd, ii = unit10m
+    Xd, Qd = torch.from_numpy(X).cuda(), torch.from_numpy(Q).cuda()
+    sd, si = engine.search(Qd, Xd, 100, engine="direct")
+    torch.cuda.synchronize()
+    np.testing.assert_array_equal(sd.cpu().numpy(), dd)
+    np.testing.assert_array_equal(si.cpu().numpy(), ii)
