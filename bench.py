@@ -157,6 +157,36 @@ class ClockSampler:
                 "reasons": sorted(reasons), "samples": len(sm)}
 
 
+def roofline_of(engine_name: str, queries: int, rows: int, d: int, main_ms: float,
+                peaks: dict) -> dict:
+    """The dominant kernel's roofline for one launch on one GPU.
+
+    Its algorithmic work is 2*Q*N_shard*d flops and the rows it must read: f16 for the
+    tensor-core filter, FP32 for the SIMT engines.  Its bound is whichever of the two takes
+    longer at the measured peaks; the SIMT engines stream the database and are taken as
+    HBM-bound.  `achieved` is that work over the launch's CUDA-event time."""
+    flops = 2.0 * queries * rows * d
+    tc = engine_name == "tc_f16"
+    kbytes = float(rows * d * (2 if tc else 4))
+    t_tensor = flops / (peaks["bf16_tflops"] * 1e12)
+    t_hbm = kbytes / (peaks["hbm_gbs"] * 1e9)
+    bound = "tensor" if tc and t_tensor >= t_hbm else "hbm"
+    main_s = main_ms / 1e3 if main_ms > 0 else None
+    if bound == "tensor":
+        achieved = flops / main_s / 1e12 if main_s else None
+        peak, unit, peak_kind = peaks["bf16_tflops"], "TFLOP/s", "dense bf16 (burst)"
+        algorithmic = "2*Q*N_shard*d flops per launch"
+    else:
+        achieved = kbytes / main_s / 1e9 if main_s else None
+        peak, unit, peak_kind = peaks["hbm_gbs"], "GB/s", "HBM copy"
+        algorithmic = (f"N_shard*d*{2 if tc else 4} bytes per launch "
+                       f"({'f16' if tc else 'FP32'} rows read once)")
+    return {"bound": bound, "kernel": engine_name, "achieved": achieved, "peak": peak,
+            "unit": unit, "frac": (achieved / peak) if achieved else None,
+            "peak_source": f"{peaks['source']} {peak_kind}", "main_kernel_ms": main_ms,
+            "algorithmic": algorithmic, "flops_per_launch": flops, "bytes_per_launch": kbytes}
+
+
 def gen_workload(name, rank, world, rows, queries):
     w = data.WORKLOADS[name]
     N = rows or w["N"]
@@ -398,44 +428,14 @@ def main(argv=None) -> int:
     per_row = TRAFFIC_READ_PER_ROW.get((a.workload, Qn, d, k))
     if per_row is not None and stats["engine"] == "tc_f16":
         traffic = per_row * m_shard + TRAFFIC_WRITE_PER_CANDIDATE * stats["candidates"]
-    # The dominant kernel's algorithmic work per launch on one GPU: 2*Q*N_shard*d flops,
-    # and the rows it must read (f16 for the tensor-core filter, FP32 for the SIMT
-    # engines).  Its bound is whichever takes longer at the measured peaks; the SIMT
-    # engines stream the database and are taken as HBM-bound.
-    flops = 2.0 * Qn * m_shard * d
-    tc = stats["engine"] == "tc_f16"
-    kbytes = float(m_shard * d * (2 if tc else 4))
-    t_tensor = flops / (peaks["bf16_tflops"] * 1e12)
-    t_hbm = kbytes / (peaks["hbm_gbs"] * 1e9)
-    bound = "tensor" if tc and t_tensor >= t_hbm else "hbm"
-    main_s = main_max / 1e3 if main_max > 0 else None
-    if bound == "tensor":
-        achieved = flops / main_s / 1e12 if main_s else None
-        peak, unit, peak_kind = peaks["bf16_tflops"], "TFLOP/s", "dense bf16 (burst)"
-        algorithmic = "2*Q*N_shard*d flops per launch"
-    else:
-        achieved = kbytes / main_s / 1e9 if main_s else None
-        peak, unit, peak_kind = peaks["hbm_gbs"], "GB/s", "HBM copy"
-        algorithmic = (f"N_shard*d*{2 if tc else 4} bytes per launch "
-                       f"({'f16' if tc else 'FP32'} rows read once)")
-    roofline = {
-        "bound": bound,
-        "kernel": stats["engine"],
-        "achieved": achieved,
-        "peak": peak,
-        "unit": unit,
-        "frac": (achieved / peak) if achieved else None,
+    roofline = roofline_of(stats["engine"], Qn, m_shard, d, main_max, peaks)
+    roofline.update({
         "traffic": traffic,
         "traffic_source": (f"ncu dram__bytes of a 3M-row sample: {per_row} B read per row x "
                            f"{m_shard} rows + {TRAFFIC_WRITE_PER_CANDIDATE} B written per "
                            f"candidate x {stats['candidates']}") if traffic else None,
-        "peak_source": f"{peaks['source']} {peak_kind}",
-        "main_kernel_ms": main_max,
-        "algorithmic": algorithmic,
-        "flops_per_launch": flops,
-        "bytes_per_launch": kbytes,
         "db_bytes_per_launch": m_shard * d * 4,
-    }
+    })
     launches = stats["kernel_launches"] + (1 if world > 1 else 0)
 
     cpu = None

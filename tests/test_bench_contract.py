@@ -78,3 +78,19 @@ def test_clock_sampler_has_a_sample_for_a_short_timed_region(tmp_path, monkeypat
     s = bench.ClockSampler(0)
     s.start()
     assert s.stop() == {"sm_mhz": 1965.0, "sm_max_mhz": 1965.0, "reasons": [], "samples": 1}
+
+
+def test_roofline_bound_follows_the_workload():
+    """Tensor-bound for the 10M-row tensor-core filter at Q = 10k; HBM-bound for a 128-query
+    filter over 12.5M rows (f16 rows read once) and for the SIMT scan (FP32 rows)."""
+    import bench
+    peaks = {"bf16_tflops": 1649.3, "hbm_gbs": 6554.6, "source": "measured"}
+    r = bench.roofline_of("tc_f16", 10_000, 10_000_000, 128, 25.0, peaks)
+    assert r["bound"] == "tensor" and r["unit"] == "TFLOP/s"
+    assert abs(r["achieved"] - 2 * 10_000 * 10_000_000 * 128 / 25e-3 / 1e12) < 1e-6
+    r = bench.roofline_of("tc_f16", 128, 12_500_000, 96, 0.87, peaks)
+    assert r["bound"] == "hbm" and r["unit"] == "GB/s"
+    assert abs(r["achieved"] - 12_500_000 * 96 * 2 / 0.87e-3 / 1e9) < 1e-6
+    r = bench.roofline_of("direct", 1, 12_500_000, 96, 1.0, peaks)
+    assert r["bound"] == "hbm" and abs(r["frac"] - 4.8 / 6.5546) < 1e-3
+    assert bench.roofline_of("direct", 1, 10, 8, 0.0, peaks)["achieved"] is None
