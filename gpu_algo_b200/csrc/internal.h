@@ -103,8 +103,8 @@ int tc_prepare(const float *X, int64_t m, int d, void *prep, cudaStream_t stream
 int tc_check_prepared(const void *prep, int64_t m, int d);
 bool tc_supported(int d, int k);
 // pair_mode: 1 CTA pairs, -1 single CTAs, 0 tc_pair_default
-bool tc_pair_default(int d, int64_t n);
-// shards > 1: the number of shards that share level bounds (their first level is smaller)
+bool tc_pair_default(int d, int64_t n, int64_t rows);
+// shards > 1: the number of shards that share level bounds
 bool tc_make_plan(int64_t n, int64_t m, int d, int k, int slices, int cand_cap, int pair_mode,
                   int64_t plan_rows, int shards, bool prepared, TcPlan *p);
 // Returns 0 ok, 1 CUDA error; it does not wait for the stream (a device timeout is

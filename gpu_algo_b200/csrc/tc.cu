@@ -1709,10 +1709,13 @@ static void layout_workspace(TcPlan &P) {
   P.total = off;
 }
 
-bool tc_pair_default(int d, int64_t n) {
-  // CTA pairs halve the row bytes each SM streams and measured faster for short tiles
-  // (d <= 256, the query tile resident); they need two query tiles
-  return kch_for(d) <= kResidentKch && n > kBM;
+constexpr int64_t kPairMinRows = 4000000;
+
+bool tc_pair_default(int d, int64_t n, int64_t rows) {
+  // CTA pairs halve the row bytes each SM streams.  For short tiles (d <= 256, the query
+  // tile resident) they measured faster over 10M rows and 1-2 % slower over 1M-3M rows,
+  // so they are the default from kPairMinRows on; they need two query tiles
+  return kch_for(d) <= kResidentKch && n > kBM && rows >= kPairMinRows;
 }
 
 bool tc_make_plan(int64_t n, int64_t m, int d, int k, int slices, int pool, int pair_mode,
@@ -1727,7 +1730,9 @@ bool tc_make_plan(int64_t n, int64_t m, int d, int k, int slices, int pool, int 
   P.q_tiles = (int)((n + kBM - 1) / kBM);
   // CTA pairs (M = 256): forced (pair_mode > 0), off (< 0) or by tc_pair_default; they need
   // two query tiles, and the tile count is then even
-  const bool want = pair_mode > 0 || (pair_mode == 0 && tc_pair_default(d, n));
+  // (a sharded search decides on the largest shard's rows, so that all shards agree)
+  const bool want = pair_mode > 0 ||
+                    (pair_mode == 0 && tc_pair_default(d, n, plan_rows > 0 ? plan_rows : m));
   P.pair = want && P.q_tiles >= 2;
   if (P.pair) P.q_tiles += P.q_tiles & 1;
   P.x_tiles = (m + kBN - 1) / kBN;

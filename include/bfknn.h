@@ -57,7 +57,8 @@ typedef enum {
 #define BFK_FLAG_TIME_MAIN 1 /* time the main kernel of every call with CUDA events      */
 #define BFK_FLAG_CTA_PAIR 2  /* TC engine: CTA pairs (tcgen05.mma.cta_group::2, M = 256);
                                 without it or BFK_FLAG_SINGLE_CTA, pairs are used for
-                                d <= 256 and more than 128 queries                      */
+                                d <= 256, more than 128 queries and at least 4M rows
+                                (opts.plan_rows when given, else m)                      */
 #define BFK_FLAG_PREPARED 4  /* the search reads its rows' TC form from a prepared buffer
                                 (bfk_search_prepared); the workspace then holds no rows */
 #define BFK_FLAG_SINGLE_CTA 8 /* TC engine: one CTA per query tile (no CTA pairs)         */

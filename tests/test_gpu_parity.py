@@ -314,8 +314,8 @@ def test_bf_dropin_runners(plumbing):
 
 def test_tc_cta_pair_bit_exact(plumbing):
     X, Q, gd, gi = plumbing
-    # one CTA per query tile, and the engine's own choice (pairs for this shape)
-    for choice, want in ((False, False), (None, True)):
+    # one CTA per query tile, and the engine's own choice (single CTAs below 4M rows)
+    for choice, want in ((False, False), (None, False)):
         d_, i_ = engine.search(dev(Q), dev(X), 10, engine="tc_f16", cta_pair=choice)
         st = engine.last_stats(dev(Q), dev(X), 10, engine="tc_f16", cta_pair=choice)
         assert st["cta_pair"] is want
