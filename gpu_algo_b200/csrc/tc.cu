@@ -3,16 +3,21 @@
 //
 // Pass 0 (prep): queries and database rows are scaled by powers of two and
 //   rounded to f16 (rows in 64-row groups sharing one scale), with their FP32
-//   squared norms and a per-query error margin m, a bound on
-//   |approximate distance - reference distance| (derived in tc_prep_q_kernel).
-// Filter passes (one CTA per (128-query tile, slice of a tile set)): TMA
-//   streams f16 row tiles (256 rows x 64 dims, 128-byte swizzle) into a
-//   shared-memory ring; one thread issues tcgen05.mma (M=128 queries, N=256
-//   rows, K=16) into a double-buffered FP32 accumulator in tensor memory; four
-//   epilogue warps read it with tcgen05.ld, one query per thread, and compute
-//       v = ||x||^2 - 2 q.x     (approximate distance - ||q||^2).
-//   Rows with v <= theta_q are appended to the query's candidate region
-//   (plain stores into a per-(query, slice) region: no atomics).
+//   squared norms, the largest f16 rounding error of a row and each query's, and
+//   a per-query error margin m, a bound on |approximate distance - reference
+//   distance| (derived in tc_prep_q_kernel).
+// Filter passes (one CTA, or a CTA pair, per (query tile, slice of a tile set)):
+//   TMA streams f16 row tiles (256 rows x 64 dims, 128-byte swizzle) into a
+//   shared-memory ring; tcgen05.mma (M = 128 queries, or 256 over a CTA pair;
+//   N = 256 rows; K = 16) accumulates into a double-buffered FP32 accumulator in
+//   tensor memory, issued by two threads on alternate tiles when a tile is at
+//   most two K chunks; sixteen epilogue warps (four per TMEM lane quarter, one
+//   per 64-column group) read it with tcgen05.ld, one query per thread.  A
+//   16-column chunk whose largest accumulator is at most a threshold T (in the
+//   accumulator's units) holds no candidate; the others get their exact
+//       v = ||x||^2 - 2 q.x     (approximate distance - ||q||^2)
+//   and rows with v <= theta_q are appended to the query's candidate region
+//   (plain stores into a per-(query, slice, column group) region: no atomics).
 // Levels: the tile sets grow geometrically: level 0 is a handful of evenly
 //   spaced tiles with theta = +inf; after each level a select pass sets
 //   R_q = k-th smallest v among the level's candidates and the next level uses
@@ -28,7 +33,8 @@
 //   (degenerate data) is finished by the exact SIMT engine, and so is every
 //   query when the inputs hold a non-finite norm or norms too small for the
 //   margin or too large for FP32 (qn + Rx outside [2^-48, 2^63), see
-//   tc_prep_q_kernel).
+//   tc_prep_q_kernel).  The count of such queries stays on the device: the
+//   fallback kernels always run and read it, so the host never waits.
 #include <cuda.h>
 #include <cudaTypedefs.h>
 
