@@ -38,6 +38,11 @@ def test_prepared_search_is_exact(tmp_path, m, d, k):
     np.testing.assert_array_equal(i_.cpu().numpy(), ei)
     st = engine.last_stats(Qd, Xd, k, engine="tc_f16", prepared=True)
     assert st["engine"] == "tc_f16" and st["device_error"] == 0
+    # the rows' norm bound and largest rounding error travel in the buffer, so the margin
+    # and the filter's candidates are those of the search that converts the rows itself
+    engine.search(Qd, Xd, k, engine="tc_f16")
+    sr = engine.last_stats(Qd, Xd, k, engine="tc_f16")
+    assert (st["candidates"], st["survivors"]) == (sr["candidates"], sr["survivors"])
 
 
 def test_prepared_workspace_is_smaller_and_mismatch_is_rejected():
