@@ -42,6 +42,7 @@ EXPORTS = (
     "bfk_filter_values_workspace",
     "bfk_filter_values",
     "bfk_search_stats",
+    "bfk_plan_info",
     "bfk_search_noalloc",
     "bfk_prepared_size",
     "bfk_prepare",
@@ -75,6 +76,13 @@ class Stats(ctypes.Structure):
                 ("device_error", ctypes.c_int32), ("kernel_launches", ctypes.c_int32),
                 ("timed_calls", ctypes.c_int32), ("main_kernel_ms", ctypes.c_float),
                 ("cta_pair", ctypes.c_int32), ("reserved", ctypes.c_int32 * 1)]
+
+
+class PlanInfo(ctypes.Structure):
+    _fields_ = [("engine", ctypes.c_int32), ("cta_pair", ctypes.c_int32),
+                ("levels", ctypes.c_int32), ("q_tiles", ctypes.c_int32),
+                ("cand_cap", ctypes.c_int32), ("reserved0", ctypes.c_int32),
+                ("level_tiles", ctypes.c_int64 * 6), ("level_slices", ctypes.c_int32 * 6)]
 
 
 class BfkError(RuntimeError):
@@ -142,6 +150,9 @@ def load() -> ctypes.CDLL:
         lib.bfk_search_stats.restype = i32
         lib.bfk_search_stats.argtypes = [vp, i64, i64, i32, i32, ctypes.POINTER(Opts), vp,
                                          ctypes.POINTER(Stats)]
+        lib.bfk_plan_info.restype = i32
+        lib.bfk_plan_info.argtypes = [i64, i64, i32, i32, ctypes.POINTER(Opts),
+                                      ctypes.POINTER(PlanInfo)]
         _lib = lib
         return lib
 

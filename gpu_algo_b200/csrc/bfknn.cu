@@ -217,6 +217,29 @@ bfk_status_t bfk_workspace_size(int64_t n, int64_t m, int32_t d, int32_t k,
   return BFK_OK;
 }
 
+bfk_status_t bfk_plan_info(int64_t n, int64_t m, int32_t d, int32_t k, const bfk_opts_t *opts,
+                           bfk_plan_info_t *out) {
+  if (!out || !opts_ok(opts)) return BFK_ERR_INVALID_ARGUMENT;
+  bfk_status_t s = validate(n, m, d, k, 0);
+  if (s != BFK_OK) return s;
+  bfk_plan_info_t info{};
+  info.engine = choose_engine(n, m, d, k, opts);
+  if (info.engine == BFK_ENGINE_TC_F16) {
+    TcPlan p;
+    if (!tc_supported(d, k) || !make_plan(n, m, d, k, opts, &p)) return BFK_ERR_UNSUPPORTED;
+    info.cta_pair = p.pair ? 1 : 0;
+    info.levels = p.levels;
+    info.q_tiles = p.q_tiles;
+    info.cand_cap = p.cand_cap;
+    for (int l = 0; l < p.levels && l < 6; l++) {
+      info.level_tiles[l] = p.level[l].tiles;
+      info.level_slices[l] = p.level[l].slices;
+    }
+  }
+  *out = info;
+  return BFK_OK;
+}
+
 static bfk_status_t search_body(const float *Q, int64_t n, const float *X, const void *prepared,
                                 int64_t m, int32_t d, int32_t k, int64_t id_offset,
                                 float *out_dists, int32_t *out_ids, void *workspace,

@@ -235,6 +235,27 @@ def last_stats(Q, X, k: int, *, engine: str = "auto", slices: int = 0,
     }
 
 
+def plan_info(n: int, m: int, d: int, k: int, *, engine: str = "auto", slices: int = 0,
+              max_candidates: int = 0, plan_rows: int = 0, shards: int = 0,
+              prepared: bool = False, cta_pair: bool | None = None) -> dict:
+    """The plan a search of this shape would run (computed on the host, no GPU): the
+    engine, and for the tensor-core engine its levels (tiles and slices of each), its
+    CTA-pair choice and candidate pool."""
+    opts = _lib.make_opts(engine, slices, max_candidates, _pair_flags(cta_pair))
+    opts.plan_rows = int(plan_rows)
+    opts.shards = int(shards)
+    if prepared:
+        opts.flags |= _lib.FLAG_PREPARED
+    info = _lib.PlanInfo()
+    _lib.check(_lib.load().bfk_plan_info(int(n), int(m), int(d), int(k), ctypes.byref(opts),
+                                         ctypes.byref(info)), "bfk_plan_info")
+    lv = info.levels
+    return {"engine": _lib.ENGINE_NAMES.get(info.engine, info.engine),
+            "cta_pair": bool(info.cta_pair), "levels": lv, "q_tiles": info.q_tiles,
+            "cand_cap": info.cand_cap, "level_tiles": list(info.level_tiles[:lv]),
+            "level_slices": list(info.level_slices[:lv])}
+
+
 def merge(cand_d: torch.Tensor, cand_i: torch.Tensor, k: int):
     """Merge (lists, n, k) sorted candidate lists into the k best per query."""
     if cand_d.dim() != 3 or cand_d.shape != cand_i.shape:

@@ -119,6 +119,17 @@ typedef struct {
   int32_t reserved[1];
 } bfk_stats_t;
 
+typedef struct {
+  int32_t engine;              /* bfk_engine_t the search would run                      */
+  int32_t cta_pair;            /* TC engine: the plan uses CTA pairs                     */
+  int32_t levels;              /* TC engine: filter passes; the last one reads every tile */
+  int32_t q_tiles;             /* TC engine: 128-query tiles (even with CTA pairs)       */
+  int32_t cand_cap;            /* TC engine: candidate entries per query                 */
+  int32_t reserved0;
+  int64_t level_tiles[6];      /* TC engine: 256-row tiles level l reads                 */
+  int32_t level_slices[6];     /* TC engine: database slices of level l                  */
+} bfk_plan_info_t;
+
 /* Library version.  No reference counterpart. */
 BFK_API bfk_status_t bfk_version(int32_t *major, int32_t *minor);
 
@@ -210,6 +221,15 @@ BFK_API bfk_status_t bfk_kernel_attrs(int32_t engine, int32_t d, int32_t k, bfk_
  * runners report (bf/fp32_tiled.py:229-239, bf/fp32_qgroup.py:279-291).
  */
 BFK_API bfk_status_t bfk_merge_attrs(int32_t lists, int32_t k, bfk_attrs_t *out);
+
+/*
+ * The plan a search of this shape would run under these options, computed on the host
+ * (no GPU, no workspace): the engine, and for the tensor-core engine its filter levels,
+ * the tiles and slices of each, its CTA-pair choice and candidate pool.  The same checks
+ * as bfk_workspace_size.  No reference counterpart.
+ */
+BFK_API bfk_status_t bfk_plan_info(int64_t n, int64_t m, int32_t d, int32_t k,
+                                   const bfk_opts_t *opts, bfk_plan_info_t *out);
 
 /*
  * Statistics of the last bfk_search that used this workspace (synchronises

@@ -143,7 +143,8 @@ def test_struct_layouts_match_the_header(tmp_path):
     cc = shutil.which("gcc")
     if cc is None:
         pytest.skip("no C compiler")
-    mirrors = {"bfk_opts_t": _lib.Opts, "bfk_attrs_t": _lib.Attrs, "bfk_stats_t": _lib.Stats}
+    mirrors = {"bfk_opts_t": _lib.Opts, "bfk_attrs_t": _lib.Attrs, "bfk_stats_t": _lib.Stats,
+               "bfk_plan_info_t": _lib.PlanInfo}
     lines = ['#include "bfknn.h"', "#include <stddef.h>", "#include <stdio.h>",
              "int main(void) {"]
     for cname, py in mirrors.items():
@@ -165,3 +166,29 @@ def test_struct_layouts_match_the_header(tmp_path):
         assert got[(cname, "sizeof")] == ctypes.sizeof(py), cname
         for fname, _ in py._fields_:
             assert got[(cname, fname)] == getattr(py, fname).offset, f"{cname}.{fname}"
+
+
+def test_plan_levels_and_cta_pairs():
+    """The planner's choices, computed on the host (bfk_plan_info): the 10M-row workload's
+    four levels with CTA pairs; a shard of an 8-GPU search keeps its own full first level
+    (the sizes of a lone search of its rows) and, under 4M rows, single CTAs; shards decide
+    on the largest shard's rows; pairs can be forced either way; 16 queries take the SIMT
+    engine."""
+    from gpu_algo_b200 import engine
+    p = engine.plan_info(10_000, 10_000_000, 128, 100)
+    assert p["engine"] == "tc_f16" and p["cta_pair"]
+    assert p["level_tiles"] == [2, 44, 1303, 39063] and p["q_tiles"] == 80
+    shard = engine.plan_info(10_000, 1_250_000, 128, 100, plan_rows=1_250_000, shards=8)
+    lone = engine.plan_info(10_000, 1_250_000, 128, 100)
+    assert shard["level_tiles"] == lone["level_tiles"] == [6, 163, 4883]
+    assert not shard["cta_pair"] and shard["q_tiles"] == 79
+    small = engine.plan_info(10_000, 3_000_000, 128, 100, plan_rows=5_000_000, shards=2)
+    assert small["cta_pair"] and small["levels"] == 4
+    assert not engine.plan_info(10_000, 1_000_000, 128, 100)["cta_pair"]
+    assert engine.plan_info(10_000, 1_000_000, 128, 100, cta_pair=True)["cta_pair"]
+    assert not engine.plan_info(10_000, 10_000_000, 128, 100, cta_pair=False)["cta_pair"]
+    assert not engine.plan_info(1_000, 20_000_000, 960, 100)["cta_pair"]
+    direct = engine.plan_info(16, 12_500_000, 96, 10)
+    assert direct["engine"] == "direct" and direct["levels"] == 0
+    with pytest.raises(_lib.BfkError):
+        engine.plan_info(10, 100, 0, 10)
