@@ -20,13 +20,18 @@ Everything else is this package's own:
   return the same exact, sorted top-k;
 * throughput per (variant, n) is n over the mean trial time; its spread is the
   mean time's spread carried through q = n / t to first order, which is the
-  quantity the published files report.
+  quantity the published files report;
+* each row also carries the search's roofline, max(2 n m d / tensor peak,
+  m d 4 / HBM bandwidth) at the measured peaks of MEASURED_PEAKS.json when the
+  working directory or the repository holds one (else fixed fallback figures),
+  and the mean time's fraction of it; the plot script ignores these keys.
 """
 from __future__ import annotations
 
 import argparse
 import itertools
 import json
+import os
 import statistics
 import sys
 from dataclasses import dataclass, field
@@ -51,6 +56,35 @@ _FLAGS = (
     ("--cluster-noise", float, 0.05, "clustered queries: noise scale around a centre"),
     ("--out-json", str, "bf_fp32_variant_repeat_over_n_d8_k1.json", "where to write the payload"),
 )
+
+
+# used when no MEASURED_PEAKS.json is found: an HBM copy rate and a dense bf16 GEMM rate
+# measured earlier on B200s
+FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "source": "fallback"}
+
+
+def load_peaks(paths=None) -> dict:
+    """The measured HBM (GB/s) and dense bf16 (TFLOP/s) peaks, from the first
+    MEASURED_PEAKS.json among `paths` (default: the working directory, then the
+    repository root), else FALLBACK_PEAKS."""
+    if paths is None:
+        root = Path(__file__).resolve().parents[2]
+        paths = [Path("MEASURED_PEAKS.json"), root / "MEASURED_PEAKS.json"]
+    for p in paths:
+        if os.path.exists(p):
+            with open(p, encoding="utf-8") as f:
+                j = json.load(f)
+            return {"hbm_gbs": float(j["hbm_gbs"]), "bf16_tflops": float(j["bf16_tflops"]),
+                    "source": "measured"}
+    return dict(FALLBACK_PEAKS)
+
+
+def roofline(n: int, m: int, d: int, peaks: dict) -> tuple[float, str]:
+    """(ms, bound) of one search of n queries over m rows of d dimensions: the longer of
+    the algorithmic flops at the tensor peak and the FP32 rows at HBM bandwidth."""
+    t_flops = 2.0 * n * m * d / (peaks["bf16_tflops"] * 1e12)
+    t_bytes = 4.0 * m * d / (peaks["hbm_gbs"] * 1e9)
+    return (max(t_flops, t_bytes) * 1e3, "tensor" if t_flops >= t_bytes else "hbm")
 
 
 def build_parser() -> argparse.ArgumentParser:
@@ -124,18 +158,23 @@ class Cell:
     trial_ms: list[float] = field(default_factory=list)
     block: int = 0
 
-    def summary(self, args) -> dict:
-        """The payload row (the reference's keys)."""
+    def summary(self, args, peaks: dict | None = None) -> dict:
+        """The payload row: the reference's keys, then the roofline keys."""
         mean_ms = statistics.fmean(self.trial_ms)
         sd_ms = statistics.pstdev(self.trial_ms)
         qps = self.n / (mean_ms / 1e3)
         # q = n / t, so dq = q * dt / t to first order
         sd_qps = qps * sd_ms / mean_ms if mean_ms > 0 else 0.0
+        peaks = peaks or load_peaks()
+        roof_ms, bound = roofline(self.n, args.m, args.d, peaks)
         return dict(variant=self.variant, distribution=args.query_mode, m=args.m, d=args.d,
                     n=self.n, k=args.k, trials=args.trials, reps=args.reps,
                     trial_query_ms=list(self.trial_ms), mean_query_ms=mean_ms,
                     std_query_ms=sd_ms, mean_queries_per_second=qps,
-                    std_queries_per_second=sd_qps, block=int(self.block))
+                    std_queries_per_second=sd_qps, block=int(self.block),
+                    roofline_ms=roof_ms, roofline_bound=bound,
+                    roofline_fraction=roof_ms / mean_ms if mean_ms > 0 else None,
+                    roofline_peaks=peaks["source"])
 
 
 def payload(args, n_values: list[int], variants: list[str], rows: list[dict],
@@ -157,6 +196,7 @@ def run_study(args, log=print) -> dict:
     Xd = torch.from_numpy(X).cuda()
     Qd = torch.from_numpy(Q).cuda()
     rows, failures = [], []
+    peaks = load_peaks()
     log(f"# over-n study: m={args.m} d={args.d} k={args.k} trials={args.trials} "
         f"reps={args.reps} queries={args.query_mode}")
     log(f"# {'variant':>8} {'n':>8} {'ms':>10} {'+-':>8} {'queries/s':>12} {'+-':>10}")
@@ -175,7 +215,7 @@ def run_study(args, log=print) -> dict:
                              "error": f"{type(exc).__name__}: {exc}"})
             log(f"  {variant:>8} {n:>8} failed: {exc}")
             continue
-        row = cell.summary(args)
+        row = cell.summary(args, peaks)
         rows.append(row)
         log(f"  {variant:>8} {n:>8} {row['mean_query_ms']:10.4f} {row['std_query_ms']:8.4f} "
             f"{row['mean_queries_per_second']:12.0f} {row['std_queries_per_second']:10.0f}")

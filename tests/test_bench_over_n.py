@@ -13,9 +13,11 @@ import pytest
 
 from gpu_algo_b200.bf import bench_over_n as b
 
-RESULT_KEYS = {"variant", "distribution", "m", "d", "n", "k", "trials", "reps", "trial_query_ms",
-               "mean_query_ms", "std_query_ms", "mean_queries_per_second",
-               "std_queries_per_second", "block"}
+REFERENCE_RESULT_KEYS = {"variant", "distribution", "m", "d", "n", "k", "trials", "reps",
+                         "trial_query_ms", "mean_query_ms", "std_query_ms",
+                         "mean_queries_per_second", "std_queries_per_second", "block"}
+RESULT_KEYS = REFERENCE_RESULT_KEYS | {"roofline_ms", "roofline_bound", "roofline_fraction",
+                                       "roofline_peaks"}
 META_KEYS = {"m", "d", "k", "seed", "trials", "reps", "skip_failures", "query_mode",
              "cluster_size", "cluster_noise", "n_values", "variants"}
 
@@ -32,6 +34,7 @@ def test_payload_keys_and_statistics():
     # the spread of n / t carried to first order from the spread of t
     assert row["std_queries_per_second"] == pytest.approx(1000 * sd / (mean ** 2 * 1e-3))
     out = b.payload(args, [1000, 2000], ["q16"], [row], [])
+    assert REFERENCE_RESULT_KEYS <= set(row)  # the keys the reference's plot script reads
     assert set(out) == {"meta", "results", "failures"}
     assert set(out["meta"]) == META_KEYS
     assert out["meta"]["n_values"] == [1000, 2000] and out["meta"]["skip_failures"] is False
@@ -57,6 +60,25 @@ def test_flags_defaults_and_data():
     np.testing.assert_array_equal(X, X2)  # rows come first from the same stream
     with pytest.raises(ValueError):
         b.synthetic_data(42, 10, 8, 4, "uniform")
+
+
+def test_roofline_fields(tmp_path):
+    """Each row's roofline: the 1M x d=8 published shape is HBM-bound for a few hundred
+    queries (the rows' 32 MB), tensor-bound above; peaks come from a MEASURED_PEAKS.json
+    when one is found, else the fallback figures."""
+    peaks = {"hbm_gbs": 8000.0, "bf16_tflops": 1000.0, "source": "measured"}
+    ms, bound = b.roofline(100, 1_000_000, 8, peaks)
+    assert bound == "hbm" and ms == pytest.approx(4 * 1_000_000 * 8 / 8e12 * 1e3)
+    ms, bound = b.roofline(128_000, 1_000_000, 8, peaks)
+    assert bound == "tensor" and ms == pytest.approx(2 * 128_000 * 1_000_000 * 8 / 1e15 * 1e3)
+    args = b.build_parser().parse_args([])
+    row = b.Cell("q16", 128_000, [0.4096], 128).summary(args, peaks)
+    assert row["roofline_bound"] == "tensor" and row["roofline_peaks"] == "measured"
+    assert row["roofline_fraction"] == pytest.approx(row["roofline_ms"] / 0.4096)
+    p = tmp_path / "MEASURED_PEAKS.json"
+    p.write_text(json.dumps({"hbm_gbs": 6000.0, "bf16_tflops": 1500.0}))
+    assert b.load_peaks([p]) == {"hbm_gbs": 6000.0, "bf16_tflops": 1500.0, "source": "measured"}
+    assert b.load_peaks([tmp_path / "absent.json"]) == b.FALLBACK_PEAKS
 
 
 @pytest.mark.gpu
